@@ -1,0 +1,181 @@
+/*
+ * dh_b200.h -- C ABI of libdh_b200.so, the B200 (sm_100a) implementation of
+ * the MDLM denoising hot path of K1ta141k/DiffusionHard.
+ *
+ * Conventions (mirroring the reference HLS kernels, hls/rng/philox_rng.hpp:29-33,
+ * hls/output_head/output_head.hpp:20-26, hls/candidate_sampler/candidate_sampler.hpp:18-29):
+ *   - every entry point returns a uint32_t status (0 = OK) and validates its
+ *     arguments BEFORE touching any buffer; a non-zero status means nothing was
+ *     launched and no output was written;
+ *   - entry points that mirror a reference function return that function's own
+ *     status codes (listed per family below); generic failures use codes >= 100;
+ *   - all array arguments are DEVICE pointers owned by the caller; no entry
+ *     point allocates memory.  Scratch space is passed as `workspace` whose
+ *     size the matching *_workspace_size() query returns;
+ *   - work is enqueued on the given CUDA stream (`void*` = cudaStream_t; NULL =
+ *     legacy default stream) and is asynchronous; entry points are stateless
+ *     and reentrant for distinct buffers / streams;
+ *   - randomness is counter-based (Philox4x32-10), so no RNG state is held.
+ *
+ * Counter layouts (build-defined where the reference leaves them open):
+ *   noise word for token v of a row:  philox((v/4, position, eval_id, stream_id),
+ *                                            (key_lo, key_hi))[v % 4]
+ *       -- identical to the reference stream kernels, philox_rng.cpp:137-139;
+ *   reveal word of a position:        philox((position/4, 0, step, 1),
+ *                                            (seed, sequence))[position % 4].
+ */
+#ifndef DH_B200_H
+#define DH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+
+/* Generic codes shared by every entry point. */
+#define DH_OK 0u
+#define DH_ERR_NULL_POINTER 100u
+#define DH_ERR_ALIGNMENT 101u
+#define DH_ERR_WORKSPACE 102u
+#define DH_ERR_UNSUPPORTED_SHAPE 103u
+#define DH_ERR_CUDA 104u
+#define DH_ERR_INVALID_ARGUMENT 105u
+
+/* RNG family -- same values as RngKernelStatus (philox_rng.hpp:29-33). */
+#define DH_RNG_INVALID_POSITION_COUNT 1u
+#define DH_RNG_INVALID_VOCABULARY_SIZE 2u
+
+/* Output-head family -- same values as OutputHeadKernelStatus (output_head.hpp:20-26). */
+#define DH_HEAD_INVALID_POSITION_COUNT 1u
+#define DH_HEAD_INVALID_HIDDEN_SIZE 2u
+#define DH_HEAD_INVALID_VOCABULARY_SIZE 3u
+#define DH_HEAD_INVALID_MASK_TOKEN 4u
+
+/* Candidate family -- same values as CandidateKernelStatus (candidate_sampler.hpp:12-16). */
+#define DH_CAND_INVALID_POSITION_COUNT 1u
+#define DH_CAND_INVALID_THRESHOLD 2u
+
+/* Reveal probability one in Q32 (candidate_sampler.hpp:10). */
+#define DH_REVEAL_PROBABILITY_ONE_Q32 (((uint64_t)1) << 32)
+
+/* ------------------------------------------------------------------- RNG */
+
+/* Philox4x32-10 on `count` independent (counter[4], key[2]) pairs; out[4*i..].
+ * Replaces philox4x32_10, hls/rng/philox_rng.cpp:33-54 / rng.py:36-61. */
+uint32_t dh_philox4x32_10(const uint32_t* counters, const uint32_t* keys, uint32_t* out,
+                          uint32_t count, void* stream);
+
+/* Factorized Q5.10 Gumbel score of each word.
+ * Replaces factorized_gumbel_score_q10, hls/rng/philox_rng.cpp:74-93. */
+uint32_t dh_gumbel_q10(const uint32_t* words, int32_t* scores, uint32_t count, void* stream);
+
+/* Word / score streams in the reference order (vocab tiles of 16, then
+ * position, then lane blocks of 4); `out` holds position_count*vocabulary_size
+ * entries.  Limits and status codes as the reference: 1 <= positions <= 64,
+ * 1 <= vocabulary <= 65535.
+ * Replace philox_word_stream_kernel (philox_rng.cpp:95-149) and
+ * philox_gumbel_stream_kernel (philox_rng.cpp:151-205). */
+uint32_t dh_philox_word_stream(uint32_t* out, uint32_t position_count,
+                               uint32_t vocabulary_size, uint32_t evaluation_id,
+                               uint32_t stream_id, uint32_t seed_low, uint32_t seed_high,
+                               void* stream);
+uint32_t dh_philox_gumbel_stream(int32_t* out, uint32_t position_count,
+                                 uint32_t vocabulary_size, uint32_t evaluation_id,
+                                 uint32_t stream_id, uint32_t seed_low, uint32_t seed_high,
+                                 void* stream);
+
+/* ------------------------------------------------- noisy argmax over logits */
+
+/* Gumbel-max candidate per row of fp32 logits (K1):
+ *   score(v) = round_half_even(logit[v] * 1024) + gumbel_q10(word(v)),
+ *   word(v) = philox((v/4, row_position[r], row_eval[r], stream_id),
+ *                    (key_lo, row_key_hi[r]))[v%4];
+ * the mask token is skipped and the lowest id wins ties.  Replaces the
+ * exponential race of mdlm._sample_categorical (mdlm.py:844-849) with the
+ * reference's hardware Q10 Gumbel race (rng.py:262-263, output_head.cpp:147-151).
+ * row_position / row_key_hi / row_eval may be NULL (= row index / 0 / 0).
+ * out_scores may be NULL.  Status: RNG family codes (rows == 0 ->
+ * DH_RNG_INVALID_POSITION_COUNT, vocab == 0 or > 65535 or mask >= vocab ->
+ * DH_RNG_INVALID_VOCABULARY_SIZE), DH_ERR_* otherwise. */
+size_t dh_noisy_argmax_workspace_size(uint32_t rows, uint32_t vocabulary_size);
+uint32_t dh_noisy_argmax_f32(const float* logits, uint64_t row_stride, uint32_t rows,
+                             uint32_t vocabulary_size, uint32_t mask_token_id,
+                             const uint32_t* row_position, const uint32_t* row_key_hi,
+                             const uint32_t* row_eval, uint32_t key_lo, uint32_t stream_id,
+                             int32_t* out_ids, int32_t* out_scores, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* Greedy argmax of fp32 logits (mask skipped, lowest id on ties): the final
+ * pass of the samplers, mdlm.py:1177-1200.  Same workspace as above. */
+uint32_t dh_greedy_argmax_f32(const float* logits, uint64_t row_stride, uint32_t rows,
+                              uint32_t vocabulary_size, uint32_t mask_token_id,
+                              int32_t* out_ids, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* ----------------------------------------------------- candidate reveal (K2) */
+
+/* Batched form of candidate_reveal_kernel (candidate_sampler.cpp:5-79) over
+ * `sequences` independent canvases of `positions` each (no 256 cap): per
+ * sequence, every position with active & valid & (word < threshold_q32)
+ * takes its candidate and clears its active bit; if any position of the
+ * sequence changed, ALL valid bits of that sequence are cleared.
+ * Layouts: tokens / candidates / words [sequences][positions]; bitmaps
+ * [sequences][ceil(positions/64)].  results[s] = (status << 32) | changed.
+ * Status: DH_CAND_INVALID_POSITION_COUNT (positions == 0),
+ * DH_CAND_INVALID_THRESHOLD (threshold > 2^32). */
+uint32_t dh_candidate_reveal(uint16_t* tokens, const uint16_t* candidates, uint64_t* active,
+                             uint64_t* valid, const uint32_t* words, uint64_t threshold_q32,
+                             uint32_t positions, uint32_t sequences, uint64_t* results,
+                             void* stream);
+
+/* ------------------------------------------ candidate-cache sampler (device) */
+
+/*
+ * Device-resident state of the candidate-cache DDPM loop (mdlm.py:1104-1218)
+ * for B sequences of L positions:
+ *   tokens      int32  [B*L]   canvas (mask id = masked)
+ *   candidates  uint16 [B*L]   cached candidate per position
+ *   active      uint64 [B*W]   bit = position still masked        (W = ceil(L/64))
+ *   valid       uint64 [B*W]   bit = cached candidate valid
+ *   eval_id     uint32 [B]     transition index of the last model evaluation
+ *   counters    int32  [3*steps]  per transition: batch active count, changed
+ *                              count, 1 if any sequence evaluated (else 0)
+ * Per sequence the cache is refilled when it is empty (the reference clears
+ * the whole cache on any change, mdlm.py:1173-1174).
+ */
+uint32_t dh_sampler_init(const int32_t* input_ids, uint32_t sequences, uint32_t positions,
+                         uint32_t mask_token_id, uint32_t steps, int32_t* tokens,
+                         uint16_t* candidates, uint64_t* active, uint64_t* valid,
+                         uint32_t* eval_id, int32_t* counters, void* stream);
+
+/* One transition over externally supplied fp32 logits [B*L, vocab] (the
+ * model(input_ids) / logits_function protocol): refill the candidate cache
+ * of every sequence whose cache is empty and that still has masked positions
+ * (K1 over its rows), then reveal with threshold_q32 (K2 with in-kernel
+ * reveal words).  `logits` is only read for sequences that refill. */
+size_t dh_sampler_workspace_size(uint32_t sequences, uint32_t positions,
+                                 uint32_t vocabulary_size);
+uint32_t dh_sampler_transition_f32(const float* logits, uint32_t sequences, uint32_t positions,
+                                   uint32_t vocabulary_size, uint32_t mask_token_id,
+                                   uint32_t seed, uint32_t step, uint32_t steps,
+                                   uint64_t threshold_q32, int32_t* tokens,
+                                   uint16_t* candidates, uint64_t* active, uint64_t* valid,
+                                   uint32_t* eval_id, int32_t* counters, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* Final greedy pass: every still-masked position takes the argmax of its
+ * fp32 logits row (mask skipped, lowest id on ties), mdlm.py:1177-1200. */
+uint32_t dh_sampler_finalize_f32(const float* logits, uint32_t sequences, uint32_t positions,
+                                 uint32_t vocabulary_size, uint32_t mask_token_id,
+                                 int32_t* tokens, uint64_t* active, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DH_B200_H */
