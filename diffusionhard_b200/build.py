@@ -24,7 +24,7 @@ INCLUDE = PKG.parent / "include"
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
-    "-O3", "-lineinfo", "-std=c++17",
+    "-O3", "-lineinfo", "-std=c++17", "-rdc=true",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-ffp-contract=off",
     "--expt-relaxed-constexpr",
     "-I", str(CSRC), "-I", str(INCLUDE),
@@ -75,8 +75,8 @@ def build(verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
     objs = [OBJ_DIR / (s.stem + ".o") for s in sources]
     if jobs or not LIB_PATH.exists() or any(o.stat().st_mtime > LIB_PATH.stat().st_mtime for o in objs):
         tmp = LIB_PATH.with_suffix(".so.tmp")
-        run([nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(tmp),
-             *map(str, objs), "-lcuda"])
+        run([nvcc, "-shared", "-rdc=true", "-gencode", "arch=compute_100a,code=sm_100a",
+             "-o", str(tmp), *map(str, objs), "-lcuda"])
         os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

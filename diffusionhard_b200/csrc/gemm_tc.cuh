@@ -1,0 +1,243 @@
+// gemm_tc.cuh -- persistent warp-specialised int8 GEMM on tcgen05 (sm_100a).
+//
+//   C[M, N] = A[M, K] . B[N, K]^T   int8 x int8 -> int32 accumulators in TMEM
+//
+// Both operands are K-major (rows of K bytes) and staged by TMA into 128-byte
+// swizzled shared-memory tiles (BM=128 rows x BK=128 bytes for A, BN rows x
+// 128 bytes for B), STAGES deep.  One CTA per SM loops over output tiles:
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      MMA issuer (one elected lane), owns the TMEM allocation
+//   warps 2..9  epilogue: 8 warps = 2 per TMEM lane quadrant, each thread owns
+//               one output row and half of the tile's columns.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the
+// epilogue of tile i overlaps the MMAs of tile i+1.  The epilogue is a policy
+// class (Epi) that receives each thread's row and kChunk consecutive int32
+// accumulators; it fuses dequantisation and whatever follows the GEMM.
+//
+// Every mbarrier wait is bounded; on expiry the kernel records an error in
+// tc::g_device_error, drains its own TMA copies and MMAs, frees TMEM, exits.
+#pragma once
+
+#include <cuda.h>
+
+#include "tc_ptx.cuh"
+
+namespace dh {
+
+struct GemmShape {
+    uint32_t M, N, K;            // K in int8 elements
+    const uint32_t* m_count;     // optional device row count (M_eff = min(M, *m_count))
+};
+
+template <uint32_t BN_>
+struct GemmCfg {
+    static constexpr uint32_t BM = 128, BN = BN_, BK = 128;
+    static constexpr uint32_t STAGES = BN == 256 ? 4 : 6;
+    static constexpr uint32_t A_BYTES = BM * BK;
+    static constexpr uint32_t B_BYTES = BN * BK;
+    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    static constexpr uint32_t EPI_WARPS = 8;
+    static constexpr uint32_t EPI_THREADS = 32 * EPI_WARPS;
+    static constexpr uint32_t THREADS = 64 + EPI_THREADS;
+    static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
+    static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+    static constexpr uint32_t IDESC = tc::idesc_i8_s32<BM, BN>();
+};
+
+template <uint32_t BN, class Epi>
+__global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
+gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                  const __grid_constant__ CUtensorMap tmap_b, GemmShape shape,
+                  const typename Epi::Params ep) {
+    using Cfg = GemmCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* a_smem = smem;
+    uint8_t* b_smem = smem + Cfg::STAGES * Cfg::A_BYTES;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(b_smem + Cfg::STAGES * Cfg::B_BYTES);
+    uint64_t* empty_bar = full_bar + Cfg::STAGES;
+    uint64_t* accf_bar = empty_bar + Cfg::STAGES;  // [2]
+    uint64_t* acce_bar = accf_bar + 2;             // [2]
+    uint64_t* drain_bar = acce_bar + 2;            // [1]
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+    const uint32_t warp = warp_id();
+    const uint32_t lane = lane_id();
+    if (warp == 0 && lane == 0) {
+        for (uint32_t s = 0; s < Cfg::STAGES; ++s) {
+            tc::mbar_init(&full_bar[s], 1);
+            tc::mbar_init(&empty_bar[s], 1);
+        }
+        for (uint32_t b = 0; b < 2; ++b) {
+            tc::mbar_init(&accf_bar[b], 1);
+            tc::mbar_init(&acce_bar[b], Cfg::EPI_THREADS);
+        }
+        tc::mbar_init(drain_bar, 1);
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tmap_a);
+        tc::prefetch_tmap(&tmap_b);
+    }
+    if (warp == 1) tc::tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    uint32_t m_eff = shape.M;
+    if (shape.m_count) m_eff = min(m_eff, *shape.m_count);
+    const uint32_t m_tiles = (m_eff + Cfg::BM - 1) / Cfg::BM;
+    const uint32_t n_tiles = (shape.N + BN - 1) / BN;
+    const uint32_t k_blocks = (shape.K + Cfg::BK - 1) / Cfg::BK;
+    const uint32_t total = m_tiles * n_tiles;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (tc::elect_one()) {
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_parity[Cfg::STAGES];
+            uint32_t issued = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                const uint32_t m0 = (tile / n_tiles) * Cfg::BM;
+                const uint32_t n0 = (tile % n_tiles) * BN;
+                for (uint32_t kb = 0; kb < k_blocks; ++kb) {
+                    if (!tc::mbar_wait(&empty_bar[stage], phase ^ 1, tc::kErrTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+                    tc::tma_load_2d(a_smem + stage * Cfg::A_BYTES, &tmap_a, &full_bar[stage],
+                                    static_cast<int32_t>(kb * Cfg::BK), static_cast<int32_t>(m0));
+                    tc::tma_load_2d(b_smem + stage * Cfg::B_BYTES, &tmap_b, &full_bar[stage],
+                                    static_cast<int32_t>(kb * Cfg::BK), static_cast<int32_t>(n0));
+                    issued_parity[stage] = phase;
+                    ++issued;
+                    if (++stage == Cfg::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Drain: every copy this CTA issued has landed before it may exit.
+            const uint32_t last = issued < Cfg::STAGES ? issued : Cfg::STAGES;
+            for (uint32_t i = 0; i < last; ++i) {
+                const uint32_t s = (stage + Cfg::STAGES - 1 - i) % Cfg::STAGES;
+                tc::mbar_wait(&full_bar[s], issued_parity[s], tc::kErrTimeoutFull);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (tc::elect_one()) {
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                if (!tc::mbar_wait(&acce_bar[acc], acc_phase ^ 1, tc::kErrTimeoutAccEmpty)) break;
+                tc::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (uint32_t kb = 0; kb < k_blocks; ++kb) {
+                    if (!tc::mbar_wait(&full_bar[stage], phase, tc::kErrTimeoutFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint64_t a_desc = tc::smem_desc_sw128(a_smem + stage * Cfg::A_BYTES);
+                    const uint64_t b_desc = tc::smem_desc_sw128(b_smem + stage * Cfg::B_BYTES);
+#pragma unroll
+                    for (uint32_t kk = 0; kk < Cfg::BK / 32; ++kk)
+                        tc::mma_i8(d_tmem, tc::desc_advance(a_desc, kk * 32),
+                                   tc::desc_advance(b_desc, kk * 32), Cfg::IDESC,
+                                   (kb | kk) != 0u);
+                    tc::mma_commit(&empty_bar[stage]);
+                    if (++stage == Cfg::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc::mma_commit(&accf_bar[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            // Drain: all MMAs issued by this thread complete before TMEM is freed.
+            tc::mma_commit(drain_bar);
+            tc::mbar_wait(drain_bar, 0, tc::kErrTimeoutAccFull);
+        }
+    } else {
+        // --------------------------------------------------------- epilogue
+        const uint32_t quad = warp & 3u;
+        const uint32_t half = (warp - 2) >> 2;
+        const uint32_t row_in_tile = quad * 32 + lane;
+        constexpr uint32_t kHalf = BN / 2;
+        constexpr uint32_t kChunk = Epi::kChunk;
+        static_assert(kHalf % kChunk == 0, "chunk must divide the half tile");
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x) {
+            const uint32_t m0 = (tile / n_tiles) * Cfg::BM;
+            const uint32_t n0 = (tile % n_tiles) * BN;
+            if (!tc::mbar_wait(&accf_bar[acc], acc_phase, tc::kErrTimeoutAccFull)) break;
+            tc::tc_fence_after();
+            const uint32_t row = m0 + row_in_tile;
+            const bool row_ok = row < m_eff;
+            typename Epi::TileState st;
+            Epi::tile_begin(ep, st, row, row_ok, n0 + half * kHalf);
+#pragma unroll 1
+            for (uint32_t c = 0; c < kHalf; c += kChunk) {
+                const uint32_t col_in_tile = half * kHalf + c;
+                const uint32_t taddr =
+                    tmem_base + ((quad * 32u) << 16) + acc * BN + col_in_tile;
+                uint32_t v[kChunk];
+#pragma unroll
+                for (uint32_t j = 0; j < kChunk / 32; ++j)
+                    tc::tmem_ld_32x32b_x32(taddr + 32 * j,
+                                           *reinterpret_cast<uint32_t(*)[32]>(&v[32 * j]));
+                tc::tmem_ld_wait();
+                Epi::chunk(ep, st, row, row_ok, n0 + col_in_tile, &v[0]);
+            }
+            Epi::tile_end(ep, st, row, row_ok);
+            tc::tc_fence_before();
+            tc::mbar_arrive(&acce_bar[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    }
+}
+
+// Host launch helper: persistent grid of min(tiles, SMs) CTAs (or `max_ctas`).
+template <uint32_t BN, class Epi>
+inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
+                                  const GemmShape& shape, const typename Epi::Params& ep,
+                                  uint32_t tiles_hint, cudaStream_t stream) {
+    using Cfg = GemmCfg<BN>;
+    auto kernel = gemm_i8_tc_kernel<BN, Epi>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    int sms = kNumSMs;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+            sms = v;
+    }
+    const uint32_t grid = tiles_hint == 0 ? 1u : (tiles_hint < static_cast<uint32_t>(sms) ? tiles_hint : sms);
+    kernel<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, shape, ep);
+    return cudaGetLastError();
+}
+
+}  // namespace dh

@@ -174,6 +174,25 @@ uint32_t dh_sampler_finalize_f32(const float* logits, uint32_t sequences, uint32
                                  int32_t* tokens, uint64_t* active, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+
+/* ------------------------------------------------ int8 tensor engine (tcgen05) */
+
+/* Raw int32 accumulators C[m, n] = A[m, k] . W[n, k]^T (int8, K-major rows;
+ * lda / ldw / ldc in elements).  The tensor-engine contract of the reference:
+ * torch._int_mm in fixed_mlp._integer_matmul (fixed_mlp.py:55-62) and the
+ * int8 MAC tile hls/tensor_engine/int8_mac_tile.cpp:7-41.  A and W must be
+ * 16-byte aligned with lda, ldw multiples of 16. */
+uint32_t dh_gemm_i8_s32(const int8_t* a, uint64_t lda, const int8_t* w, uint64_t ldw, int32_t* c,
+                        uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* stream);
+
+/* ------------------------------------------------------------- diagnostics */
+
+/* Reads (and optionally clears) the device error word.  Non-zero means a
+ * bounded wait inside a kernel expired (1..4: pipeline barrier that timed
+ * out); the kernel abandoned its work and its outputs are undefined.
+ * Synchronous. */
+uint32_t dh_device_error(uint32_t* out, uint32_t clear);
+
 #ifdef __cplusplus
 }
 #endif
