@@ -24,6 +24,14 @@
 
 namespace dh {
 
+// Default hooks for epilogue policies: extra shared memory (bytes, placed
+// after the pipeline stages) initialised once per CTA by all threads.
+struct EpiBase {
+    static constexpr uint32_t kExtraSmem = 0;
+    template <class P>
+    static DH_DEVINL void init_smem(const P&, uint8_t*) {}
+};
+
 struct GemmShape {
     uint32_t M, N, K;            // K in int8 elements
     const uint32_t* m_count;     // optional device row count (M_eff = min(M, *m_count))
@@ -42,6 +50,8 @@ struct GemmCfg {
     static constexpr uint32_t THREADS = 64 + EPI_THREADS;
     static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
     static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+    template <class Epi>
+    static constexpr uint32_t smem_bytes() { return SMEM_BYTES + Epi::kExtraSmem; }
     static constexpr uint32_t IDESC = tc::idesc_i8_s32<BM, BN>();
 };
 
@@ -62,6 +72,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint64_t* acce_bar = accf_bar + 2;             // [2]
     uint64_t* drain_bar = acce_bar + 2;            // [1]
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    uint8_t* extra_smem = smem + Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
 
     const uint32_t warp = warp_id();
     const uint32_t lane = lane_id();
@@ -80,6 +91,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
         tc::prefetch_tmap(&tmap_b);
     }
     if (warp == 1) tc::tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+    Epi::init_smem(ep, extra_smem);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -183,7 +195,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t row = m0 + row_in_tile;
             const bool row_ok = row < m_eff;
             typename Epi::TileState st;
-            Epi::tile_begin(ep, st, row, row_ok, n0 + half * kHalf);
+            Epi::tile_begin(ep, st, row, row_ok, n0 + half * kHalf, extra_smem);
 #pragma unroll 1
             for (uint32_t c = 0; c < kHalf; c += kChunk) {
                 const uint32_t col_in_tile = half * kHalf + c;
@@ -224,7 +236,7 @@ inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg::SMEM_BYTES);
+                                             Cfg::template smem_bytes<Epi>());
         if (e != cudaSuccess) return e;
         configured = true;
     }
@@ -236,7 +248,7 @@ inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
             sms = v;
     }
     const uint32_t grid = tiles_hint == 0 ? 1u : (tiles_hint < static_cast<uint32_t>(sms) ? tiles_hint : sms);
-    kernel<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, shape, ep);
+    kernel<<<grid, Cfg::THREADS, Cfg::template smem_bytes<Epi>(), stream>>>(ta, tb, shape, ep);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,268 @@
+// head.cu -- K9: the 768 x 50258 int8 output head fused with Philox-Gumbel
+// noisy argmax; logits never reach HBM.
+//
+// The int8 GEMM runs on tcgen05 (gemm_tc.cuh); the epilogue turns each
+// accumulator into a score and keeps, per row, the running (max score, lowest
+// token id) in registers, merged across tiles with one 64-bit atomicMax per
+// row and tile (score in the high word with the sign bit flipped, ~id in the
+// low word -- the tie rule of output_head.cpp:147-151 and
+// ordered_noisy_argmax_reducer.sv:106-133).
+//
+// Score modes:
+//   kRequantQ20    the HLS contract (output_head.cpp:126-146): round-half-away
+//                  (acc * mult_q20[v]) >> 20, + bias_q10[v] + noise
+//   kDequantNoisy  the model path: logit = float(double(acc) *
+//                  double(a_scale[r] * w_scale[v]) + double(bias[v])) -- exactly
+//                  the reference W8A8 output (fixed_mlp.py:98-106) -- then
+//                  round_half_even(logit * 1024) + Gumbel_Q10 (rng.py:262)
+//   kDequantGreedy argmax of the same fp32 logit (final greedy pass)
+// noise = factorized Gumbel of philox((v/4, pos[r], eval[r], stream),
+// (key_lo, key_hi[r]))[v%4], or an explicit [rows, vocab] int32 array.
+// Integer scores saturate at +-2^31-1 (the reference keeps int64); the two
+// agree whenever |score| < 2^31, i.e. |logit| < 2^21 in Q10 units.
+#include <cuda_bf16.h>
+
+#include "dh_philox.cuh"
+#include "gemm_tc.cuh"
+#include "tmap.h"
+
+namespace dh {
+
+uint32_t make_i8_operand_maps(CUtensorMap* ta, CUtensorMap* tb, const int8_t* a, uint64_t lda,
+                              const int8_t* w, uint64_t ldw, uint32_t m, uint32_t n, uint32_t k,
+                              uint32_t bn);
+
+namespace {
+
+enum HeadMode : uint32_t { kRequantQ20 = 0, kDequantNoisy = 1, kDequantGreedy = 2 };
+
+struct HeadParams {
+    uint32_t mode;
+    uint32_t vocab, mask_id;
+    const float* a_scale;      // [rows]          (dequant modes)
+    const float* w_scale;      // [vocab]
+    const float* bias;         // [vocab] fp32
+    const int32_t* mult_q20;   // [vocab]         (requant mode)
+    const int32_t* bias_q10;   // [vocab]
+    const int32_t* noise;      // [rows, vocab] or null -> Philox
+    const uint32_t* row_position;  // null -> row index
+    const uint32_t* row_key_hi;    // null -> const_key_hi
+    const uint32_t* row_eval;      // null -> const_eval
+    uint32_t const_eval, const_key_hi, key_lo, stream_id;
+    unsigned long long* packed;    // [rows] running (score, ~id), zero-initialised
+};
+
+DH_DEVINL int32_t sat_i32(int64_t v) {
+    return v > 2147483647LL ? 2147483647 : (v < -2147483647LL ? -2147483647 : static_cast<int32_t>(v));
+}
+
+DH_DEVINL int32_t requant_q20(int32_t acc, int32_t mult) {
+    const int64_t prod = static_cast<int64_t>(acc) * mult;
+    const int64_t half = 1LL << 19;
+    return prod >= 0 ? static_cast<int32_t>((prod + half) >> 20)
+                     : -static_cast<int32_t>((-prod + half) >> 20);
+}
+
+DH_DEVINL float ref_logit(int32_t acc, float a_scale, float w_scale, float bias) {
+    const float combined = __fmul_rn(a_scale, w_scale);
+    // double(acc) * double(combined) is exact (24 x 24 bits), so one DFMA equals
+    // the reference's separate multiply and add in float64.
+    const double v = __fma_rn(static_cast<double>(acc), static_cast<double>(combined),
+                              static_cast<double>(bias));
+    return __double2float_rn(v);
+}
+
+DH_DEVINL int32_t q10(float logit) {
+    const float scaled = __fmul_rn(logit, 1024.0f);
+    if (!(scaled == scaled)) return -(1 << 30);
+    if (scaled > 1073741824.0f) return 1 << 30;
+    if (scaled < -1073741824.0f) return -(1 << 30);
+    return __float2int_rn(scaled);
+}
+
+struct EpiHead : EpiBase {
+    static constexpr uint32_t kChunk = 32;
+    static constexpr uint32_t kExtraSmem = 32 * 256 * 2;  // merged Gumbel table
+    using Params = HeadParams;
+    struct TileState {
+        unsigned long long best;
+        float a_scale;
+        uint32_t pos, key_hi, ev;
+        const int16_t* table;
+    };
+    static DH_DEVINL void init_smem(const Params&, uint8_t* extra) {
+        load_gumbel_table(reinterpret_cast<int16_t*>(extra));
+    }
+    static DH_DEVINL void tile_begin(const Params& p, TileState& st, uint32_t row, bool ok,
+                                     uint32_t, uint8_t* extra) {
+        st.best = 0ull;
+        st.table = reinterpret_cast<const int16_t*>(extra);
+        if (!ok) return;
+        st.a_scale = p.a_scale ? p.a_scale[row] : 0.f;
+        st.pos = p.row_position ? p.row_position[row] : row;
+        st.key_hi = p.row_key_hi ? p.row_key_hi[row] : p.const_key_hi;
+        st.ev = p.row_eval ? p.row_eval[row] : p.const_eval;
+    }
+    static DH_DEVINL void chunk(const Params& p, TileState& st, uint32_t row, bool ok,
+                                uint32_t col0, const uint32_t* v) {
+        if (!ok || col0 >= p.vocab) return;
+        unsigned long long best = st.best;
+        if (p.mode == kDequantGreedy) {
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j) {
+                const uint32_t t = col0 + j;
+                if (t >= p.vocab || t == p.mask_id) continue;
+                const float l = ref_logit(static_cast<int32_t>(v[j]), st.a_scale,
+                                          __ldg(p.w_scale + t), __ldg(p.bias + t));
+                const unsigned long long pk = pack_float_id(l, t);
+                best = pk > best ? pk : best;
+            }
+            st.best = best;
+            return;
+        }
+#pragma unroll
+        for (uint32_t g = 0; g < 32; g += 4) {
+            const uint32_t t0 = col0 + g;
+            if (t0 >= p.vocab) break;
+            Philox4 w{0, 0, 0, 0};
+            if (!p.noise) w = philox4x32_10(t0 >> 2, st.pos, st.ev, p.stream_id, p.key_lo, st.key_hi);
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+                const uint32_t t = t0 + i;
+                if (t >= p.vocab || t == p.mask_id) continue;
+                const int32_t acc = static_cast<int32_t>(v[g + i]);
+                const int32_t noise = p.noise ? p.noise[static_cast<uint64_t>(row) * p.vocab + t]
+                                              : gumbel_q10(philox_lane(w, i), st.table);
+                int64_t s;
+                if (p.mode == kRequantQ20)
+                    s = static_cast<int64_t>(requant_q20(acc, __ldg(p.mult_q20 + t))) +
+                        __ldg(p.bias_q10 + t) + noise;
+                else
+                    s = static_cast<int64_t>(q10(ref_logit(acc, st.a_scale, __ldg(p.w_scale + t),
+                                                           __ldg(p.bias + t)))) + noise;
+                const unsigned long long pk = pack_score_id(sat_i32(s), t);
+                best = pk > best ? pk : best;
+            }
+        }
+        st.best = best;
+    }
+    static DH_DEVINL void tile_end(const Params& p, TileState& st, uint32_t row, bool ok) {
+        if (ok && st.best) atomicMax(p.packed + row, st.best);
+    }
+};
+
+__global__ void zero_u64_kernel(unsigned long long* p, uint32_t n, const uint32_t* count) {
+    const uint32_t m = count ? min(n, *count) : n;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < m; i += gridDim.x * blockDim.x)
+        p[i] = 0ull;
+}
+
+__global__ void head_finalize_kernel(const unsigned long long* packed, uint32_t rows,
+                                     const uint32_t* count, uint32_t greedy, int32_t* ids,
+                                     int32_t* scores, uint16_t* ids16) {
+    const uint32_t m = count ? min(rows, *count) : rows;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < m; i += gridDim.x * blockDim.x) {
+        const unsigned long long b = packed[i];
+        const uint32_t id = b == 0ull ? 0u : packed_id(b);
+        if (ids) ids[i] = static_cast<int32_t>(id);
+        if (ids16) ids16[i] = static_cast<uint16_t>(id);
+        if (scores) {
+            if (!greedy) {
+                scores[i] = packed_score(b);
+            } else {
+                const uint32_t k = static_cast<uint32_t>(b >> 32);
+                scores[i] = static_cast<int32_t>((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+            }
+        }
+    }
+}
+
+uint32_t launch_head(const int8_t* hidden, uint64_t ld_hidden, const int8_t* weights,
+                     uint64_t ld_weights, uint32_t rows, const uint32_t* rows_count,
+                     uint32_t hidden_size, const HeadParams& hp, cudaStream_t st) {
+    CUtensorMap ta, tb;
+    uint32_t s = make_i8_operand_maps(&ta, &tb, hidden, ld_hidden, weights, ld_weights, rows,
+                                      hp.vocab, hidden_size, 256);
+    if (s != DH_OK) return s;
+    const uint32_t zb = std::min<uint32_t>((rows + 255) / 256, 1024u);
+    zero_u64_kernel<<<zb, 256, 0, st>>>(hp.packed, rows, rows_count);
+    DH_LAUNCH_CHECK();
+    GemmShape shape{rows, hp.vocab, hidden_size, rows_count};
+    const uint32_t tiles = ((rows + 127) / 128) * ((hp.vocab + 255) / 256);
+    if (launch_gemm_i8<256, EpiHead>(ta, tb, shape, hp, tiles, st) != cudaSuccess) return DH_ERR_CUDA;
+    return DH_OK;
+}
+
+}  // namespace
+}  // namespace dh
+
+using namespace dh;
+
+extern "C" {
+
+uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_t* weights,
+                           uint64_t ld_weights, uint32_t rows, const uint32_t* rows_count,
+                           uint32_t hidden_size, uint32_t vocabulary_size, uint32_t mask_token_id,
+                           uint32_t mode, const float* a_scale, const float* w_scale,
+                           const float* bias, const int32_t* mult_q20, const int32_t* bias_q10,
+                           const int32_t* noise, const uint32_t* row_position,
+                           const uint32_t* row_key_hi, const uint32_t* row_eval,
+                           uint32_t const_eval, uint32_t key_lo, uint32_t stream_id,
+                           uint64_t* packed, int32_t* out_ids, int32_t* out_scores, void* stream) {
+    if (rows == 0) return DH_HEAD_INVALID_POSITION_COUNT;
+    if (hidden_size == 0) return DH_HEAD_INVALID_HIDDEN_SIZE;
+    if (vocabulary_size == 0 || vocabulary_size > 65535) return DH_HEAD_INVALID_VOCABULARY_SIZE;
+    if (mask_token_id >= vocabulary_size) return DH_HEAD_INVALID_MASK_TOKEN;
+    if (mode > kDequantGreedy) return DH_ERR_INVALID_ARGUMENT;
+    if (!packed) return DH_ERR_NULL_POINTER;
+    if (mode == kRequantQ20 && (!mult_q20 || !bias_q10)) return DH_ERR_NULL_POINTER;
+    if (mode != kRequantQ20 && (!a_scale || !w_scale || !bias)) return DH_ERR_NULL_POINTER;
+    HeadParams hp{mode, vocabulary_size, mask_token_id, a_scale, w_scale, bias, mult_q20, bias_q10,
+                  noise, row_position, row_key_hi, row_eval, const_eval, 0u, key_lo, stream_id,
+                  reinterpret_cast<unsigned long long*>(packed)};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint32_t s = launch_head(hidden, ld_hidden, weights, ld_weights, rows, rows_count, hidden_size,
+                             hp, st);
+    if (s != DH_OK) return s;
+    if (out_ids || out_scores) {
+        head_finalize_kernel<<<std::min<uint32_t>((rows + 255) / 256, 1024u), 256, 0, st>>>(
+            hp.packed, rows, rows_count, mode == kDequantGreedy, out_ids, out_scores, nullptr);
+        DH_LAUNCH_CHECK();
+    }
+    return DH_OK;
+}
+
+// Mirror of output_head_int8_kernel (output_head.cpp:23-157): same arguments
+// and status codes; the noise stream is either given as a [positions, vocab]
+// array or generated in place as philox_gumbel_stream_kernel would
+// (counter (v/4, position, evaluation_id, stream_id), key (seed_low, seed_high)).
+// hidden / weights rows are `hidden_size` bytes and must be 16-byte aligned
+// (hidden_size a multiple of 16: pad with zeros otherwise).  `workspace`
+// holds position_count uint64 words.
+uint32_t dh_output_head_int8(const int8_t* hidden, const int8_t* weights,
+                             const int32_t* requant_multiplier_q20, const int32_t* bias,
+                             const int32_t* noise, uint16_t* candidate_ids,
+                             uint32_t position_count, uint32_t hidden_size,
+                             uint32_t vocabulary_size, uint32_t mask_token_id,
+                             uint32_t evaluation_id, uint32_t stream_id, uint32_t seed_low,
+                             uint32_t seed_high, uint64_t* workspace, void* stream) {
+    if (position_count == 0 || position_count > 64) return DH_HEAD_INVALID_POSITION_COUNT;
+    if (hidden_size == 0 || hidden_size > 768) return DH_HEAD_INVALID_HIDDEN_SIZE;
+    if (vocabulary_size == 0 || vocabulary_size > 65535) return DH_HEAD_INVALID_VOCABULARY_SIZE;
+    if (mask_token_id >= vocabulary_size) return DH_HEAD_INVALID_MASK_TOKEN;
+    if (!requant_multiplier_q20 || !bias || !candidate_ids || !workspace) return DH_ERR_NULL_POINTER;
+    if (hidden_size % 16 != 0) return DH_ERR_ALIGNMENT;
+    HeadParams hp{kRequantQ20, vocabulary_size, mask_token_id, nullptr, nullptr, nullptr,
+                  requant_multiplier_q20, bias, noise, nullptr, nullptr, nullptr, evaluation_id,
+                  seed_high, seed_low, stream_id, reinterpret_cast<unsigned long long*>(workspace)};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint32_t s = launch_head(hidden, hidden_size, weights, hidden_size, position_count, nullptr,
+                             hidden_size, hp, st);
+    if (s != DH_OK) return s;
+    head_finalize_kernel<<<1, 64, 0, st>>>(hp.packed, position_count, nullptr, 0u, nullptr,
+                                           nullptr, candidate_ids);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+}  // extern "C"

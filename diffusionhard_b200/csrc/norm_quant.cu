@@ -1,0 +1,194 @@
+// norm_quant.cu -- HBM-bound row kernels of the DDiT forward:
+//   K10 embed_gather       x[r] = embedding[token[r]]                  (mlx_mdlm.py:262-268)
+//   K3  ln_smooth_quant    LayerNorm (no affine, eps 1e-5; the adaLN affine is
+//                          folded into the next linear, model_specialization.py:10-29)
+//                          -> divide by the SmoothQuant scale -> per-token
+//                          symmetric int8 + row scale      (fixed_mlp.py:11-35, 82-90)
+//   K3' quant_rows_bf16    same quantiser for bf16 activations (attention
+//                          output, GELU output)
+// One warp per row; rows are read once (float4 / 16-byte vector loads) and
+// kept in registers between the statistics and the quantisation pass.
+#include <cuda_bf16.h>
+
+#include "dh_common.cuh"
+
+namespace dh {
+namespace {
+
+constexpr uint32_t kD = 768;
+constexpr uint32_t kRowWarps = 8;
+
+DH_DEVINL int8_t quant_i8(float v, float inv_scale) {
+    float q = rintf(v * inv_scale);
+    q = fminf(fmaxf(q, -127.0f), 127.0f);
+    return static_cast<int8_t>(q);
+}
+
+__global__ void __launch_bounds__(kRowWarps * 32)
+embed_gather_kernel(const int32_t* __restrict__ tokens, const float* __restrict__ embed,
+                    float* __restrict__ x, uint32_t rows, uint32_t vocab,
+                    const uint32_t* __restrict__ run_flag) {
+    if (run_flag && *run_flag == 0u) return;
+    const uint32_t r = blockIdx.x * kRowWarps + warp_id();
+    if (r >= rows) return;
+    uint32_t t = static_cast<uint32_t>(tokens[r]);
+    if (t >= vocab) t = vocab - 1;
+    const float4* src = reinterpret_cast<const float4*>(embed + static_cast<uint64_t>(t) * kD);
+    float4* dst = reinterpret_cast<float4*>(x + static_cast<uint64_t>(r) * kD);
+#pragma unroll
+    for (uint32_t j = 0; j < kD / 128; ++j) dst[lane_id() + 32 * j] = __ldg(src + lane_id() + 32 * j);
+}
+
+// LayerNorm + SmoothQuant + int8.  Optional row gather: output row i reads
+// input row rows_index[i] (used to project only selected rows).
+__global__ void __launch_bounds__(kRowWarps * 32)
+ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ inv_smooth,
+                int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
+                const uint32_t* __restrict__ rows_index, const uint32_t* __restrict__ rows_count,
+                const uint32_t* __restrict__ run_flag) {
+    if (run_flag && *run_flag == 0u) return;
+    const uint32_t i = blockIdx.x * kRowWarps + warp_id();
+    const uint32_t n = rows_count ? min(rows, *rows_count) : rows;
+    if (i >= n) return;
+    const uint32_t r = rows_index ? rows_index[i] : i;
+    const float4* src = reinterpret_cast<const float4*>(x + static_cast<uint64_t>(r) * kD);
+    float4 v[kD / 128];
+    float sum = 0.f;
+#pragma unroll
+    for (uint32_t j = 0; j < kD / 128; ++j) {
+        v[j] = src[lane_id() + 32 * j];
+        sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+    const float mean = warp_sum_f32(sum) * (1.0f / kD);
+    float sq = 0.f;
+#pragma unroll
+    for (uint32_t j = 0; j < kD / 128; ++j) {
+        const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+        sq += (a * a + b * b) + (c * c + d * d);
+    }
+    const float var = warp_sum_f32(sq) * (1.0f / kD);
+    const float rstd = rsqrtf(var + 1e-5f);
+    const float4* is = reinterpret_cast<const float4*>(inv_smooth);
+    float amax = 0.f;
+#pragma unroll
+    for (uint32_t j = 0; j < kD / 128; ++j) {
+        const float4 s = __ldg(is + lane_id() + 32 * j);
+        v[j].x = (v[j].x - mean) * rstd * s.x;
+        v[j].y = (v[j].y - mean) * rstd * s.y;
+        v[j].z = (v[j].z - mean) * rstd * s.z;
+        v[j].w = (v[j].w - mean) * rstd * s.w;
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+    }
+    amax = warp_max_f32(amax);
+    const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
+    const float inv = 1.0f / sc;
+    char4* dst = reinterpret_cast<char4*>(out + static_cast<uint64_t>(i) * kD);
+#pragma unroll
+    for (uint32_t j = 0; j < kD / 128; ++j)
+        dst[lane_id() + 32 * j] = make_char4(quant_i8(v[j].x, inv), quant_i8(v[j].y, inv),
+                                             quant_i8(v[j].z, inv), quant_i8(v[j].w, inv));
+    if (lane_id() == 0) scale[i] = sc;
+}
+
+// bf16 rows of C = 768 or 3072 columns -> SmoothQuant -> int8 + row scale.
+template <uint32_t C>
+__global__ void __launch_bounds__(kRowWarps * 32)
+quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __restrict__ inv_smooth,
+                       int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
+                       const uint32_t* __restrict__ run_flag) {
+    if (run_flag && *run_flag == 0u) return;
+    const uint32_t r = blockIdx.x * kRowWarps + warp_id();
+    if (r >= rows) return;
+    constexpr uint32_t kVec = C / 256;  // 8-element (16-byte) vectors per lane
+    const uint4* src = reinterpret_cast<const uint4*>(in + static_cast<uint64_t>(r) * C);
+    uint4 raw[kVec];
+    float amax = 0.f;
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j) {
+        raw[j] = src[lane_id() + 32 * j];
+        const uint32_t c0 = (lane_id() + 32 * j) * 8;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            amax = fmaxf(amax, fmaxf(fabsf(f.x * __ldg(inv_smooth + c0 + 2 * e)),
+                                     fabsf(f.y * __ldg(inv_smooth + c0 + 2 * e + 1))));
+        }
+    }
+    amax = warp_max_f32(amax);
+    const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
+    const float inv = 1.0f / sc;
+    uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * C);
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j) {
+        const uint32_t c0 = (lane_id() + 32 * j) * 8;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
+        int8_t q[8];
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            q[2 * e] = quant_i8(f.x * __ldg(inv_smooth + c0 + 2 * e), inv);
+            q[2 * e + 1] = quant_i8(f.y * __ldg(inv_smooth + c0 + 2 * e + 1), inv);
+        }
+        dst[lane_id() + 32 * j] = *reinterpret_cast<const uint2*>(q);
+    }
+    if (lane_id() == 0) scale[r] = sc;
+}
+
+}  // namespace
+}  // namespace dh
+
+using namespace dh;
+
+extern "C" {
+
+uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x, uint32_t rows,
+                         uint32_t vocabulary_size, const uint32_t* run_flag, void* stream) {
+    if (!tokens || !embedding || !x) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if ((reinterpret_cast<uintptr_t>(embedding) | reinterpret_cast<uintptr_t>(x)) & 15u)
+        return DH_ERR_ALIGNMENT;
+    embed_gather_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
+                          static_cast<cudaStream_t>(stream)>>>(tokens, embedding, x, rows,
+                                                               vocabulary_size, run_flag);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+uint32_t dh_ln_smooth_quant(const float* x, const float* inv_smooth, int8_t* out, float* scale,
+                            uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
+                            const uint32_t* run_flag, void* stream) {
+    if (!x || !inv_smooth || !out || !scale) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(inv_smooth) |
+         reinterpret_cast<uintptr_t>(out)) & 15u)
+        return DH_ERR_ALIGNMENT;
+    ln_quant_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
+                      static_cast<cudaStream_t>(stream)>>>(x, inv_smooth, out, scale, rows,
+                                                           rows_index, rows_count, run_flag);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out, float* scale,
+                            uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream) {
+    if (!in || !inv_smooth || !out || !scale) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u)
+        return DH_ERR_ALIGNMENT;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint32_t grid = (rows + kRowWarps - 1) / kRowWarps;
+    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in);
+    if (cols == 768)
+        quant_rows_bf16_kernel<768><<<grid, kRowWarps * 32, 0, st>>>(src, inv_smooth, out, scale,
+                                                                     rows, run_flag);
+    else if (cols == 3072)
+        quant_rows_bf16_kernel<3072><<<grid, kRowWarps * 32, 0, st>>>(src, inv_smooth, out, scale,
+                                                                      rows, run_flag);
+    else
+        return DH_ERR_UNSUPPORTED_SHAPE;
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+}  // extern "C"

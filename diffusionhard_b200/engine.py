@@ -1,0 +1,268 @@
+"""MDLM engine: device-resident W8A8 DDiT + fused head + candidate-cache loop.
+
+Host orchestration over the C ABI (include/dh_b200.h).  Per forward and
+block: LN+SmoothQuant+int8 -> QKV GEMM (+rotary) -> attention -> requant ->
+attention-out GEMM (+residual) -> LN+quant -> MLP-up GEMM (+GELU) -> requant ->
+MLP-down GEMM (+residual).  Every launch of a transition is enqueued on one
+stream with no host synchronisation; a whole generation can be captured in
+one CUDA graph (`generate(..., graph=True)`).
+
+The transition structure follows mdlm._run_ddpm_candidate_cache_sampler
+(mdlm.py:1104-1218); candidates are computed only for the rows revealed at a
+transition (loop.cu), which is pathwise identical to the full-row candidate
+cache.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any, Dict, List, Optional
+
+import numpy as np
+
+from . import _lib
+from .model import MDLMConfig, QuantizedMDLM
+from .sampler import hardware_candidate_cache_bytes, reveal_thresholds_q32
+
+
+class _DevLinear:
+    def __init__(self, torch, ql, device) -> None:
+        self.w = torch.from_numpy(np.ascontiguousarray(ql.weight_q)).to(device)
+        self.w_scale = torch.from_numpy(ql.w_scale.astype(np.float32)).to(device)
+        self.bias = torch.from_numpy(ql.bias.astype(np.float32)).to(device)
+        self.inv_smooth = torch.from_numpy(ql.inv_smooth.astype(np.float32)).to(device)
+        self.out_features, self.in_features = ql.weight_q.shape
+
+
+class MDLMEngine:
+    """Weights and activation buffers for `batch` sequences of `seq_len` rows.
+
+    Attention keys: this forward writes its K / V rows at key offset
+    `kv_offset` of K / V^T buffers with `kv_stride` keys per (sequence, head)
+    and attends over the first `kv_len` keys.  Default: kv_len = kv_stride =
+    seq_len, offset 0.  Prefix reuse (prefix_drift._cached_suffix_forward,
+    prefix_drift.py:155-238) shares per-block K / V buffers between a prefix
+    engine (seq_len = P, kv_len = P, offset 0: the isolated prefix) and a
+    suffix engine (seq_len = S, pos_offset = P, kv_offset = P,
+    kv_len = P + S): the prefix K / V are written once and never recomputed.
+    """
+
+    def __init__(self, qm: QuantizedMDLM, batch: int, seq_len: int, device: Any = "cuda", *,
+                 pos_offset: int = 0, kv_len: Optional[int] = None, kv_offset: int = 0,
+                 kv_buffers: Optional[List[tuple]] = None) -> None:
+        import torch
+
+        self.torch = torch
+        cfg = qm.config
+        if cfg.hidden != 768 or cfg.heads != 12 or cfg.head_dim != 64 or cfg.mlp != 3072:
+            raise ValueError("the kernels are specialised for d=768, 12x64 heads, MLP 3072")
+        kv_len = seq_len if kv_len is None else kv_len
+        if seq_len % 128 or kv_len % 128:
+            raise ValueError("seq_len and kv_len must be multiples of 128")
+        if pos_offset + seq_len > cfg.max_positions or kv_offset + seq_len > max(kv_len, kv_offset + seq_len):
+            raise ValueError("rotary positions exceed the model length")
+        self.cfg, self.qm = cfg, qm
+        self.B, self.L = batch, seq_len
+        self.pos_offset, self.kv_len, self.kv_offset = pos_offset, kv_len, kv_offset
+        self.M = batch * seq_len
+        self.device = torch.device(device)
+        d = self.device
+        self.embedding = torch.from_numpy(qm.embedding).to(d)
+        self.rope_cos = torch.from_numpy(np.ascontiguousarray(qm.rope_cos)).to(d)
+        self.rope_sin = torch.from_numpy(np.ascontiguousarray(qm.rope_sin)).to(d)
+        self.blocks = [{k: _DevLinear(torch, v, d) for k, v in blk.items()} for blk in qm.blocks]
+        self.head = _DevLinear(torch, qm.head, d)
+        M, H = self.M, cfg.heads
+        bf16 = torch.bfloat16
+        self.x = torch.empty((M, 768), dtype=torch.float32, device=d)
+        self.act_q = torch.empty((M, 3072), dtype=torch.int8, device=d)
+        self.act_scale = torch.empty(M, dtype=torch.float32, device=d)
+        self.q = torch.empty((batch, H, seq_len, 64), dtype=bf16, device=d)
+        if kv_buffers is None:
+            k = torch.empty((batch, H, kv_len, 64), dtype=bf16, device=d)
+            vt = torch.empty((batch, H, 64, kv_len), dtype=bf16, device=d)
+            kv_buffers = [(k, vt)] * len(self.blocks)
+        self.kv_buffers = kv_buffers
+        self.kv_stride = kv_buffers[0][0].shape[2]
+        if kv_offset + seq_len > self.kv_stride or kv_len > self.kv_stride:
+            raise ValueError("K / V buffers too short")
+        self.attn = torch.empty((M, 768), dtype=bf16, device=d)
+        self.mlp = torch.empty((M, 3072), dtype=bf16, device=d)
+        # head input (gathered rows) and loop state
+        self.head_q = torch.empty((M, 768), dtype=torch.int8, device=d)
+        self.head_scale = torch.empty(M, dtype=torch.float32, device=d)
+        self.packed = torch.zeros(M, dtype=torch.int64, device=d)
+        W = (seq_len + 63) // 64
+        u32 = torch.int32
+        self.tokens = torch.empty(M, dtype=torch.int32, device=d)
+        self.active = torch.empty(batch * W, dtype=torch.int64, device=d)
+        self.need_eval = torch.empty(batch, dtype=u32, device=d)
+        self.eval_id = torch.empty(batch, dtype=u32, device=d)
+        self.fwd_rows = torch.full((1,), M, dtype=u32, device=d)
+        self.sel_count = torch.zeros(1, dtype=u32, device=d)
+        self.sel_rows = torch.empty(M, dtype=u32, device=d)
+        self.sel_pos = torch.empty(M, dtype=u32, device=d)
+        self.sel_key = torch.empty(M, dtype=u32, device=d)
+        self.sel_eval = torch.empty(M, dtype=u32, device=d)
+        self.counters: Optional[Any] = None
+        self._graphs: Dict[Any, Any] = {}
+        self.launches_per_forward = 1 + 9 * len(self.blocks)
+
+    @staticmethod
+    def kv_cache(qm: QuantizedMDLM, batch: int, kv_stride: int, device: Any = "cuda") -> List[tuple]:
+        """Per-block K [B, 12, kv_stride, 64] and V^T [B, 12, 64, kv_stride] (bf16)."""
+        import torch
+
+        return [(torch.empty((batch, 12, kv_stride, 64), dtype=torch.bfloat16, device=device),
+                 torch.empty((batch, 12, 64, kv_stride), dtype=torch.bfloat16, device=device))
+                for _ in qm.blocks]
+
+    # ------------------------------------------------------------ forward
+
+    def _p(self, t):
+        return _lib.ptr(t)
+
+    def forward(self, tokens: Any = None, run_rows: Any = None, hook: Any = None) -> None:
+        """Forward over self.tokens (or `tokens`, int32 [M] on the device);
+        leaves the residual stream in self.x.  run_rows: device word, the
+        forward is skipped when it holds 0.  hook(i) runs after block i."""
+        s = _lib.stream_handle()
+        tok = self.tokens if tokens is None else tokens
+        rr = self._p(run_rows) if run_rows is not None else None
+        _lib.call("dh_embed_gather", self._p(tok), self._p(self.embedding), self._p(self.x), self.M,
+                  self.cfg.vocab_size, rr, s)
+        for i, blk in enumerate(self.blocks):
+            self._forward_block(i, blk, rr, s)
+            if hook is not None:
+                hook(i)
+
+    def _forward_block(self, i: int, blk: dict, rr: Any, s: Any) -> None:
+        M, L = self.M, self.L
+        p = self._p
+        call = _lib.call
+        k, vt = self.kv_buffers[i]
+        qkv, out, up, down = blk["qkv"], blk["out"], blk["up"], blk["down"]
+        call("dh_ln_smooth_quant", p(self.x), p(qkv.inv_smooth), p(self.act_q), p(self.act_scale), M,
+             None, None, rr, s)
+        call("dh_gemm_qkv_rope", p(self.act_q), p(self.act_scale), p(qkv.w), p(qkv.w_scale), p(qkv.bias),
+             p(self.rope_cos), p(self.rope_sin), M, L, self.pos_offset, self.kv_stride, self.kv_offset,
+             p(self.q), p(k), p(vt), rr, s)
+        call("dh_attention", p(self.q), p(k), p(vt), p(self.attn), self.B, L, self.kv_len, self.kv_stride,
+             rr, s)
+        call("dh_quant_rows_bf16", p(self.attn), p(out.inv_smooth), p(self.act_q), p(self.act_scale), M,
+             768, rr, s)
+        call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(out.w), p(out.w_scale), p(out.bias),
+             p(self.x), M, 768, 768, rr, s)
+        call("dh_ln_smooth_quant", p(self.x), p(up.inv_smooth), p(self.act_q), p(self.act_scale), M,
+             None, None, rr, s)
+        call("dh_gemm_gelu", p(self.act_q), p(self.act_scale), p(up.w), p(up.w_scale), p(up.bias),
+             p(self.mlp), M, 3072, 768, rr, s)
+        call("dh_quant_rows_bf16", p(self.mlp), p(down.inv_smooth), p(self.act_q), p(self.act_scale), M,
+             3072, rr, s)
+        call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(down.w), p(down.w_scale),
+             p(down.bias), p(self.x), M, 768, 3072, rr, s)
+
+    def final_hidden_q(self, rows_index: Any = None, rows_count: Any = None):
+        """Final LayerNorm + head SmoothQuant + int8 of (selected) rows."""
+        s = _lib.stream_handle()
+        _lib.call("dh_ln_smooth_quant", self._p(self.x), self._p(self.head.inv_smooth),
+                  self._p(self.head_q), self._p(self.head_scale), self.M,
+                  self._p(rows_index) if rows_index is not None else None,
+                  self._p(rows_count) if rows_count is not None else None, None, s)
+        return self.head_q, self.head_scale
+
+    def head_argmax(self, rows: int, mode: int, rows_count: Any = None, row_position: Any = None,
+                    row_key_hi: Any = None, row_eval: Any = None, key_lo: int = 0,
+                    out_ids: Any = None, out_scores: Any = None, const_eval: int = 0) -> None:
+        s = _lib.stream_handle()
+        h = self.head
+        _lib.call("dh_head_argmax_i8", self._p(self.head_q), 768, self._p(h.w), 768, rows,
+                  self._p(rows_count) if rows_count is not None else None, 768, self.cfg.vocab_size,
+                  self.cfg.mask_token_id, mode, self._p(self.head_scale), self._p(h.w_scale),
+                  self._p(h.bias), None, None, None, self._p(row_position), self._p(row_key_hi),
+                  self._p(row_eval), const_eval, key_lo, 0, self._p(self.packed), self._p(out_ids),
+                  self._p(out_scores), s)
+
+    # ------------------------------------------------------------- loop
+
+    def _enqueue_generation(self, steps: int, seed: int, thresholds: List[int]) -> None:
+        s = _lib.stream_handle()
+        B, L = self.B, self.L
+        p = self._p
+        call = _lib.call
+        for k in range(steps + 1):
+            final = 1 if k == steps else 0
+            call("dh_loop_plan", B, L, min(k, steps - 1), steps, final, p(self.active), p(self.need_eval),
+                 p(self.eval_id), p(self.fwd_rows), p(self.sel_count), p(self.counters), s)
+            self.forward(run_rows=self.fwd_rows)
+            thr = 0 if final else thresholds[k]
+            call("dh_loop_select", B, L, min(k, steps - 1), seed, thr, final, p(self.active),
+                 p(self.eval_id), p(self.sel_rows), p(self.sel_pos), p(self.sel_key), p(self.sel_eval),
+                 p(self.sel_count), s)
+            self.final_hidden_q(self.sel_rows, self.sel_count)
+            self.head_argmax(self.M, 2 if final else 1, rows_count=self.sel_count,
+                             row_position=self.sel_pos, row_key_hi=self.sel_key, row_eval=self.sel_eval,
+                             key_lo=seed)
+            call("dh_loop_commit", B, L, min(k, steps - 1), steps, final, p(self.packed), p(self.sel_rows),
+                 p(self.sel_count), p(self.tokens), p(self.active), p(self.need_eval), p(self.counters), s)
+
+    def launches_per_generation(self, steps: int) -> int:
+        per_transition = 1 + self.launches_per_forward + 1 + 1 + 2 + 1
+        return 1 + (steps + 1) * per_transition
+
+    def generate(self, input_ids: Any, *, steps: int, seed: int = 0, sampling_epsilon: float = 1e-5,
+                 graph: bool = False) -> tuple[Any, dict]:
+        """Candidate-cache generation of B sequences (device input_ids int
+        [B, L]).  Returns (device int32 ids [B, L], metadata)."""
+        torch = self.torch
+        if self.counters is None or self.counters.numel() != 3 * steps:
+            self.counters = torch.zeros(3 * steps, dtype=torch.int32, device=self.device)
+        ids = input_ids.to(device=self.device, dtype=torch.int32).contiguous().view(-1)
+        if ids.numel() != self.M:
+            raise ValueError("input_ids must be [batch, seq_len]")
+        self._ids_in = ids
+        thresholds = reveal_thresholds_q32(steps, sampling_epsilon)
+        s = _lib.stream_handle()
+        _lib.call("dh_loop_init", _lib.ptr(ids), self.B, self.L, self.cfg.mask_token_id, steps,
+                  _lib.ptr(self.tokens), _lib.ptr(self.active), _lib.ptr(self.need_eval),
+                  _lib.ptr(self.eval_id), _lib.ptr(self.counters), s)
+        if graph:
+            key = (steps, seed, sampling_epsilon)
+            g = self._graphs.get(key)
+            if g is None:
+                # warm-up outside capture (function attributes, tensor maps)
+                self._enqueue_generation(steps, seed, thresholds)
+                _lib.call("dh_loop_init", _lib.ptr(ids), self.B, self.L, self.cfg.mask_token_id, steps,
+                          _lib.ptr(self.tokens), _lib.ptr(self.active), _lib.ptr(self.need_eval),
+                          _lib.ptr(self.eval_id), _lib.ptr(self.counters), s)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._enqueue_generation(steps, seed, thresholds)
+                self._graphs[key] = g
+            g.replay()
+        else:
+            self._enqueue_generation(steps, seed, thresholds)
+        return self.tokens.view(self.B, self.L), {}
+
+    def metadata(self, steps: int) -> dict:
+        counters = self.counters.view(steps, 3).cpu().tolist()
+        active = [c[0] for c in counters if c[0] > 0]
+        n = len(active)
+        changed = [c[1] for c in counters[:n]]
+        evaluated = [c[2] for c in counters[:n]]
+        remaining_before_final = active[-1] - changed[-1] if n else 0
+        evaluations = sum(evaluated) + (1 if remaining_before_final > 0 else 0)
+        cache_bytes, id_bytes = hardware_candidate_cache_bytes(self.M, self.cfg.mask_token_id)
+        return {
+            "sampling_transitions": n,
+            "model_evaluations": evaluations,
+            "probability_cache_hits": n - sum(evaluated),
+            "candidate_cache_hits": n - sum(evaluated),
+            "transition_active_tokens": active,
+            "transition_changed_tokens": changed,
+            "cache_hit_sampling_overhead_modeled": False,
+            "cache_correctness_class": "distribution-equivalent",
+            "hardware_candidate_cache_bytes": cache_bytes,
+            "candidate_id_bytes": id_bytes,
+        }

@@ -185,6 +185,132 @@ uint32_t dh_sampler_finalize_f32(const float* logits, uint32_t sequences, uint32
 uint32_t dh_gemm_i8_s32(const int8_t* a, uint64_t lda, const int8_t* w, uint64_t ldw, int32_t* c,
                         uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* stream);
 
+/* ------------------------------------------------------- DDiT forward path */
+/* W8A8 convention (fixed_mlp.quantized_linear, fixed_mlp.py:65-136, with static
+ * SmoothQuant scales s per input channel): an activation row a is quantised as
+ * a' = a / s (passed here as inv_smooth = 1/s), a_scale = max|a'| / 127
+ * (1 if 0), q = clamp(round(a' / a_scale), -127, 127); the linear output is
+ * acc * (a_scale * w_scale) + bias with w_scale per output channel.  d = 768,
+ * 12 heads x 64, MLP 3072.  `run_flag` / `run_rows` (device words, may be
+ * NULL) let a captured graph skip a forward: 0 = do nothing. */
+
+/* x[r, :] = embedding[tokens[r], :]  (fp32 rows of 768; mlx_mdlm.py:262-268). */
+uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x, uint32_t rows,
+                         uint32_t vocabulary_size, const uint32_t* run_flag, void* stream);
+
+/* LayerNorm (no affine, eps 1e-5) -> SmoothQuant -> per-token int8 (K3).
+ * The adaLN affine is folded into the following linear
+ * (model_specialization.py:10-29).  Optional gather: output row i reads input
+ * row rows_index[i] for i < *rows_count. */
+uint32_t dh_ln_smooth_quant(const float* x, const float* inv_smooth, int8_t* out, float* scale,
+                            uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
+                            const uint32_t* run_flag, void* stream);
+
+/* bf16 rows (cols = 768 or 3072) -> SmoothQuant -> per-token int8 (K3'). */
+uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out, float* scale,
+                            uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream);
+
+/* QKV projection (K4): [m, 768] x [2304, 768]^T, dequant, rotate-half rotary
+ * on q and k at position (row % seq_len) + pos_offset (mlx_mdlm.py:298-329),
+ * written as bf16 Q [B, 12, seq_len, 64], K [B, 12, kv_stride, 64] and V^T
+ * [B, 12, 64, kv_stride] at key offset kv_offset -- the layout of a cached
+ * prefix followed by the active rows (prefix_drift.py:155-238).
+ * rope_cos / rope_sin: [positions, 32] fp32. */
+uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, const int8_t* w,
+                          const float* w_scale, const float* bias, const float* rope_cos,
+                          const float* rope_sin, uint32_t m, uint32_t seq_len, uint32_t pos_offset,
+                          uint32_t kv_stride, uint32_t kv_offset, void* q, void* k, void* vt,
+                          const uint32_t* run_rows, void* stream);
+
+/* x[m, n] += dequant(A . W^T) (+ bias): attention-out (K6) and MLP-down (K8),
+ * with the adaLN gates folded into W and bias (mlx_mdlm.py:442-453). */
+uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, const int8_t* w,
+                          const float* w_scale, const float* bias, float* x, uint32_t m, uint32_t n,
+                          uint32_t k, const uint32_t* run_rows, void* stream);
+
+/* out[m, n] = bf16(gelu_tanh(dequant(A . W^T) + bias)): MLP-up (K7). */
+uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
+                      const float* w_scale, const float* bias, void* out, uint32_t m, uint32_t n,
+                      uint32_t k, const uint32_t* run_rows, void* stream);
+
+/* Bidirectional attention softmax(Q K^T / 8) V (K5) over the first kv_len
+ * keys of K / V^T buffers of kv_stride rows per (sequence, head); bf16 in,
+ * fp32 softmax, bf16 out [sequences * q_len, 768].  q_len, kv_len multiples
+ * of 128, kv_stride a multiple of 8. */
+uint32_t dh_attention(const void* q, const void* k, const void* vt, void* out, uint32_t sequences,
+                      uint32_t q_len, uint32_t kv_len, uint32_t kv_stride, const uint32_t* run_flag,
+                      void* stream);
+
+/* ------------------------------------------------ fused int8 head (K9) */
+
+/* Head + noisy argmax over `rows` int8 hidden rows (ld_hidden bytes apart)
+ * and the int8 [vocab, hidden_size] weight (ld_weights bytes per row), on
+ * tcgen05; logits never leave the chip.  Per row, the best (score, lowest id)
+ * is merged into packed[row] (zeroed by this call) and, if given, written to
+ * out_ids / out_scores.  mode 0: HLS requant score, requant_q20(acc,
+ * mult_q20[v]) + bias_q10[v] + noise (output_head.cpp:126-146); mode 1: the
+ * reference W8A8 logit float(double(acc) * double(a_scale[r]*w_scale[v]) +
+ * double(bias[v])) (fixed_mlp.py:98-106), Q10-rounded (rng.py:262), + noise;
+ * mode 2: argmax of that fp32 logit (greedy pass, mdlm.py:1190).  noise is
+ * the given [rows, vocab] array or the factorized Gumbel of
+ * philox((v/4, row_position[r], row_eval[r] or const_eval, stream_id),
+ * (key_lo, row_key_hi[r]))[v%4].  rows_count (device, may be NULL) limits the
+ * rows processed, for data-dependent row sets.  Mask token skipped.
+ * Status: head family codes, then DH_ERR_*. */
+uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_t* weights,
+                           uint64_t ld_weights, uint32_t rows, const uint32_t* rows_count,
+                           uint32_t hidden_size, uint32_t vocabulary_size, uint32_t mask_token_id,
+                           uint32_t mode, const float* a_scale, const float* w_scale,
+                           const float* bias, const int32_t* mult_q20, const int32_t* bias_q10,
+                           const int32_t* noise, const uint32_t* row_position,
+                           const uint32_t* row_key_hi, const uint32_t* row_eval,
+                           uint32_t const_eval, uint32_t key_lo, uint32_t stream_id,
+                           uint64_t* packed, int32_t* out_ids, int32_t* out_scores, void* stream);
+
+/* Mirror of output_head_int8_kernel (output_head.cpp:23-157): same arguments,
+ * limits and status codes (1 <= positions <= 64, 1 <= hidden <= 768,
+ * 1 <= vocab <= 65535, mask < vocab); `noise` is the [positions, vocab] race
+ * noise or NULL to generate it in place exactly as philox_gumbel_stream_kernel
+ * orders it (counter (v/4, position, evaluation_id, stream_id), key
+ * (seed_low, seed_high)).  hidden_size must be a multiple of 16 (zero-pad).
+ * workspace: position_count uint64 words. */
+uint32_t dh_output_head_int8(const int8_t* hidden, const int8_t* weights,
+                             const int32_t* requant_multiplier_q20, const int32_t* bias,
+                             const int32_t* noise, uint16_t* candidate_ids,
+                             uint32_t position_count, uint32_t hidden_size,
+                             uint32_t vocabulary_size, uint32_t mask_token_id,
+                             uint32_t evaluation_id, uint32_t stream_id, uint32_t seed_low,
+                             uint32_t seed_high, uint64_t* workspace, void* stream);
+
+/* ------------------------------------ model loop (selected-row head) state */
+/*
+ * Device state of the candidate-cache loop around the model, B sequences x L
+ * positions: tokens int32 [B*L]; active uint64 [B*W] (W = ceil(L/64));
+ * need_eval / eval_id uint32 [B]; counters int32 [3*steps] (per transition:
+ * batch active count, changed count, 1 if a forward ran); fwd_rows and
+ * sel_count are single device words; sel_rows / sel_pos / sel_key / sel_eval
+ * uint32 [B*L] hold the rows revealed at the current transition.
+ * Per transition k: dh_loop_plan -> (forward if *fwd_rows) -> dh_loop_select ->
+ * dh_ln_smooth_quant (gathering sel_rows) -> dh_head_argmax_i8 (mode 1, rows
+ * limited by sel_count) -> dh_loop_commit.  final_pass = 1 runs the greedy
+ * pass of mdlm.py:1177-1200 over every still-masked position.
+ */
+uint32_t dh_loop_init(const int32_t* input_ids, uint32_t sequences, uint32_t positions,
+                      uint32_t mask_token_id, uint32_t steps, int32_t* tokens, uint64_t* active,
+                      uint32_t* need_eval, uint32_t* eval_id, int32_t* counters, void* stream);
+uint32_t dh_loop_plan(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t steps,
+                      uint32_t final_pass, const uint64_t* active, uint32_t* need_eval,
+                      uint32_t* eval_id, uint32_t* fwd_rows, uint32_t* sel_count,
+                      int32_t* counters, void* stream);
+uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t seed,
+                        uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
+                        const uint32_t* eval_id, uint32_t* sel_rows, uint32_t* sel_pos,
+                        uint32_t* sel_key, uint32_t* sel_eval, uint32_t* sel_count, void* stream);
+uint32_t dh_loop_commit(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t steps,
+                        uint32_t final_pass, const uint64_t* packed, const uint32_t* sel_rows,
+                        const uint32_t* sel_count, int32_t* tokens, uint64_t* active,
+                        uint32_t* need_eval, int32_t* counters, void* stream);
+
 /* ------------------------------------------------------------- diagnostics */
 
 /* Reads (and optionally clears) the device error word.  Non-zero means a

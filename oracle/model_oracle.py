@@ -1,0 +1,105 @@
+"""CPU oracle of the W8A8 DDiT forward.  TEST INFRASTRUCTURE ONLY.
+
+Restates, in torch-CPU float32 / float64, the reference arithmetic:
+  * W8A8 linear with static SmoothQuant scales: fixed_mlp.quantized_linear
+    (src/diffusion_accel/fixed_mlp.py:65-136; _quantize_symmetric :11-35),
+    with the activation amax of the smoothing scale taken from calibration
+    instead of the live batch (the static pattern of fixed_attention.py:410-420);
+  * the folded DDiT block and final layer: hardware_package.folded_mdlm_forward
+    (hardware_package.py:195-289), mlx_mdlm._DDiTBlock (mlx_mdlm.py:397-453);
+  * rotate-half rotary (mlx_mdlm.py:316-329) and fp32 SDPA with scale 1/8;
+  * prefix-cached suffix forward (prefix_drift._cached_suffix_forward,
+    prefix_drift.py:155-238) over K/V = [prefix ; suffix].
+Pinned to the reference in tests/test_model_oracle.py (golden fixtures made by
+tests/golden/make_model_golden.py from the reference's own functions).
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+
+def w8a8_linear(a, ql, return_parts: bool = False):
+    """Reference quantized_linear arithmetic with a static smoothing scale."""
+    import torch
+
+    s = torch.from_numpy(ql.smooth)
+    a = a / s[None, :]
+    maximum = a.abs().amax(dim=1)
+    scale = torch.where(maximum > 0, maximum / 127.0, torch.ones_like(maximum))
+    q = torch.round(a / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    w_scale = torch.from_numpy(ql.w_scale)
+    acc = torch.matmul(q.double(), torch.from_numpy(ql.weight_q).double().t()).to(torch.int64)
+    combined = scale[:, None] * w_scale[None, :]
+    out = (acc.double() * combined.double() + torch.from_numpy(ql.bias).double()[None, :]).float()
+    if return_parts:
+        return out, q, scale, acc
+    return out
+
+
+def _rot(t, cos, sin):
+    import torch
+
+    h = t.shape[-1] // 2
+    a, b = t[..., :h], t[..., h:]
+    return torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1)
+
+
+def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
+            prefix_kv: Optional[List[Tuple[object, object]]] = None, capture_kv: bool = False,
+            record: Optional[Dict[str, object]] = None):
+    """W8A8 forward of `ids` [B, L].  Returns the final LayerNorm output [B, L, d].
+
+    positions: rotary positions of the rows (default 0..L-1).
+    prefix_kv: per block (K_rot, V) [B, P, H, 64] prepended to the keys/values.
+    capture_kv: store per-block (K_rot, V) of these rows in record["kv"].
+    record: optional dict receiving "x{i}" (residual after block i),
+        "head_q" / "head_scale" (int8 head input and its row scales).
+    """
+    import torch
+    import torch.nn.functional as F
+
+    cfg = qm.config
+    B, L = ids.shape
+    pos = np.arange(L) if positions is None else positions
+    cos = torch.from_numpy(qm.rope_cos[pos])[None, :, None, :]
+    sin = torch.from_numpy(qm.rope_sin[pos])[None, :, None, :]
+    kv = []
+    with torch.no_grad():
+        x = torch.from_numpy(qm.embedding)[torch.from_numpy(ids.astype(np.int64))]
+        for i, blk in enumerate(qm.blocks):
+            h = F.layer_norm(x, [cfg.hidden]).reshape(B * L, cfg.hidden)
+            qkv = w8a8_linear(h, blk["qkv"]).view(B, L, 3, cfg.heads, cfg.head_dim)
+            q, k, v = qkv.unbind(dim=2)
+            q, k = _rot(q, cos, sin), _rot(k, cos, sin)
+            if capture_kv:
+                kv.append((k.clone(), v.clone()))
+            if prefix_kv is not None:
+                k = torch.cat([prefix_kv[i][0], k], dim=1)
+                v = torch.cat([prefix_kv[i][1], v], dim=1)
+            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+            a = a.transpose(1, 2).reshape(B * L, cfg.hidden)
+            x = x + w8a8_linear(a, blk["out"]).view(B, L, cfg.hidden)
+            h = F.layer_norm(x, [cfg.hidden]).reshape(B * L, cfg.hidden)
+            u = F.gelu(w8a8_linear(h, blk["up"]), approximate="tanh")
+            x = x + w8a8_linear(u, blk["down"]).view(B, L, cfg.hidden)
+            if record is not None:
+                record[f"x{i}"] = x.clone()
+        h = F.layer_norm(x, [cfg.hidden])
+        if record is not None:
+            hs = h.reshape(B * L, cfg.hidden) / torch.from_numpy(qm.head.smooth)[None, :]
+            maximum = hs.abs().amax(dim=1)
+            scale = torch.where(maximum > 0, maximum / 127.0, torch.ones_like(maximum))
+            record["head_q"] = torch.round(hs / scale[:, None]).clamp(-127, 127).to(torch.int8)
+            record["head_scale"] = scale
+            if capture_kv:
+                record["kv"] = kv
+        return h
+
+
+def logits(qm, h):
+    """Head logits from the final hidden (reference W8A8 output, fp32)."""
+    B, L, d = h.shape
+    return w8a8_linear(h.reshape(B * L, d), qm.head).view(B, L, -1)
