@@ -1,0 +1,409 @@
+#!/usr/bin/env python3
+"""Benchmark: generated tokens/s of the MDLM-169.6M W8A8 denoising loop.
+
+Workload per GPU (the full-model configuration the metric is quoted on):
+random-init MDLM-OWT-169.6M (N(0, 0.02) weights, folded, W8A8 with SmoothQuant
+alpha=0.5 from a seeded calibration batch), batch 32 x L=1024 all-masked
+canvases, 64 ddpm_cache transitions of the log-linear schedule + the final
+greedy pass, on the candidate-cache loop with the fused int8 head.
+One bench step = one complete generation.  With N GPUs every rank runs its
+own 32 sequences (weak scaling, no collective on the hot path); the Philox key
+uses the global sequence index, so tokens do not depend on N.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  `value` is device-timed (CUDA events, max
+over ranks) with inputs resident on the GPU; `e2e` is the same metric
+through the public drop-in API (run_ddpm_candidate_cache_sampler) from
+pinned host ids, with the host<->device copies inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "generated tok/s, MDLM-169.6M int8 L=1024 64 steps, 1/2/4/8 B200; head GB/s+TC util"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"dh_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9 and parts[1].isdigit():
+                rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        loaded = [s for s in sm if s > 600] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": int(statistics.median(loaded)), "sm_max_mhz": int(rows[0][2]),
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+def dist_setup():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def time_kernel(fn, iters: int = 20) -> float:
+    """Average ms of `fn` (enqueue on the current stream) over `iters` launches."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def kernel_breakdown(eng) -> dict:
+    """Per-kernel average launch time of one forward's kernels (ms)."""
+    from diffusionhard_b200 import _lib
+
+    p, s, M, L = _lib.ptr, _lib.stream_handle(), eng.M, eng.L
+    blk = eng.blocks[0]
+    k, vt = eng.kv_buffers[0]
+    qkv, out, up, down = blk["qkv"], blk["out"], blk["up"], blk["down"]
+    c = _lib.call
+    fns = {
+        "embed_gather": lambda: c("dh_embed_gather", p(eng.tokens), p(eng.embedding), p(eng.x), M,
+                                  eng.cfg.vocab_size, None, s),
+        "ln_smooth_quant": lambda: c("dh_ln_smooth_quant", p(eng.x), p(qkv.inv_smooth), p(eng.act_q),
+                                     p(eng.act_scale), M, None, None, None, s),
+        "gemm_qkv_rope": lambda: c("dh_gemm_qkv_rope", p(eng.act_q), p(eng.act_scale), p(qkv.w),
+                                   p(qkv.w_scale), p(qkv.bias), p(eng.rope_cos), p(eng.rope_sin), M, L, 0,
+                                   eng.kv_stride, 0, p(eng.q), p(k), p(vt), None, s),
+        "attention": lambda: c("dh_attention", p(eng.q), p(k), p(vt), p(eng.attn), eng.B, L, eng.kv_len,
+                               eng.kv_stride, None, s),
+        "quant_rows_768": lambda: c("dh_quant_rows_bf16", p(eng.attn), p(out.inv_smooth), p(eng.act_q),
+                                    p(eng.act_scale), M, 768, None, s),
+        "gemm_out_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(out.w),
+                                       p(out.w_scale), p(out.bias), p(eng.x), M, 768, 768, None, s),
+        "gemm_up_gelu": lambda: c("dh_gemm_gelu", p(eng.act_q), p(eng.act_scale), p(up.w), p(up.w_scale),
+                                  p(up.bias), p(eng.mlp), M, 3072, 768, None, s),
+        "quant_rows_3072": lambda: c("dh_quant_rows_bf16", p(eng.mlp), p(down.inv_smooth), p(eng.act_q),
+                                     p(eng.act_scale), M, 3072, None, s),
+        "gemm_down_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(down.w),
+                                        p(down.w_scale), p(down.bias), p(eng.x), M, 768, 3072, None, s),
+    }
+    return {name: time_kernel(fn) for name, fn in fns.items()}
+
+
+def roofline_for(name: str, ms: float, eng, peaks: dict, peaks_kind: str) -> dict:
+    M, L, B = eng.M, eng.L, eng.B
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    gemm = {"gemm_qkv_rope": (768, 2304), "gemm_out_residual": (768, 768), "gemm_up_gelu": (768, 3072),
+            "gemm_down_residual": (3072, 768)}
+    if name in gemm:
+        K, N = gemm[name]
+        ach = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        return {"kernel": name, "bound": "tensor", "achieved": round(ach, 1),
+                "peak": round(int8_peak, 1), "unit": "TOP/s", "frac": round(ach / int8_peak, 4),
+                "peak_source": f"int8 dense = 2 x {peaks_kind} bf16 burst ({peaks['bf16_tflops']} TFLOP/s)",
+                "work_per_launch": f"2*{M}*{N}*{K} int8 ops"}
+    if name == "attention":
+        flops = 4.0 * B * 12 * L * eng.kv_len * 64
+        ach = flops / (ms * 1e-3) / 1e12
+        return {"kernel": name, "bound": "tensor", "achieved": round(ach, 1), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
+                "peak_source": f"{peaks_kind} bf16 burst", "work_per_launch": "4*B*12*L*kv_len*64 bf16 FLOP"}
+    bytes_per = {"ln_smooth_quant": M * (768 * 4 + 768 + 4), "quant_rows_768": M * (768 * 2 + 768 + 4),
+                 "quant_rows_3072": M * (3072 * 2 + 3072 + 4), "embed_gather": M * (768 * 4 * 2 + 4)}[name]
+    ach = bytes_per / (ms * 1e-3) / 1e9
+    return {"kernel": name, "bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(ach / peaks["hbm_gbs"], 4), "peak_source": f"{peaks_kind} copy bandwidth",
+            "work_per_launch": f"{bytes_per} bytes"}
+
+
+def head_microbench(qm, peaks: dict, peaks_kind: str) -> dict:
+    """Fused head + sampler on the head-microbench shape: 32768 masked rows
+    (B=64 x L=1024, 50% masked) x 50258 vocab x 768, Philox-Gumbel argmax."""
+    import numpy as np
+    import torch
+
+    from diffusionhard_b200 import _lib
+
+    rows = 32768
+    g = torch.Generator(device="cuda").manual_seed(0)
+    h = torch.randint(-127, 128, (rows, 768), dtype=torch.int8, device="cuda", generator=g)
+    a_scale = torch.rand(rows, device="cuda", generator=g) * 0.01 + 0.02
+    wq = torch.from_numpy(qm.head.weight_q).cuda()
+    w_scale = torch.from_numpy(qm.head.w_scale).cuda()
+    bias = torch.from_numpy(qm.head.bias).cuda()
+    pos = torch.arange(rows, dtype=torch.int32, device="cuda") % 1024
+    key = torch.arange(rows, dtype=torch.int32, device="cuda") // 1024
+    packed = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    V = qm.config.vocab_size
+
+    def run():
+        _lib.call("dh_head_argmax_i8", _lib.ptr(h), 768, _lib.ptr(wq), 768, rows, None, 768, V,
+                  qm.config.mask_token_id, 1, _lib.ptr(a_scale), _lib.ptr(w_scale), _lib.ptr(bias), None,
+                  None, None, _lib.ptr(pos), _lib.ptr(key), None, 3, 0, 0, _lib.ptr(packed), None, None,
+                  _lib.stream_handle())
+
+    ms = time_kernel(run, iters=10)
+    ops = 2.0 * rows * V * 768
+    ach = ops / (ms * 1e-3) / 1e12
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    del np
+    return {"rows": rows, "vocab": V, "ms": round(ms, 4), "achieved_top_s": round(ach, 1),
+            "int8_peak_top_s": round(int8_peak, 1), "tensor_frac": round(ach / int8_peak, 4),
+            "weight_gbs": round(V * 768 * (rows / 128) / (ms * 1e-3) / 1e9, 1),
+            "note": "per-element Philox4x32-10 + Gumbel Q10 + exact fp64 dequant in the epilogue"}
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    from diffusionhard_b200.model import MDLMConfig, build_quantized
+    from oracle import cpu_baseline
+
+    qm = build_quantized(MDLMConfig(), seed=0)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline.measure(qm, transitions=1, steps=args.denoise_steps)
+        if i >= args.warmup:
+            samples.append(r["seconds_per_evaluated_transition"])
+    dt = statistics.mean(samples)
+    L = args.seq_len
+    value = L / (dt * (args.denoise_steps + 1))
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "MDLM-169.6M W8A8 random-init, L=1024 all-masked, 64 ddpm_cache steps "
+                                   "(CPU: one evaluated transition of 1 sequence per step, extrapolated)",
+                       "global_batch": 1, "seq_len": L, "steps": args.denoise_steps},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": r["cores"], "kind": "port",
+                             "sample": r["sample"]},
+            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=32, help="sequences per GPU")
+    ap.add_argument("--seq-len", type=int, default=1024)
+    ap.add_argument("--denoise-steps", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    import torch
+
+    world, rank, local = dist_setup() if args.impl == "ours" or int(os.environ.get("WORLD_SIZE", "1")) > 1 \
+        else (1, 0, 0)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    from diffusionhard_b200 import _lib
+    from diffusionhard_b200.api import run_ddpm_candidate_cache_sampler
+    from diffusionhard_b200.engine import MDLMEngine
+    from diffusionhard_b200.model import MDLMConfig, build_quantized
+
+    peaks, peaks_kind = load_peaks()
+    cfg = MDLMConfig()
+    qm = build_quantized(cfg, seed=0)
+    B, L, S = args.batch, args.seq_len, args.denoise_steps
+    eng = MDLMEngine(qm, B, L)
+    eng.seq_offset = rank * B
+    ids_dev = torch.full((B, L), cfg.mask_token_id, dtype=torch.int64, device="cuda")
+    host_ids = torch.full((B, L), cfg.mask_token_id, dtype=torch.int64).pin_memory()
+
+    for _ in range(args.warmup):
+        eng.generate(ids_dev, steps=S, seed=0, graph=True)
+    torch.cuda.synchronize()
+    barrier(world)
+
+    # ------------------------------------------------ device-timed region
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            eng.generate(ids_dev, steps=S, seed=0, graph=True)
+        end.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    clock_info = clocks.summary()
+    tokens = world * B * L * args.steps
+    value = tokens / (ms * 1e-3)
+    meta = eng.metadata(S)
+    masks_left = int((eng.tokens == cfg.mask_token_id).sum().item())
+
+    # ------------------------------------------------ end-to-end (public API, host buffers)
+    for _ in range(2):
+        run_ddpm_candidate_cache_sampler(eng, host_ids, mask_token_id=cfg.mask_token_id, steps=S, seed=0)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.steps):
+        ids_out, _, meta_e2e = run_ddpm_candidate_cache_sampler(eng, host_ids, mask_token_id=cfg.mask_token_id,
+                                                                steps=S, seed=0)
+    e_end.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+    wall_e2e = max_over_ranks((time.perf_counter() - t0) * 1e3, world)
+    e2e_value = tokens / (e2e_ms * 1e-3)
+
+    # ------------------------------------------------ kernel breakdown / roofline
+    bd = kernel_breakdown(eng)
+    per_gen = {k: v * (1 if k == "embed_gather" else (len(eng.blocks) * (2 if k == "ln_smooth_quant" else 1)))
+               for k, v in bd.items()}
+    dominant = max(per_gen, key=per_gen.get)
+    roof = roofline_for(dominant, bd[dominant], eng, peaks, peaks_kind)
+    traffic_file = ROOT / "profiles" / "traffic.json"
+    traffic = None
+    if traffic_file.exists():
+        traffic = json.loads(traffic_file.read_text()).get(dominant)
+    roof["traffic"] = traffic
+    head = head_microbench(qm, peaks, peaks_kind) if rank == 0 else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import cpu_baseline
+
+        r = cpu_baseline.measure(qm, transitions=3, steps=S)
+        cpu = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in r.items()
+               if k in ("value", "unit", "cores", "kind", "sample")}
+
+    err = __import__("numpy").zeros(1, "uint32")
+    _lib.call("dh_device_error", err.ctypes.data, 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (random-init N(0,0.02) weights, all-masked canvases)",
+            "config": {"workload": "MDLM-169.6M W8A8, batch 32 x L=1024 per GPU, 64 ddpm_cache steps + final pass",
+                       "global_batch": world * B, "seq_len": L, "steps": S, "parallelism": f"dp{world} batch-sharded",
+                       "l2": "activations per forward (> 1 GB) exceed L2; no flush needed"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": B * L * 8,
+                    "d2h_bytes_per_step": B * L * 8 + 3 * S * 4, "wall_ms_per_step": round(wall_e2e / args.steps, 3)},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "gpu_launches": eng.launches_per_generation(S) * args.steps,
+            "clocks": clock_info,
+            "kernel_ms": {k: round(v, 4) for k, v in bd.items()},
+            "kernel_ms_per_generation_est": {k: round(v * (S + 1), 2) for k, v in per_gen.items()},
+            "head_microbench": head,
+            "generation": {"model_evaluations": meta["model_evaluations"],
+                           "sampling_transitions": meta["sampling_transitions"], "masks_left": masks_left,
+                           "e2e_matches_device": bool(torch.equal(ids_out.cuda().to(torch.int32), eng.tokens.view(B, L)))},
+            "device_error": int(err[0]),
+        }
+        print(json.dumps(line), flush=True)
+    eng._graphs.clear()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -69,7 +69,7 @@ loop_plan_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t final_pass,
 // One CTA per sequence.  Warp-level compaction (ballot) then one atomicAdd per
 // warp reserves contiguous slots in the global row list.
 __global__ void __launch_bounds__(256)
-loop_select_kernel(uint32_t L, uint32_t step, uint32_t seed, uint64_t threshold,
+loop_select_kernel(uint32_t L, uint32_t step, uint32_t seed, uint32_t seq_offset, uint64_t threshold,
                    uint32_t final_pass, const uint64_t* __restrict__ active,
                    const uint32_t* __restrict__ eval_id, uint32_t* __restrict__ sel_rows,
                    uint32_t* __restrict__ sel_pos, uint32_t* __restrict__ sel_key,
@@ -86,7 +86,7 @@ loop_select_kernel(uint32_t L, uint32_t step, uint32_t seed, uint64_t threshold,
                 if (final_pass) {
                     take = true;
                 } else {
-                    Philox4 r = philox4x32_10(p >> 2, 0u, step, 1u, seed, b);
+                    Philox4 r = philox4x32_10(p >> 2, 0u, step, 1u, seed, seq_offset + b);
                     take = static_cast<uint64_t>(philox_lane(r, p & 3u)) < threshold;
                 }
             }
@@ -100,7 +100,7 @@ loop_select_kernel(uint32_t L, uint32_t step, uint32_t seed, uint64_t threshold,
             const uint32_t slot = base + __popc(mask & ((1u << lane_id()) - 1u));
             sel_rows[slot] = b * L + p;
             sel_pos[slot] = p;
-            sel_key[slot] = b;
+            sel_key[slot] = seq_offset + b;
             sel_eval[slot] = ev;
         }
     }
@@ -197,7 +197,7 @@ uint32_t dh_loop_plan(uint32_t sequences, uint32_t positions, uint32_t step, uin
 }
 
 uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t seed,
-                        uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
+                        uint32_t seq_offset, uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
                         const uint32_t* eval_id, uint32_t* sel_rows, uint32_t* sel_pos,
                         uint32_t* sel_key, uint32_t* sel_eval, uint32_t* sel_count, void* stream) {
     if (threshold_q32 > DH_REVEAL_PROBABILITY_ONE_Q32) return DH_CAND_INVALID_THRESHOLD;
@@ -205,7 +205,7 @@ uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, u
         return DH_ERR_NULL_POINTER;
     if (sequences == 0 || positions == 0) return DH_ERR_INVALID_ARGUMENT;
     loop_select_kernel<<<sequences, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        positions, step, seed, threshold_q32, final_pass, active, eval_id, sel_rows, sel_pos,
+        positions, step, seed, seq_offset, threshold_q32, final_pass, active, eval_id, sel_rows, sel_pos,
         sel_key, sel_eval, sel_count);
     DH_LAUNCH_CHECK();
     return DH_OK;

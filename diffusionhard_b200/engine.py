@@ -105,6 +105,7 @@ class MDLMEngine:
         self.sel_key = torch.empty(M, dtype=u32, device=d)
         self.sel_eval = torch.empty(M, dtype=u32, device=d)
         self.counters: Optional[Any] = None
+        self.seq_offset = 0  # global index of local sequence 0 (Philox key_hi)
         self._graphs: Dict[Any, Any] = {}
         self.launches_per_forward = 1 + 9 * len(self.blocks)
 
@@ -196,7 +197,7 @@ class MDLMEngine:
                  p(self.eval_id), p(self.fwd_rows), p(self.sel_count), p(self.counters), s)
             self.forward(run_rows=self.fwd_rows)
             thr = 0 if final else thresholds[k]
-            call("dh_loop_select", B, L, min(k, steps - 1), seed, thr, final, p(self.active),
+            call("dh_loop_select", B, L, min(k, steps - 1), seed, self.seq_offset, thr, final, p(self.active),
                  p(self.eval_id), p(self.sel_rows), p(self.sel_pos), p(self.sel_key), p(self.sel_eval),
                  p(self.sel_count), s)
             self.final_hidden_q(self.sel_rows, self.sel_count)
@@ -227,7 +228,7 @@ class MDLMEngine:
                   _lib.ptr(self.tokens), _lib.ptr(self.active), _lib.ptr(self.need_eval),
                   _lib.ptr(self.eval_id), _lib.ptr(self.counters), s)
         if graph:
-            key = (steps, seed, sampling_epsilon)
+            key = (steps, seed, sampling_epsilon, self.seq_offset)
             g = self._graphs.get(key)
             if g is None:
                 # warm-up outside capture (function attributes, tensor maps)

@@ -303,7 +303,7 @@ uint32_t dh_loop_plan(uint32_t sequences, uint32_t positions, uint32_t step, uin
                       uint32_t* eval_id, uint32_t* fwd_rows, uint32_t* sel_count,
                       int32_t* counters, void* stream);
 uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t seed,
-                        uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
+                        uint32_t seq_offset, uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
                         const uint32_t* eval_id, uint32_t* sel_rows, uint32_t* sel_pos,
                         uint32_t* sel_key, uint32_t* sel_eval, uint32_t* sel_count, void* stream);
 uint32_t dh_loop_commit(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t steps,

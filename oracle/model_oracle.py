@@ -21,6 +21,12 @@ from typing import Dict, List, Optional, Tuple
 import numpy as np
 
 
+# When True, the int8 product uses torch._int_mm -- the reference's own CPU
+# path (fixed_mlp._integer_matmul, fixed_mlp.py:55-62); otherwise an exact
+# float64 matmul (identical int32 results, no int8 kernel needed).
+USE_INT_MM = False
+
+
 def w8a8_linear(a, ql, return_parts: bool = False):
     """Reference quantized_linear arithmetic with a static smoothing scale."""
     import torch
@@ -31,7 +37,14 @@ def w8a8_linear(a, ql, return_parts: bool = False):
     scale = torch.where(maximum > 0, maximum / 127.0, torch.ones_like(maximum))
     q = torch.round(a / scale[:, None]).clamp(-127, 127).to(torch.int8)
     w_scale = torch.from_numpy(ql.w_scale)
-    acc = torch.matmul(q.double(), torch.from_numpy(ql.weight_q).double().t()).to(torch.int64)
+    if USE_INT_MM:
+        wq = getattr(ql, "_wq_t", None)
+        if wq is None:
+            wq = torch.from_numpy(ql.weight_q).t().contiguous()
+            ql._wq_t = wq
+        acc = torch._int_mm(q.contiguous(), wq).to(torch.int64)
+    else:
+        acc = torch.matmul(q.double(), torch.from_numpy(ql.weight_q).double().t()).to(torch.int64)
     combined = scale[:, None] * w_scale[None, :]
     out = (acc.double() * combined.double() + torch.from_numpy(ql.bias).double()[None, :]).float()
     if return_parts:
