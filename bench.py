@@ -161,17 +161,17 @@ def kernel_breakdown(eng) -> dict:
         "ln_smooth_quant": lambda: c("dh_ln_smooth_quant", p(eng.x), p(qkv.inv_smooth), p(eng.act_q),
                                      p(eng.act_scale), M, None, None, None, s),
         "gemm_qkv_rope": lambda: c("dh_gemm_qkv_rope", p(eng.act_q), p(eng.act_scale), p(qkv.w),
-                                   p(qkv.w_scale), p(qkv.bias), p(eng.rope_cos), p(eng.rope_sin), M, L, 0,
+                                   p(qkv.w_scale), p(qkv.bias), p(eng.rope_cos), p(eng.rope_sin), p(out.inv_smooth), M, L, 0,
                                    eng.kv_stride, 0, p(eng.q), p(k), p(vt), None, s),
         "attention": lambda: c("dh_attention", p(eng.q), p(k), p(vt), p(eng.attn), eng.B, L, eng.kv_len,
                                eng.kv_stride, None, s),
-        "quant_rows_768": lambda: c("dh_quant_rows_bf16", p(eng.attn), p(out.inv_smooth), p(eng.act_q),
+        "quant_rows_768": lambda: c("dh_quant_rows_bf16", p(eng.attn), None, p(eng.act_q),
                                     p(eng.act_scale), M, 768, None, s),
         "gemm_out_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(out.w),
                                        p(out.w_scale), p(out.bias), p(eng.x), M, 768, 768, None, s),
         "gemm_up_gelu": lambda: c("dh_gemm_gelu", p(eng.act_q), p(eng.act_scale), p(up.w), p(up.w_scale),
-                                  p(up.bias), p(eng.mlp), M, 3072, 768, None, s),
-        "quant_rows_3072": lambda: c("dh_quant_rows_bf16", p(eng.mlp), p(down.inv_smooth), p(eng.act_q),
+                                  p(up.bias), p(down.inv_smooth), p(eng.mlp), M, 3072, 768, None, s),
+        "quant_rows_3072": lambda: c("dh_quant_rows_bf16", p(eng.mlp), None, p(eng.act_q),
                                      p(eng.act_scale), M, 3072, None, s),
         "gemm_down_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(down.w),
                                         p(down.w_scale), p(down.bias), p(eng.x), M, 768, 3072, None, s),
@@ -242,6 +242,29 @@ def head_microbench(qm, peaks: dict, peaks_kind: str) -> dict:
             "note": "per-element Philox4x32-10 + Gumbel Q10 + exact fp64 dequant in the epilogue"}
 
 
+def profile_forward(args) -> None:
+    """One forward over B x L rows plus the head over 512 selected rows."""
+    import torch
+
+    from diffusionhard_b200.engine import MDLMEngine
+    from diffusionhard_b200.model import MDLMConfig, build_quantized
+
+    cfg = MDLMConfig()
+    qm = build_quantized(cfg, seed=0)
+    eng = MDLMEngine(qm, args.batch, args.seq_len)
+    eng.tokens.fill_(cfg.mask_token_id)
+    rows = torch.arange(512, dtype=torch.int32, device="cuda") * 61
+    count = torch.tensor([512], dtype=torch.int32, device="cuda")
+    pos = rows % args.seq_len
+    key = rows // args.seq_len
+    for _ in range(2):
+        eng.forward()
+        eng.final_hidden_q(rows, count)
+        eng.head_argmax(eng.M, 1, rows_count=count, row_position=pos, row_key_hi=key, key_lo=0)
+    torch.cuda.synchronize()
+    print("profile-forward done", flush=True)
+
+
 def run_reference(args, world: int, rank: int) -> None:
     if rank != 0:
         return
@@ -280,6 +303,9 @@ def main() -> None:
     ap.add_argument("--seq-len", type=int, default=1024)
     ap.add_argument("--denoise-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-forward", action="store_true",
+                    help="run one warm-up forward, then one forward + one head call "
+                         "(a short launch list for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -302,6 +328,9 @@ def main() -> None:
     from diffusionhard_b200.model import MDLMConfig, build_quantized
 
     peaks, peaks_kind = load_peaks()
+    if args.profile_forward:
+        profile_forward(args)
+        return
     cfg = MDLMConfig()
     qm = build_quantized(cfg, seed=0)
     B, L, S = args.batch, args.seq_len, args.denoise_steps

@@ -11,10 +11,11 @@
 //   warp 0   TMA: Q once, then K_j and V_j tiles of 128 keys
 //   warp 1   tcgen05 MMA (kind::f16, bf16 x bf16 -> fp32 in TMEM):
 //            S_j = Q K_j^T (128 x 128 x 64), O_j = P_j V_j (128 x 64 x 128)
-//   warps 2-5 softmax: one thread per query row reads its S row from TMEM,
-//            keeps the running max / sum in registers (base-2 domain), writes
-//            P_j (bf16) to 128-byte-swizzled shared memory as the A operand of
-//            the PV MMA, and folds O_j into a register accumulator.
+//   warps 2-5 softmax: one thread per query row reads its S row from TMEM
+//            once, keeps the running max / sum in registers (base-2 domain),
+//            writes P_j (bf16) to 128-byte-swizzled shared memory as the A
+//            operand of the PV MMA; O accumulates in TMEM across key tiles and
+//            is rescaled in place only when the row max grows by > 2^8.
 // 80 KB shared memory and 256 TMEM columns per CTA, so two CTAs share an SM
 // and one CTA's softmax overlaps the other's MMAs.  All waits are bounded.
 #include <cuda.h>
@@ -54,6 +55,18 @@ DH_DEVINL void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Hardware base-2 exponential (MUFU), flush-to-zero.
+DH_DEVINL float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+DH_DEVINL uint32_t pack_bf16(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 __global__ void __launch_bounds__(kThreads, 2)
 attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const AttnArgs args) {
@@ -75,7 +88,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
 
     if (warp == 0 && lane == 0) {
         for (uint32_t i = 0; i < kNumBars; ++i) {
-            const bool softmax_side = i == kSFree || i == kPFull || i == kOFree;
+            const bool softmax_side = i == kSFree || i == kPFull;
             tc::mbar_init(&bars[i], softmax_side ? 128u : 1u);
         }
         tc::fence_barrier_init();
@@ -132,8 +145,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                 tc::mma_commit(&bars[kSFull]);
                 tc::mma_commit(&bars[kKEmpty]);
                 ok = tc::mbar_wait(&bars[kPFull], full, tc::kErrTimeoutFull) &&
-                     tc::mbar_wait(&bars[kVFull], full, tc::kErrTimeoutFull) &&
-                     tc::mbar_wait(&bars[kOFree], empty, tc::kErrTimeoutAccEmpty);
+                     tc::mbar_wait(&bars[kVFull], full, tc::kErrTimeoutFull);
                 if (!ok) break;
                 tc::tc_fence_after();
 #pragma unroll
@@ -142,117 +154,123 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                     tc::mma_bf16(o_tmem,
                                  tc::desc_advance(tc::smem_desc_sw128(p_s + sub * (kPBytes / 2)), off),
                                  tc::desc_advance(tc::smem_desc_sw128(v_s + sub * (kVBytes / 2)), off),
-                                 kIdescO, kk != 0);
+                                 kIdescO, (kk | j) != 0);
                 }
-                tc::mma_commit(&bars[kOFull]);
                 tc::mma_commit(&bars[kVEmpty]);
                 tc::mma_commit(&bars[kPEmpty]);
+                if (j + 1 == n_kv) tc::mma_commit(&bars[kOFull]);
             }
             tc::mma_commit(&bars[kDrain]);
             tc::mbar_wait(&bars[kDrain], 0, tc::kErrTimeoutAccFull);
         }
     } else {
         // ----------------------------------------------------------- softmax
+        // One thread per query row.  S_j is read from TMEM once into
+        // registers; p = exp2(s*c - m) with the running max m kept stale
+        // until the tile max exceeds it by more than 8 (p <= 2^8 meanwhile),
+        // and only then O (accumulated in TMEM across tiles) and l are
+        // rescaled -- a warp-uniform, rare path.
         const uint32_t quad = warp & 3u;
         const uint32_t r = quad * 32 + lane;  // query row within the tile
         const uint32_t lane_base = (quad * 32u) << 16;
         const float c = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
-        float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
-        float o[kDh];
-#pragma unroll
-        for (uint32_t d = 0; d < kDh; ++d) o[d] = 0.f;
+        float m = 0.f, l = 0.f;
         bool ok = true;
         for (uint32_t j = 0; j < n_kv && ok; ++j) {
             const uint32_t full = j & 1u, empty = full ^ 1u;
             if (!tc::mbar_wait(&bars[kSFull], full, tc::kErrTimeoutAccFull)) { ok = false; break; }
             tc::tc_fence_after();
-            // pass 1: row max of this tile
-            float tmax = -INFINITY;
-#pragma unroll 1
-            for (uint32_t cc = 0; cc < 4; ++cc) {
-                uint32_t v[32];
-                tc::tmem_ld_32x32b_x32(tmem + lane_base + cc * 32, v);
-                tc::tmem_ld_wait();
+            uint32_t sv[128];
 #pragma unroll
-                for (uint32_t e = 0; e < 32; ++e) tmax = fmaxf(tmax, __uint_as_float(v[e]));
-            }
-            const float m_new = fmaxf(m, tmax * c);
-            const float alpha = exp2f(m - m_new);
-            m = m_new;
-            // P buffer free (previous PV finished reading it)
-            if (!tc::mbar_wait(&bars[kPEmpty], empty, tc::kErrTimeoutEmpty)) { ok = false; break; }
-            // pass 2: p = exp2(s*c - m), bf16 into swizzled smem
-            float sum = 0.f;
-#pragma unroll 1
-            for (uint32_t cc = 0; cc < 4; ++cc) {
-                uint32_t v[32];
-                tc::tmem_ld_32x32b_x32(tmem + lane_base + cc * 32, v);
-                tc::tmem_ld_wait();
-                uint8_t* sub = p_s + (cc >> 1) * (kPBytes / 2) + (r >> 3) * 1024 + (r & 7u) * 128;
-#pragma unroll
-                for (uint32_t g = 0; g < 4; ++g) {  // 4 chunks of 8 keys
-                    uint4 pk;
-                    __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-                    for (uint32_t e = 0; e < 4; ++e) {
-                        const float p0 = exp2f(__uint_as_float(v[8 * g + 2 * e]) * c - m_new);
-                        const float p1 = exp2f(__uint_as_float(v[8 * g + 2 * e + 1]) * c - m_new);
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-                        // the sum uses the rounded values the MMA will see
-                        const float2 f2 = __bfloat1622float2(b2);
-                        sum += f2.x + f2.y;
-                        hp[e] = b2;
-                    }
-                    const uint32_t chunk = ((cc & 1u) * 4 + g) ^ (r & 7u);
-                    *reinterpret_cast<uint4*>(sub + chunk * 16) = pk;
-                }
-            }
-            l = l * alpha + sum;
+            for (uint32_t cc = 0; cc < 4; ++cc)
+                tc::tmem_ld_32x32b_x32(tmem + lane_base + cc * 32,
+                                       *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
+            tc::tmem_ld_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[kSFree]);
-            fence_proxy_async_smem();
-            tc::mbar_arrive(&bars[kPFull]);
-            // fold the previous tile's O (lagged by one tile)
-            if (j > 0) {
-                if (!tc::mbar_wait(&bars[kOFull], empty, tc::kErrTimeoutAccFull)) { ok = false; break; }
-                tc::tc_fence_after();
-                uint32_t v0[32], v1[32];
-                tc::tmem_ld_32x32b_x32(tmem + lane_base + 128, v0);
-                tc::tmem_ld_32x32b_x32(tmem + lane_base + 160, v1);
-                tc::tmem_ld_wait();
-                tc::tc_fence_before();
-                tc::mbar_arrive(&bars[kOFree]);
+            float tmax = __uint_as_float(sv[0]);
 #pragma unroll
-                for (uint32_t d = 0; d < 32; ++d) {
-                    o[d] = o[d] * alpha_prev + __uint_as_float(v0[d]);
-                    o[d + 32] = o[d + 32] * alpha_prev + __uint_as_float(v1[d]);
-                }
+            for (uint32_t e = 1; e < 127; e += 2) {
+                float t3;
+                asm("max.f32 %0, %1, %2, %3;" : "=f"(t3) : "f"(tmax), "f"(__uint_as_float(sv[e])),
+                    "f"(__uint_as_float(sv[e + 1])));
+                tmax = t3;
             }
-            alpha_prev = alpha;
+            tmax = fmaxf(tmax, __uint_as_float(sv[127]));
+            const float mt = tmax * c;
+            float alpha = 1.f;
+            bool need = false;
+            if (j == 0) {
+                m = mt;
+            } else if (mt > m + 8.0f) {
+                need = true;
+                alpha = ex2_approx(m - mt);
+                m = mt;
+                l *= alpha;
+            }
+            const float2 c2 = make_float2(c, c);
+            const float2 nm2 = make_float2(-m, -m);
+            float2 sum2 = make_float2(0.f, 0.f);
+            uint32_t pk[64];
+#pragma unroll
+            for (uint32_t e = 0; e < 64; ++e) {
+                const float2 sv2 = make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1]));
+                const float2 a = __ffma2_rn(sv2, c2, nm2);
+                const float2 pe = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+                sum2 = __fadd2_rn(sum2, pe);
+                pk[e] = pack_bf16(pe.x, pe.y);
+            }
+            // P buffer free and O stable: the previous PV finished.
+            if (!tc::mbar_wait(&bars[kPEmpty], empty, tc::kErrTimeoutEmpty)) { ok = false; break; }
+            if (__any_sync(0xFFFFFFFFu, need)) {
+                tc::tc_fence_after();
+#pragma unroll
+                for (uint32_t h2 = 0; h2 < 2; ++h2) {
+                    uint32_t ov[32];
+                    tc::tmem_ld_32x32b_x32(tmem + lane_base + 128 + 32 * h2, ov);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (uint32_t d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+                    tc::tmem_st_32x32b_x32(tmem + lane_base + 128 + 32 * h2, ov);
+                }
+                tc::tmem_st_wait();
+            }
+            uint8_t* rowp = p_s + (r >> 3) * 1024 + (r & 7u) * 128;
+#pragma unroll
+            for (uint32_t g = 0; g < 16; ++g) {  // 16 chunks of 8 keys
+                const uint32_t sub = g >> 3;
+                const uint32_t chunk = (g & 7u) ^ (r & 7u);
+                *reinterpret_cast<uint4*>(rowp + sub * (kPBytes / 2) + chunk * 16) =
+                    make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+            }
+            l += sum2.x + sum2.y;
+            fence_proxy_async_smem();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars[kPFull]);
         }
         if (ok && n_kv > 0) {
-            if (tc::mbar_wait(&bars[kOFull], (n_kv - 1) & 1u, tc::kErrTimeoutAccFull)) {
+            if (tc::mbar_wait(&bars[kOFull], 0, tc::kErrTimeoutAccFull)) {
                 tc::tc_fence_after();
                 uint32_t v0[32], v1[32];
                 tc::tmem_ld_32x32b_x32(tmem + lane_base + 128, v0);
                 tc::tmem_ld_32x32b_x32(tmem + lane_base + 160, v1);
                 tc::tmem_ld_wait();
-#pragma unroll
-                for (uint32_t d = 0; d < 32; ++d) {
-                    o[d] = o[d] * alpha_prev + __uint_as_float(v0[d]);
-                    o[d + 32] = o[d + 32] * alpha_prev + __uint_as_float(v1[d]);
-                }
                 const float inv_l = 1.0f / l;
                 const uint64_t tok = static_cast<uint64_t>(seq) * args.q_len + q_tile * kTile + r;
                 __nv_bfloat16* dst = args.out + tok * (kHeads * kDh) + head * kDh;
 #pragma unroll
-                for (uint32_t d = 0; d < kDh; d += 8) {
-                    uint4 pk;
-                    __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-                    for (uint32_t e = 0; e < 4; ++e)
-                        hp[e] = __floats2bfloat162_rn(o[d + 2 * e] * inv_l, o[d + 2 * e + 1] * inv_l);
-                    *reinterpret_cast<uint4*>(dst + d) = pk;
+                for (uint32_t d = 0; d < 32; d += 8) {
+                    uint4 a, b;
+                    a.x = pack_bf16(__uint_as_float(v0[d]) * inv_l, __uint_as_float(v0[d + 1]) * inv_l);
+                    a.y = pack_bf16(__uint_as_float(v0[d + 2]) * inv_l, __uint_as_float(v0[d + 3]) * inv_l);
+                    a.z = pack_bf16(__uint_as_float(v0[d + 4]) * inv_l, __uint_as_float(v0[d + 5]) * inv_l);
+                    a.w = pack_bf16(__uint_as_float(v0[d + 6]) * inv_l, __uint_as_float(v0[d + 7]) * inv_l);
+                    b.x = pack_bf16(__uint_as_float(v1[d]) * inv_l, __uint_as_float(v1[d + 1]) * inv_l);
+                    b.y = pack_bf16(__uint_as_float(v1[d + 2]) * inv_l, __uint_as_float(v1[d + 3]) * inv_l);
+                    b.z = pack_bf16(__uint_as_float(v1[d + 4]) * inv_l, __uint_as_float(v1[d + 5]) * inv_l);
+                    b.w = pack_bf16(__uint_as_float(v1[d + 6]) * inv_l, __uint_as_float(v1[d + 7]) * inv_l);
+                    *reinterpret_cast<uint4*>(dst + d) = a;
+                    *reinterpret_cast<uint4*>(dst + 32 + d) = b;
                 }
             }
         }

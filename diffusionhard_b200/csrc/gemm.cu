@@ -20,11 +20,11 @@ struct EpiStoreI32 : EpiBase {
         uint32_t n;
     };
     struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, uint32_t, bool, uint32_t, uint8_t*) {}
-    static DH_DEVINL void chunk(const Params& p, TileState&, uint32_t row, bool ok, uint32_t col0,
+    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
+    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
-        if (!ok) return;
-        int32_t* dst = p.c + static_cast<uint64_t>(row) * p.ldc + col0;
+        if (!ctx.row_ok) return;
+        int32_t* dst = p.c + static_cast<uint64_t>(ctx.row) * p.ldc + col0;
         if (col0 + 32 <= p.n && (p.ldc & 3u) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
 #pragma unroll
             for (uint32_t j = 0; j < 32; j += 4)
@@ -38,7 +38,7 @@ struct EpiStoreI32 : EpiBase {
                 if (col0 + j < p.n) dst[j] = static_cast<int32_t>(v[j]);
         }
     }
-    static DH_DEVINL void tile_end(const Params&, TileState&, uint32_t, bool) {}
+    static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
 
 // y = acc * (a_scale[row] * w_scale[col]) + bias[col]   (fp32)
@@ -46,18 +46,35 @@ DH_DEVINL float dequant(uint32_t acc, float ab, float w, float b) {
     return __fmaf_rn(static_cast<float>(static_cast<int32_t>(acc)), ab * w, b);
 }
 
+// Staging layouts (per epilogue warp, 32 rows): a row of 128 B is 8 chunks of
+// 16 B stored at chunk c ^ (row & 7); a row of 64 B is 4 chunks stored at
+// c ^ ((row >> 1) & 3).  Row-owner writes and row-major reads by 8 (resp. 4)
+// consecutive lanes are both bank-conflict free.
+DH_DEVINL uint32_t swz128(uint32_t row, uint32_t chunk) { return row * 128 + ((chunk ^ (row & 7u)) << 4); }
+DH_DEVINL uint32_t swz64(uint32_t row, uint32_t chunk) { return row * 64 + ((chunk ^ ((row >> 1) & 3u)) << 4); }
+
+DH_DEVINL uint32_t pack_bf16x2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // QKV projection (N = 3 * 768): dequant + rotary on q and k (rotate-half,
 // mlx_mdlm.py:316-329 / mdlm.py:399-410), then scatter to the attention
-// layouts: Q, K as [B, H, len, 64] and V transposed as [B, H, 64, kv_len], all
-// bf16.  A chunk is 64 columns = one head of one of q / k / v.
+// layouts: Q [B, H, len, 64], K [B, H, kv_stride, 64] and V transposed
+// [B, H, 64, kv_stride], all bf16.  A chunk is 64 columns = one head of one of
+// q / k / v.  A warp's 32 rows are 32 consecutive tokens of one sequence, so
+// its Q / K block is 4 KB contiguous and its V^T block is 64 runs of 64 bytes:
+// both are written through the warp's staging buffer with full-line stores.
 struct EpiQKV : EpiBase {
     static constexpr uint32_t kChunk = 64;
+    static constexpr uint32_t kStagingPerWarp = 32 * 128;
     struct Params {
         const float* a_scale;
         const float* w_scale;
         const float* bias;
         const float* rope_cos;  // [max_pos, 32]
         const float* rope_sin;
+        const float* v_scale;   // [768] per-channel factor on V (SmoothQuant 1/s of attn-out), or null
         uint32_t seq_len;       // rows per sequence in this forward
         uint32_t pos_offset;    // rotary position of the first row of a sequence
         uint32_t kv_stride;     // rows per (sequence, head) in the K / V buffers
@@ -67,55 +84,94 @@ struct EpiQKV : EpiBase {
         __nv_bfloat16* vt;
     };
     struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, uint32_t, bool, uint32_t, uint8_t*) {}
-    static DH_DEVINL void chunk(const Params& p, TileState&, uint32_t row, bool ok, uint32_t col0,
+    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
+    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
-        if (!ok) return;
-        const float ab = p.a_scale[row];
+        constexpr uint32_t heads = 12;
+        const float ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
         const uint32_t which = col0 / 768u;
         const uint32_t h = (col0 % 768u) / 64u;
-        const uint32_t b = row / p.seq_len;
-        const uint32_t t = row % p.seq_len;
+        const uint32_t t = ctx.row % p.seq_len;
         float y[64];
+        const float4* w4 = reinterpret_cast<const float4*>(p.w_scale + col0);
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
 #pragma unroll
-        for (uint32_t j = 0; j < 64; ++j)
-            y[j] = dequant(v[j], ab, __ldg(p.w_scale + col0 + j), __ldg(p.bias + col0 + j));
-        const uint32_t heads = 12;
+        for (uint32_t j = 0; j < 16; ++j) {
+            const float4 w = __ldg(w4 + j), bb = __ldg(b4 + j);
+            y[4 * j] = dequant(v[4 * j], ab, w.x, bb.x);
+            y[4 * j + 1] = dequant(v[4 * j + 1], ab, w.y, bb.y);
+            y[4 * j + 2] = dequant(v[4 * j + 2], ab, w.z, bb.z);
+            y[4 * j + 3] = dequant(v[4 * j + 3], ab, w.w, bb.w);
+        }
+        const uint32_t b = ctx.row0 / p.seq_len;
+        const uint32_t t0 = ctx.row0 % p.seq_len;
+        const uint32_t lane = ctx.lane;
         if (which < 2) {
-            const float* cs = p.rope_cos + static_cast<uint64_t>(t + p.pos_offset) * 32;
-            const float* sn = p.rope_sin + static_cast<uint64_t>(t + p.pos_offset) * 32;
+            const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + static_cast<uint64_t>(t + p.pos_offset) * 32);
+            const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + static_cast<uint64_t>(t + p.pos_offset) * 32);
 #pragma unroll
-            for (uint32_t i = 0; i < 32; ++i) {
-                const float c = __ldg(cs + i), s = __ldg(sn + i);
-                const float x1 = y[i], x2 = y[i + 32];
-                y[i] = x1 * c - x2 * s;
-                y[i + 32] = x2 * c + x1 * s;
+            for (uint32_t i4 = 0; i4 < 8; ++i4) {
+                const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+                const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
+                const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (uint32_t e = 0; e < 4; ++e) {
+                    const uint32_t i = 4 * i4 + e;
+                    const float x1 = y[i], x2 = y[i + 32];
+                    y[i] = x1 * cc[e] - x2 * ss[e];
+                    y[i + 32] = x2 * cc[e] + x1 * ss[e];
+                }
             }
+#pragma unroll
+            for (uint32_t w = 0; w < 32; w += 4)
+                *reinterpret_cast<uint4*>(ctx.stage + swz128(lane, w / 4)) =
+                    make_uint4(pack_bf16x2(y[2 * w], y[2 * w + 1]), pack_bf16x2(y[2 * w + 2], y[2 * w + 3]),
+                               pack_bf16x2(y[2 * w + 4], y[2 * w + 5]), pack_bf16x2(y[2 * w + 6], y[2 * w + 7]));
+            __syncwarp();
             const uint32_t len = which == 0 ? p.seq_len : p.kv_stride;
-            const uint32_t pos = which == 0 ? t : t + p.kv_offset;
-            __nv_bfloat16* dst = (which == 0 ? p.q : p.k) +
-                                 ((static_cast<uint64_t>(b) * heads + h) * len + pos) * 64;
+            const uint32_t pos0 = which == 0 ? t0 : t0 + p.kv_offset;
+            // the warp's 32 rows x 128 B are contiguous: 4 rows per instruction
+            uint4* dst = reinterpret_cast<uint4*>((which == 0 ? p.q : p.k) +
+                                                  ((static_cast<uint64_t>(b) * heads + h) * len + pos0) * 64);
 #pragma unroll
-            for (uint32_t j = 0; j < 64; j += 8) {
-                uint4 pk;
-                __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-                for (uint32_t e = 0; e < 4; ++e) hp[e] = __floats2bfloat162_rn(y[j + 2 * e], y[j + 2 * e + 1]);
-                *reinterpret_cast<uint4*>(dst + j) = pk;
+            for (uint32_t i = 0; i < 8; ++i) {
+                const uint32_t rr = i * 4 + (lane >> 3);
+                if (ctx.row0 + rr < ctx.m_eff)
+                    dst[rr * 8 + (lane & 7u)] = *reinterpret_cast<const uint4*>(ctx.stage + swz128(rr, lane & 7u));
             }
+            __syncwarp();
         } else {
-            __nv_bfloat16* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride +
-                                 t + p.kv_offset;
+            if (p.v_scale) {
+                const float4* vs4 = reinterpret_cast<const float4*>(p.v_scale + h * 64);
 #pragma unroll
-            for (uint32_t j = 0; j < 64; ++j) dst[static_cast<uint64_t>(j) * p.kv_stride] = __float2bfloat16_rn(y[j]);
+                for (uint32_t j = 0; j < 16; ++j) {
+                    const float4 f = __ldg(vs4 + j);
+                    y[4 * j] *= f.x;
+                    y[4 * j + 1] *= f.y;
+                    y[4 * j + 2] *= f.z;
+                    y[4 * j + 3] *= f.w;
+                }
+            }
+            // V^T: for each channel d the warp's 32 consecutive tokens form
+            // one 64-byte run, so lane = token stores are already coalesced.
+            if (ctx.row_ok) {
+                __nv_bfloat16* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride +
+                                     t + p.kv_offset;
+#pragma unroll
+                for (uint32_t d = 0; d < 64; ++d)
+                    dst[static_cast<uint64_t>(d) * p.kv_stride] = __float2bfloat16_rn(y[d]);
+            }
         }
     }
-    static DH_DEVINL void tile_end(const Params&, TileState&, uint32_t, bool) {}
+    static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
 
 // x[row, col] += acc * (a_scale * w_scale) + bias  (attention out, MLP down).
+// The residual read-modify-write goes through the staging buffer with one
+// 128-byte row segment per warp instruction.
 struct EpiResidual : EpiBase {
     static constexpr uint32_t kChunk = 32;
+    static constexpr uint32_t kStagingPerWarp = 32 * 128;
     struct Params {
         const float* a_scale;
         const float* w_scale;
@@ -124,26 +180,46 @@ struct EpiResidual : EpiBase {
         uint32_t n;
     };
     struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, uint32_t, bool, uint32_t, uint8_t*) {}
-    static DH_DEVINL void chunk(const Params& p, TileState&, uint32_t row, bool ok, uint32_t col0,
+    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
+    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
-        if (!ok) return;
-        const float ab = p.a_scale[row];
-        float4* dst = reinterpret_cast<float4*>(p.x + static_cast<uint64_t>(row) * p.n + col0);
+        const float ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        const uint32_t lane = ctx.lane;
 #pragma unroll
         for (uint32_t j = 0; j < 32; j += 4) {
-            float4 o = dst[j / 4];
             const float4 w = __ldg(reinterpret_cast<const float4*>(p.w_scale + col0 + j));
-            float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p.bias) b = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
-            o.x += dequant(v[j], ab, w.x, b.x);
-            o.y += dequant(v[j + 1], ab, w.y, b.y);
-            o.z += dequant(v[j + 2], ab, w.z, b.z);
-            o.w += dequant(v[j + 3], ab, w.w, b.w);
-            dst[j / 4] = o;
+            float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (p.bias) bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+            *reinterpret_cast<float4*>(ctx.stage + swz128(lane, j / 4)) =
+                make_float4(dequant(v[j], ab, w.x, bb.x), dequant(v[j + 1], ab, w.y, bb.y),
+                            dequant(v[j + 2], ab, w.z, bb.z), dequant(v[j + 3], ab, w.w, bb.w));
         }
+        __syncwarp();
+        // lane -> (row i*4 + lane/8, columns 4*(lane%8) .. +3): 4 rows x 128 B per instruction
+        const uint32_t cq = (lane & 7u) * 4;
+        float4 xv[8];
+#pragma unroll
+        for (uint32_t i = 0; i < 8; ++i) {
+            const uint32_t rr = i * 4 + (lane >> 3);
+            if (ctx.row0 + rr < ctx.m_eff)
+                xv[i] = *reinterpret_cast<const float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq);
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < 8; ++i) {
+            const uint32_t rr = i * 4 + (lane >> 3);
+            if (ctx.row0 + rr < ctx.m_eff) {
+                const float4 y = *reinterpret_cast<const float4*>(ctx.stage + swz128(rr, lane & 7u));
+                float4 o = xv[i];
+                o.x += y.x;
+                o.y += y.y;
+                o.z += y.z;
+                o.w += y.w;
+                *reinterpret_cast<float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq) = o;
+            }
+        }
+        __syncwarp();
     }
-    static DH_DEVINL void tile_end(const Params&, TileState&, uint32_t, bool) {}
+    static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
 
 DH_DEVINL float gelu_tanh(float x) {
@@ -154,38 +230,56 @@ DH_DEVINL float gelu_tanh(float x) {
     return 0.5f * x * (1.0f + t);
 }
 
-// out[row, col] = bf16(gelu_tanh(acc * (a_scale * w_scale) + bias))  (MLP up).
+// out[row, col] = bf16(gelu_tanh(acc * (a_scale * w_scale) + bias) * out_scale)
+// (MLP up), stored as 64-byte row segments, two rows per warp instruction.
 struct EpiGelu : EpiBase {
     static constexpr uint32_t kChunk = 32;
+    static constexpr uint32_t kStagingPerWarp = 32 * 64;
     struct Params {
         const float* a_scale;
         const float* w_scale;
         const float* bias;
+        const float* out_scale;  // per-column factor (SmoothQuant 1/s of the next linear) or null
         __nv_bfloat16* out;
         uint32_t n;
     };
     struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, uint32_t, bool, uint32_t, uint8_t*) {}
-    static DH_DEVINL void chunk(const Params& p, TileState&, uint32_t row, bool ok, uint32_t col0,
+    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
+    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
-        if (!ok) return;
-        const float ab = p.a_scale[row];
-        __nv_bfloat16* dst = p.out + static_cast<uint64_t>(row) * p.n + col0;
+        const float ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        const uint32_t lane = ctx.lane;
+        uint32_t pk[16];
+        const float4* w4 = reinterpret_cast<const float4*>(p.w_scale + col0);
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+        const float4* o4 = reinterpret_cast<const float4*>(p.out_scale + col0);
 #pragma unroll
-        for (uint32_t j = 0; j < 32; j += 8) {
-            uint4 pk;
-            __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-            for (uint32_t e = 0; e < 4; ++e) {
-                const uint32_t c = j + 2 * e;
-                const float a0 = gelu_tanh(dequant(v[c], ab, __ldg(p.w_scale + col0 + c), __ldg(p.bias + col0 + c)));
-                const float a1 = gelu_tanh(dequant(v[c + 1], ab, __ldg(p.w_scale + col0 + c + 1), __ldg(p.bias + col0 + c + 1)));
-                hp[e] = __floats2bfloat162_rn(a0, a1);
-            }
-            *reinterpret_cast<uint4*>(dst + j) = pk;
+        for (uint32_t q = 0; q < 8; ++q) {
+            const float4 w = __ldg(w4 + q), bb = __ldg(b4 + q);
+            const float4 os = p.out_scale ? __ldg(o4 + q) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float a0 = gelu_tanh(dequant(v[4 * q], ab, w.x, bb.x)) * os.x;
+            const float a1 = gelu_tanh(dequant(v[4 * q + 1], ab, w.y, bb.y)) * os.y;
+            const float a2 = gelu_tanh(dequant(v[4 * q + 2], ab, w.z, bb.z)) * os.z;
+            const float a3 = gelu_tanh(dequant(v[4 * q + 3], ab, w.w, bb.w)) * os.w;
+            pk[2 * q] = pack_bf16x2(a0, a1);
+            pk[2 * q + 1] = pack_bf16x2(a2, a3);
         }
+#pragma unroll
+        for (uint32_t w = 0; w < 16; w += 4)
+            *reinterpret_cast<uint4*>(ctx.stage + swz64(lane, w / 4)) = make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
+        __syncwarp();
+        // lane -> (row i*8 + lane/4, 16-byte piece lane%4): 8 rows x 64 B per instruction
+#pragma unroll
+        for (uint32_t i = 0; i < 4; ++i) {
+            const uint32_t rr = i * 8 + (lane >> 2);
+            const uint32_t r = ctx.row0 + rr;
+            if (r < ctx.m_eff)
+                *reinterpret_cast<uint4*>(p.out + static_cast<uint64_t>(r) * p.n + col0 + (lane & 3u) * 8) =
+                    *reinterpret_cast<const uint4*>(ctx.stage + swz64(rr, lane & 3u));
+        }
+        __syncwarp();
     }
-    static DH_DEVINL void tile_end(const Params&, TileState&, uint32_t, bool) {}
+    static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
 
 }  // namespace
@@ -230,7 +324,7 @@ extern "C" uint32_t dh_gemm_i8_s32(const int8_t* a, uint64_t lda, const int8_t* 
 
 extern "C" uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, const int8_t* w,
                                      const float* w_scale, const float* bias, const float* rope_cos,
-                                     const float* rope_sin, uint32_t m, uint32_t seq_len,
+                                     const float* rope_sin, const float* v_scale, uint32_t m, uint32_t seq_len,
                                      uint32_t pos_offset, uint32_t kv_stride, uint32_t kv_offset,
                                      void* q, void* k, void* vt, const uint32_t* run_rows,
                                      void* stream) {
@@ -238,11 +332,17 @@ extern "C" uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, cons
         return DH_ERR_NULL_POINTER;
     if (seq_len == 0 || m % seq_len != 0 || kv_offset + seq_len > kv_stride)
         return DH_ERR_INVALID_ARGUMENT;
-    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15u) return DH_ERR_ALIGNMENT;
+    // a warp's 32 rows must lie in one sequence, and V^T pairs are 4-byte stores
+    if (seq_len % 32 != 0) return DH_ERR_UNSUPPORTED_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+         reinterpret_cast<uintptr_t>(w_scale) | reinterpret_cast<uintptr_t>(bias) |
+         reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin) |
+         reinterpret_cast<uintptr_t>(v_scale)) & 15u)
+        return DH_ERR_ALIGNMENT;
     CUtensorMap ta, tb;
     uint32_t st = make_i8_operand_maps(&ta, &tb, a, 768, w, 768, m, 2304, 768, 256);
     if (st != DH_OK) return st;
-    EpiQKV::Params p{a_scale, w_scale, bias, rope_cos, rope_sin, seq_len, pos_offset, kv_stride,
+    EpiQKV::Params p{a_scale, w_scale, bias, rope_cos, rope_sin, v_scale, seq_len, pos_offset, kv_stride,
                      kv_offset, static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k),
                      static_cast<__nv_bfloat16*>(vt)};
     GemmShape shape{m, 2304, 768, run_rows};
@@ -275,15 +375,18 @@ extern "C" uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, cons
 }
 
 extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
-                                 const float* w_scale, const float* bias, void* out, uint32_t m,
+                                 const float* w_scale, const float* bias, const float* out_scale,
+                                 void* out, uint32_t m,
                                  uint32_t n, uint32_t k, const uint32_t* run_rows, void* stream) {
     if (!a_scale || !w_scale || !bias || !out) return DH_ERR_NULL_POINTER;
     if (n % 256 != 0) return DH_ERR_UNSUPPORTED_SHAPE;
-    if (reinterpret_cast<uintptr_t>(out) & 15u) return DH_ERR_ALIGNMENT;
+    if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(w_scale) |
+         reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(out_scale)) & 15u)
+        return DH_ERR_ALIGNMENT;
     CUtensorMap ta, tb;
     uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, 256);
     if (st != DH_OK) return st;
-    EpiGelu::Params p{a_scale, w_scale, bias, static_cast<__nv_bfloat16*>(out), n};
+    EpiGelu::Params p{a_scale, w_scale, bias, out_scale, static_cast<__nv_bfloat16*>(out), n};
     GemmShape shape{m, n, k, run_rows};
     const uint32_t tiles = ((m + 127) / 128) * (n / 256);
     if (launch_gemm_i8<256, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=

@@ -27,9 +27,23 @@ namespace dh {
 // Default hooks for epilogue policies: extra shared memory (bytes, placed
 // after the pipeline stages) initialised once per CTA by all threads.
 struct EpiBase {
-    static constexpr uint32_t kExtraSmem = 0;
+    static constexpr uint32_t kExtraSmem = 0;      // shared by the CTA
+    static constexpr uint32_t kStagingPerWarp = 0;  // private to each epilogue warp
     template <class P>
     static DH_DEVINL void init_smem(const P&, uint8_t*) {}
+};
+
+// What an epilogue thread knows about its place in the tile.  All 32 lanes of
+// an epilogue warp call chunk() together (rows past m_eff included), so a
+// policy may use warp-cooperative stores through its staging buffer.
+struct EpiCtx {
+    uint32_t row;      // this thread's output row
+    bool row_ok;       // row < m_eff
+    uint32_t row0;     // first row of this warp (32 consecutive rows)
+    uint32_t m_eff;    // number of valid rows
+    uint32_t lane;
+    uint8_t* stage;    // kStagingPerWarp bytes private to this warp
+    uint8_t* extra;    // kExtraSmem bytes shared by the CTA
 };
 
 struct GemmShape {
@@ -48,10 +62,14 @@ struct GemmCfg {
     static constexpr uint32_t EPI_WARPS = 8;
     static constexpr uint32_t EPI_THREADS = 32 * EPI_WARPS;
     static constexpr uint32_t THREADS = 64 + EPI_THREADS;
-    static constexpr uint32_t BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
+    // barriers + TMEM address, rounded so the epilogue buffers after it stay
+    // 128-byte aligned
+    static constexpr uint32_t BAR_BYTES = ((8 * (2 * STAGES + 5) + 16) + 127) / 128 * 128;
     static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
     template <class Epi>
-    static constexpr uint32_t smem_bytes() { return SMEM_BYTES + Epi::kExtraSmem; }
+    static constexpr uint32_t smem_bytes() {
+        return SMEM_BYTES + Epi::kExtraSmem + EPI_WARPS * Epi::kStagingPerWarp;
+    }
     static constexpr uint32_t IDESC = tc::idesc_i8_s32<BM, BN>();
 };
 
@@ -59,7 +77,7 @@ template <uint32_t BN, class Epi>
 __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
 gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_b, GemmShape shape,
-                  const typename Epi::Params ep) {
+                  const __grid_constant__ typename Epi::Params ep) {
     using Cfg = GemmCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -194,8 +212,11 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             tc::tc_fence_after();
             const uint32_t row = m0 + row_in_tile;
             const bool row_ok = row < m_eff;
+            const EpiCtx ctx{row, row_ok, m0 + quad * 32, m_eff, lane,
+                             extra_smem + Epi::kExtraSmem + (warp - 2) * Epi::kStagingPerWarp,
+                             extra_smem};
             typename Epi::TileState st;
-            Epi::tile_begin(ep, st, row, row_ok, n0 + half * kHalf, extra_smem);
+            Epi::tile_begin(ep, st, ctx, n0 + half * kHalf);
 #pragma unroll 1
             for (uint32_t c = 0; c < kHalf; c += kChunk) {
                 const uint32_t col_in_tile = half * kHalf + c;
@@ -207,9 +228,9 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     tc::tmem_ld_32x32b_x32(taddr + 32 * j,
                                            *reinterpret_cast<uint32_t(*)[32]>(&v[32 * j]));
                 tc::tmem_ld_wait();
-                Epi::chunk(ep, st, row, row_ok, n0 + col_in_tile, &v[0]);
+                Epi::chunk(ep, st, ctx, n0 + col_in_tile, &v[0]);
             }
-            Epi::tile_end(ep, st, row, row_ok);
+            Epi::tile_end(ep, st, ctx);
             tc::tc_fence_before();
             tc::mbar_arrive(&acce_bar[acc]);
             if (++acc == 2) {

@@ -93,19 +93,20 @@ struct EpiHead : EpiBase {
     static DH_DEVINL void init_smem(const Params&, uint8_t* extra) {
         load_gumbel_table(reinterpret_cast<int16_t*>(extra));
     }
-    static DH_DEVINL void tile_begin(const Params& p, TileState& st, uint32_t row, bool ok,
-                                     uint32_t, uint8_t* extra) {
+    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t) {
+        const uint32_t row = ctx.row;
         st.best = 0ull;
-        st.table = reinterpret_cast<const int16_t*>(extra);
-        if (!ok) return;
+        st.table = reinterpret_cast<const int16_t*>(ctx.extra);
+        if (!ctx.row_ok) return;
         st.a_scale = p.a_scale ? p.a_scale[row] : 0.f;
         st.pos = p.row_position ? p.row_position[row] : row;
         st.key_hi = p.row_key_hi ? p.row_key_hi[row] : p.const_key_hi;
         st.ev = p.row_eval ? p.row_eval[row] : p.const_eval;
     }
-    static DH_DEVINL void chunk(const Params& p, TileState& st, uint32_t row, bool ok,
-                                uint32_t col0, const uint32_t* v) {
-        if (!ok || col0 >= p.vocab) return;
+    static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
+                                const uint32_t* v) {
+        const uint32_t row = ctx.row;
+        if (!ctx.row_ok || col0 >= p.vocab) return;
         unsigned long long best = st.best;
         if (p.mode == kDequantGreedy) {
 #pragma unroll
@@ -120,12 +121,35 @@ struct EpiHead : EpiBase {
             st.best = best;
             return;
         }
+        const bool full_chunk = col0 + 32 <= p.vocab && (p.vocab & 3u) == 0;
 #pragma unroll
         for (uint32_t g = 0; g < 32; g += 4) {
             const uint32_t t0 = col0 + g;
             if (t0 >= p.vocab) break;
             Philox4 w{0, 0, 0, 0};
             if (!p.noise) w = philox4x32_10(t0 >> 2, st.pos, st.ev, p.stream_id, p.key_lo, st.key_hi);
+            float ws[4] = {0.f, 0.f, 0.f, 0.f}, bs[4] = {0.f, 0.f, 0.f, 0.f};
+            int32_t ms[4] = {0, 0, 0, 0}, bq[4] = {0, 0, 0, 0};
+            if (p.mode == kRequantQ20) {
+#pragma unroll
+                for (uint32_t i = 0; i < 4; ++i)
+                    if (t0 + i < p.vocab) {
+                        ms[i] = __ldg(p.mult_q20 + t0 + i);
+                        bq[i] = __ldg(p.bias_q10 + t0 + i);
+                    }
+            } else if (full_chunk) {
+                const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.w_scale + t0));
+                const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + t0));
+                ws[0] = w4.x; ws[1] = w4.y; ws[2] = w4.z; ws[3] = w4.w;
+                bs[0] = b4.x; bs[1] = b4.y; bs[2] = b4.z; bs[3] = b4.w;
+            } else {
+#pragma unroll
+                for (uint32_t i = 0; i < 4; ++i)
+                    if (t0 + i < p.vocab) {
+                        ws[i] = __ldg(p.w_scale + t0 + i);
+                        bs[i] = __ldg(p.bias + t0 + i);
+                    }
+            }
 #pragma unroll
             for (uint32_t i = 0; i < 4; ++i) {
                 const uint32_t t = t0 + i;
@@ -135,19 +159,17 @@ struct EpiHead : EpiBase {
                                               : gumbel_q10(philox_lane(w, i), st.table);
                 int64_t s;
                 if (p.mode == kRequantQ20)
-                    s = static_cast<int64_t>(requant_q20(acc, __ldg(p.mult_q20 + t))) +
-                        __ldg(p.bias_q10 + t) + noise;
+                    s = static_cast<int64_t>(requant_q20(acc, ms[i])) + bq[i] + noise;
                 else
-                    s = static_cast<int64_t>(q10(ref_logit(acc, st.a_scale, __ldg(p.w_scale + t),
-                                                           __ldg(p.bias + t)))) + noise;
+                    s = static_cast<int64_t>(q10(ref_logit(acc, st.a_scale, ws[i], bs[i]))) + noise;
                 const unsigned long long pk = pack_score_id(sat_i32(s), t);
                 best = pk > best ? pk : best;
             }
         }
         st.best = best;
     }
-    static DH_DEVINL void tile_end(const Params& p, TileState& st, uint32_t row, bool ok) {
-        if (ok && st.best) atomicMax(p.packed + row, st.best);
+    static DH_DEVINL void tile_end(const Params& p, TileState& st, const EpiCtx& ctx) {
+        if (ctx.row_ok && st.best) atomicMax(p.packed + ctx.row, st.best);
     }
 };
 
@@ -217,6 +239,8 @@ uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_
     if (!packed) return DH_ERR_NULL_POINTER;
     if (mode == kRequantQ20 && (!mult_q20 || !bias_q10)) return DH_ERR_NULL_POINTER;
     if (mode != kRequantQ20 && (!a_scale || !w_scale || !bias)) return DH_ERR_NULL_POINTER;
+    if ((reinterpret_cast<uintptr_t>(w_scale) | reinterpret_cast<uintptr_t>(bias)) & 15u)
+        return DH_ERR_ALIGNMENT;
     HeadParams hp{mode, vocabulary_size, mask_token_id, a_scale, w_scale, bias, mult_q20, bias_q10,
                   noise, row_position, row_key_hi, row_eval, const_eval, 0u, key_lo, stream_id,
                   reinterpret_cast<unsigned long long*>(packed)};

@@ -90,7 +90,11 @@ ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ inv_smoot
     if (lane_id() == 0) scale[i] = sc;
 }
 
-// bf16 rows of C = 768 or 3072 columns -> SmoothQuant -> int8 + row scale.
+// bf16 rows of C = 768 or 3072 columns -> per-token int8 + row scale.  The
+// SmoothQuant division is already applied by the producer (the attention
+// output inherits it from V, the GELU output from the MLP-up epilogue), or
+// here when inv_smooth is given.  The row amax is taken in packed bf16x2
+// (exact), the quantisation in fp32.
 template <uint32_t C>
 __global__ void __launch_bounds__(kRowWarps * 32)
 quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __restrict__ inv_smooth,
@@ -102,35 +106,49 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
     constexpr uint32_t kVec = C / 256;  // 8-element (16-byte) vectors per lane
     const uint4* src = reinterpret_cast<const uint4*>(in + static_cast<uint64_t>(r) * C);
     uint4 raw[kVec];
-    float amax = 0.f;
 #pragma unroll
-    for (uint32_t j = 0; j < kVec; ++j) {
-        raw[j] = src[lane_id() + 32 * j];
-        const uint32_t c0 = (lane_id() + 32 * j) * 8;
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
+    for (uint32_t j = 0; j < kVec; ++j) raw[j] = __ldcs(src + lane_id() + 32 * j);
+    if (inv_smooth) {
+        const float4* is = reinterpret_cast<const float4*>(inv_smooth);
 #pragma unroll
-        for (uint32_t e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            amax = fmaxf(amax, fmaxf(fabsf(f.x * __ldg(inv_smooth + c0 + 2 * e)),
-                                     fabsf(f.y * __ldg(inv_smooth + c0 + 2 * e + 1))));
+        for (uint32_t j = 0; j < kVec; ++j) {
+            const uint32_t c4 = (lane_id() + 32 * j) * 2;
+            const float4 s0 = __ldg(is + c4), s1 = __ldg(is + c4 + 1);
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw[j]);
+            const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (uint32_t e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(h[e]);
+                h[e] = __floats2bfloat162_rn(f.x * sc[2 * e], f.y * sc[2 * e + 1]);
+            }
         }
     }
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.f);
+#pragma unroll
+    for (uint32_t j = 0; j < kVec; ++j) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
+    }
+    float amax = fmaxf(__low2float(m2), __high2float(m2));
     amax = warp_max_f32(amax);
     const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
     const float inv = 1.0f / sc;
     uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * C);
 #pragma unroll
     for (uint32_t j = 0; j < kVec; ++j) {
-        const uint32_t c0 = (lane_id() + 32 * j) * 8;
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
-        int8_t q[8];
+        uint32_t packed[2];
 #pragma unroll
         for (uint32_t e = 0; e < 4; ++e) {
             const float2 f = __bfloat1622float2(h[e]);
-            q[2 * e] = quant_i8(f.x * __ldg(inv_smooth + c0 + 2 * e), inv);
-            q[2 * e + 1] = quant_i8(f.y * __ldg(inv_smooth + c0 + 2 * e + 1), inv);
+            const int32_t q0 = __float2int_rn(fminf(fmaxf(f.x * inv, -127.f), 127.f));
+            const int32_t q1 = __float2int_rn(fminf(fmaxf(f.y * inv, -127.f), 127.f));
+            const uint32_t b2 = (static_cast<uint32_t>(q0) & 0xFFu) | ((static_cast<uint32_t>(q1) & 0xFFu) << 8);
+            if (e & 1u) packed[e >> 1] |= b2 << 16;
+            else packed[e >> 1] = b2;
         }
-        dst[lane_id() + 32 * j] = *reinterpret_cast<const uint2*>(q);
+        dst[lane_id() + 32 * j] = make_uint2(packed[0], packed[1]);
     }
     if (lane_id() == 0) scale[r] = sc;
 }
@@ -172,7 +190,7 @@ uint32_t dh_ln_smooth_quant(const float* x, const float* inv_smooth, int8_t* out
 
 uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream) {
-    if (!in || !inv_smooth || !out || !scale) return DH_ERR_NULL_POINTER;
+    if (!in || !out || !scale) return DH_ERR_NULL_POINTER;
     if (rows == 0) return DH_OK;
     if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u)
         return DH_ERR_ALIGNMENT;

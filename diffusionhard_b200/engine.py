@@ -146,19 +146,19 @@ class MDLMEngine:
         call("dh_ln_smooth_quant", p(self.x), p(qkv.inv_smooth), p(self.act_q), p(self.act_scale), M,
              None, None, rr, s)
         call("dh_gemm_qkv_rope", p(self.act_q), p(self.act_scale), p(qkv.w), p(qkv.w_scale), p(qkv.bias),
-             p(self.rope_cos), p(self.rope_sin), M, L, self.pos_offset, self.kv_stride, self.kv_offset,
+             p(self.rope_cos), p(self.rope_sin), p(out.inv_smooth), M, L, self.pos_offset, self.kv_stride, self.kv_offset,
              p(self.q), p(k), p(vt), rr, s)
         call("dh_attention", p(self.q), p(k), p(vt), p(self.attn), self.B, L, self.kv_len, self.kv_stride,
              rr, s)
-        call("dh_quant_rows_bf16", p(self.attn), p(out.inv_smooth), p(self.act_q), p(self.act_scale), M,
+        call("dh_quant_rows_bf16", p(self.attn), None, p(self.act_q), p(self.act_scale), M,
              768, rr, s)
         call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(out.w), p(out.w_scale), p(out.bias),
              p(self.x), M, 768, 768, rr, s)
         call("dh_ln_smooth_quant", p(self.x), p(up.inv_smooth), p(self.act_q), p(self.act_scale), M,
              None, None, rr, s)
         call("dh_gemm_gelu", p(self.act_q), p(self.act_scale), p(up.w), p(up.w_scale), p(up.bias),
-             p(self.mlp), M, 3072, 768, rr, s)
-        call("dh_quant_rows_bf16", p(self.mlp), p(down.inv_smooth), p(self.act_q), p(self.act_scale), M,
+             p(down.inv_smooth), p(self.mlp), M, 3072, 768, rr, s)
+        call("dh_quant_rows_bf16", p(self.mlp), None, p(self.act_q), p(self.act_scale), M,
              3072, rr, s)
         call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(down.w), p(down.w_scale),
              p(down.bias), p(self.x), M, 768, 3072, rr, s)
@@ -186,26 +186,42 @@ class MDLMEngine:
 
     # ------------------------------------------------------------- loop
 
-    def _enqueue_generation(self, steps: int, seed: int, thresholds: List[int]) -> None:
+    def enqueue_transition(self, k: int, steps: int, seed: int, threshold_q32: int) -> None:
+        """Transition k of `steps` (k == steps: the final greedy pass)."""
         s = _lib.stream_handle()
         B, L = self.B, self.L
         p = self._p
         call = _lib.call
+        final = 1 if k == steps else 0
+        kk = min(k, steps - 1)
+        call("dh_loop_plan", B, L, kk, steps, final, p(self.active), p(self.need_eval), p(self.eval_id),
+             p(self.fwd_rows), p(self.sel_count), p(self.counters), s)
+        self.forward(run_rows=self.fwd_rows)
+        call("dh_loop_select", B, L, kk, seed, self.seq_offset, 0 if final else threshold_q32, final,
+             p(self.active), p(self.eval_id), p(self.sel_rows), p(self.sel_pos), p(self.sel_key),
+             p(self.sel_eval), p(self.sel_count), s)
+        self.final_hidden_q(self.sel_rows, self.sel_count)
+        self.head_argmax(self.M, 2 if final else 1, rows_count=self.sel_count, row_position=self.sel_pos,
+                         row_key_hi=self.sel_key, row_eval=self.sel_eval, key_lo=seed)
+        call("dh_loop_commit", B, L, kk, steps, final, p(self.packed), p(self.sel_rows), p(self.sel_count),
+             p(self.tokens), p(self.active), p(self.need_eval), p(self.counters), s)
+
+    def _enqueue_generation(self, steps: int, seed: int, thresholds: List[int]) -> None:
         for k in range(steps + 1):
-            final = 1 if k == steps else 0
-            call("dh_loop_plan", B, L, min(k, steps - 1), steps, final, p(self.active), p(self.need_eval),
-                 p(self.eval_id), p(self.fwd_rows), p(self.sel_count), p(self.counters), s)
-            self.forward(run_rows=self.fwd_rows)
-            thr = 0 if final else thresholds[k]
-            call("dh_loop_select", B, L, min(k, steps - 1), seed, self.seq_offset, thr, final, p(self.active),
-                 p(self.eval_id), p(self.sel_rows), p(self.sel_pos), p(self.sel_key), p(self.sel_eval),
-                 p(self.sel_count), s)
-            self.final_hidden_q(self.sel_rows, self.sel_count)
-            self.head_argmax(self.M, 2 if final else 1, rows_count=self.sel_count,
-                             row_position=self.sel_pos, row_key_hi=self.sel_key, row_eval=self.sel_eval,
-                             key_lo=seed)
-            call("dh_loop_commit", B, L, min(k, steps - 1), steps, final, p(self.packed), p(self.sel_rows),
-                 p(self.sel_count), p(self.tokens), p(self.active), p(self.need_eval), p(self.counters), s)
+            self.enqueue_transition(k, steps, seed, thresholds[k] if k < steps else 0)
+
+    def init_loop(self, input_ids: Any, steps: int) -> None:
+        """Load ids [B, L] (device) and reset the loop state."""
+        torch = self.torch
+        if self.counters is None or self.counters.numel() != 3 * steps:
+            self.counters = torch.zeros(3 * steps, dtype=torch.int32, device=self.device)
+        ids = input_ids.to(device=self.device, dtype=torch.int32).contiguous().view(-1)
+        if ids.numel() != self.M:
+            raise ValueError("input_ids must be [batch, seq_len]")
+        self._ids_in = ids
+        _lib.call("dh_loop_init", _lib.ptr(ids), self.B, self.L, self.cfg.mask_token_id, steps,
+                  _lib.ptr(self.tokens), _lib.ptr(self.active), _lib.ptr(self.need_eval),
+                  _lib.ptr(self.eval_id), _lib.ptr(self.counters), _lib.stream_handle())
 
     def launches_per_generation(self, steps: int) -> int:
         per_transition = 1 + self.launches_per_forward + 1 + 1 + 2 + 1
@@ -216,26 +232,15 @@ class MDLMEngine:
         """Candidate-cache generation of B sequences (device input_ids int
         [B, L]).  Returns (device int32 ids [B, L], metadata)."""
         torch = self.torch
-        if self.counters is None or self.counters.numel() != 3 * steps:
-            self.counters = torch.zeros(3 * steps, dtype=torch.int32, device=self.device)
-        ids = input_ids.to(device=self.device, dtype=torch.int32).contiguous().view(-1)
-        if ids.numel() != self.M:
-            raise ValueError("input_ids must be [batch, seq_len]")
-        self._ids_in = ids
         thresholds = reveal_thresholds_q32(steps, sampling_epsilon)
-        s = _lib.stream_handle()
-        _lib.call("dh_loop_init", _lib.ptr(ids), self.B, self.L, self.cfg.mask_token_id, steps,
-                  _lib.ptr(self.tokens), _lib.ptr(self.active), _lib.ptr(self.need_eval),
-                  _lib.ptr(self.eval_id), _lib.ptr(self.counters), s)
+        self.init_loop(input_ids, steps)
         if graph:
             key = (steps, seed, sampling_epsilon, self.seq_offset)
             g = self._graphs.get(key)
             if g is None:
                 # warm-up outside capture (function attributes, tensor maps)
                 self._enqueue_generation(steps, seed, thresholds)
-                _lib.call("dh_loop_init", _lib.ptr(ids), self.B, self.L, self.cfg.mask_token_id, steps,
-                          _lib.ptr(self.tokens), _lib.ptr(self.active), _lib.ptr(self.need_eval),
-                          _lib.ptr(self.eval_id), _lib.ptr(self.counters), s)
+                self.init_loop(input_ids, steps)
                 torch.cuda.synchronize()
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):

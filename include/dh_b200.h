@@ -206,7 +206,9 @@ uint32_t dh_ln_smooth_quant(const float* x, const float* inv_smooth, int8_t* out
                             uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
                             const uint32_t* run_flag, void* stream);
 
-/* bf16 rows (cols = 768 or 3072) -> SmoothQuant -> per-token int8 (K3'). */
+/* bf16 rows (cols = 768 or 3072) -> per-token int8 (K3').  inv_smooth may be
+ * NULL when the producer already applied the SmoothQuant 1/s (see v_scale /
+ * out_scale below). */
 uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream);
 
@@ -215,10 +217,13 @@ uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out
  * written as bf16 Q [B, 12, seq_len, 64], K [B, 12, kv_stride, 64] and V^T
  * [B, 12, 64, kv_stride] at key offset kv_offset -- the layout of a cached
  * prefix followed by the active rows (prefix_drift.py:155-238).
- * rope_cos / rope_sin: [positions, 32] fp32. */
+ * rope_cos / rope_sin: [positions, 32] fp32.  v_scale (768, may be NULL)
+ * multiplies V per channel: with the SmoothQuant 1/s of the attention-out
+ * linear, softmax(QK^T)(V diag(1/s)) = (softmax(QK^T) V) diag(1/s) arrives
+ * pre-smoothed. */
 uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, const int8_t* w,
                           const float* w_scale, const float* bias, const float* rope_cos,
-                          const float* rope_sin, uint32_t m, uint32_t seq_len, uint32_t pos_offset,
+                          const float* rope_sin, const float* v_scale, uint32_t m, uint32_t seq_len, uint32_t pos_offset,
                           uint32_t kv_stride, uint32_t kv_offset, void* q, void* k, void* vt,
                           const uint32_t* run_rows, void* stream);
 
@@ -228,9 +233,11 @@ uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, const int8_t* w
                           const float* w_scale, const float* bias, float* x, uint32_t m, uint32_t n,
                           uint32_t k, const uint32_t* run_rows, void* stream);
 
-/* out[m, n] = bf16(gelu_tanh(dequant(A . W^T) + bias)): MLP-up (K7). */
+/* out[m, n] = bf16(gelu_tanh(dequant(A . W^T) + bias) * out_scale[n]): MLP-up
+ * (K7); out_scale (may be NULL) is the SmoothQuant 1/s of MLP-down. */
 uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
-                      const float* w_scale, const float* bias, void* out, uint32_t m, uint32_t n,
+                      const float* w_scale, const float* bias, const float* out_scale, void* out,
+                      uint32_t m, uint32_t n,
                       uint32_t k, const uint32_t* run_rows, void* stream);
 
 /* Bidirectional attention softmax(Q K^T / 8) V (K5) over the first kv_len
