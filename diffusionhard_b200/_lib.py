@@ -26,6 +26,7 @@ STATUS_NAMES = {
     103: "DH_ERR_UNSUPPORTED_SHAPE",
     104: "DH_ERR_CUDA",
     105: "DH_ERR_INVALID_ARGUMENT",
+    106: "DH_ERR_SCRATCH_LIMIT",
 }
 
 

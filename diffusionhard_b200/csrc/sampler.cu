@@ -14,6 +14,7 @@
 #include "dh_philox.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace dh {
 namespace {
@@ -371,6 +372,40 @@ uint32_t launch_argmax(const ArgmaxRows& a, bool noisy, uint32_t mode, int32_t* 
     return DH_OK;
 }
 
+// ------------------------------------------------ no-allocation variant of K1
+//
+// Scratch of dh_noisy_argmax_f32_noalloc: the per-(row, vocab chunk) partial
+// maxima live in this file-scope array instead of a caller workspace.  Every
+// GPU that loads the library holds these 512 KiB until the process exits.
+// Host code must not use the array's name as a device address: the address is
+// resolved once per device with cudaGetSymbolAddress.
+constexpr uint32_t kNoAllocScratchWords = 1u << 16;  // 65,536 x 8 bytes = 512 KiB
+static __device__ __align__(256) uint64_t g_noalloc_argmax_scratch[kNoAllocScratchWords];
+
+constexpr int kMaxDevices = 64;
+
+// Device address of the scratch array for the current device (set-up on the
+// first call per device; nullptr and *status set on failure).
+uint64_t* noalloc_scratch(uint32_t* status) {
+    static std::mutex mu;
+    static uint64_t* addr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        *status = DH_ERR_CUDA;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_argmax_scratch) != cudaSuccess || !p) {
+            *status = DH_ERR_CUDA;
+            return nullptr;
+        }
+        addr[dev] = static_cast<uint64_t*>(p);
+    }
+    return addr[dev];
+}
+
 }  // namespace
 }  // namespace dh
 
@@ -452,6 +487,33 @@ uint32_t dh_noisy_argmax_f32(const float* logits, uint64_t row_stride, uint32_t 
     ArgmaxRows a{logits, row_stride, rows, vocabulary_size, mask_token_id, row_position,
                  row_key_hi, row_eval, key_lo, stream_id, 0u, 0u, nullptr, nullptr};
     return launch_argmax(a, true, kFinalizeIds, out_ids, out_scores, nullptr, workspace,
+                         static_cast<cudaStream_t>(stream));
+}
+
+// Same computation as dh_noisy_argmax_f32 without a caller workspace: for
+// callers that cannot allocate device memory (see the header).  Calls that run
+// at the same time on one GPU share the scratch array and race; serialise
+// them (one stream, or events).  Nothing in the array needs to start at zero:
+// each call writes every partial slot it later reads.
+uint32_t dh_noisy_argmax_f32_noalloc(const float* logits, uint64_t row_stride, uint32_t rows,
+                                     uint32_t vocabulary_size, uint32_t mask_token_id,
+                                     const uint32_t* row_position, const uint32_t* row_key_hi,
+                                     const uint32_t* row_eval, uint32_t key_lo, uint32_t stream_id,
+                                     int32_t* out_ids, int32_t* out_scores, void* stream) {
+    if (rows == 0 || rows > 65535u * 16u) return DH_RNG_INVALID_POSITION_COUNT;
+    if (vocabulary_size == 0 || vocabulary_size > 65535 || mask_token_id >= vocabulary_size)
+        return DH_RNG_INVALID_VOCABULARY_SIZE;
+    if (!logits || !out_ids) return DH_ERR_NULL_POINTER;
+    if (row_stride < vocabulary_size) return DH_ERR_INVALID_ARGUMENT;
+    if (rows > 65535u) return DH_ERR_UNSUPPORTED_SHAPE;
+    if (static_cast<uint64_t>(rows) * argmax_chunks(vocabulary_size) > kNoAllocScratchWords)
+        return DH_ERR_SCRATCH_LIMIT;
+    uint32_t status = DH_OK;
+    uint64_t* scratch = noalloc_scratch(&status);
+    if (!scratch) return status;
+    ArgmaxRows a{logits, row_stride, rows, vocabulary_size, mask_token_id, row_position,
+                 row_key_hi, row_eval, key_lo, stream_id, 0u, 0u, nullptr, nullptr};
+    return launch_argmax(a, true, kFinalizeIds, out_ids, out_scores, nullptr, scratch,
                          static_cast<cudaStream_t>(stream));
 }
 

@@ -44,6 +44,7 @@ extern "C" {
 #define DH_ERR_UNSUPPORTED_SHAPE 103u
 #define DH_ERR_CUDA 104u
 #define DH_ERR_INVALID_ARGUMENT 105u
+#define DH_ERR_SCRATCH_LIMIT 106u
 
 /* RNG family -- same values as RngKernelStatus (philox_rng.hpp:29-33). */
 #define DH_RNG_INVALID_POSITION_COUNT 1u
@@ -108,6 +109,24 @@ uint32_t dh_noisy_argmax_f32(const float* logits, uint64_t row_stride, uint32_t 
                              const uint32_t* row_eval, uint32_t key_lo, uint32_t stream_id,
                              int32_t* out_ids, int32_t* out_scores, void* workspace,
                              size_t workspace_bytes, void* stream);
+
+/* dh_noisy_argmax_f32 for callers that cannot allocate device memory, such
+ * as a plugin running inside a host framework that owns every device
+ * allocation, or code that must not call cudaMalloc (which may synchronise
+ * the device) once serving has started.  No counterpart in the reference.
+ * Same arguments, results and status codes, minus the workspace: the
+ * scratch is a 512 KiB array inside the library (held by every GPU that loads
+ * it until the process exits).  rows * ceil(vocabulary_size / 4096) must not
+ * exceed 65,536 (e.g. 5,041 rows of the 50,258-token vocabulary), else
+ * DH_ERR_SCRATCH_LIMIT.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  Calls share the array: calls that overlap on one GPU race
+ * and must be serialised by the caller.  Allocates nothing. */
+uint32_t dh_noisy_argmax_f32_noalloc(const float* logits, uint64_t row_stride, uint32_t rows,
+                                     uint32_t vocabulary_size, uint32_t mask_token_id,
+                                     const uint32_t* row_position, const uint32_t* row_key_hi,
+                                     const uint32_t* row_eval, uint32_t key_lo, uint32_t stream_id,
+                                     int32_t* out_ids, int32_t* out_scores, void* stream);
 
 /* Greedy argmax of fp32 logits (mask skipped, lowest id on ties): the final
  * pass of the samplers, mdlm.py:1177-1200.  Same workspace as above. */
