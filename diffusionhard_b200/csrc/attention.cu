@@ -16,13 +16,17 @@
 //            writes P_j (bf16) to 128-byte-swizzled shared memory as the A
 //            operand of the PV MMA; O accumulates in TMEM across key tiles and
 //            is rescaled in place only when the row max grows by > 2^8.
-// 80 KB shared memory and 256 TMEM columns per CTA, so two CTAs share an SM
-// and one CTA's softmax overlaps the other's MMAs.  All waits are bounded.
+// K tiles are double-buffered so S_{j+1} can start while tile j's softmax runs
+// (V_{j+1} has that whole softmax to arrive).  96 KB shared memory and 256
+// TMEM columns per CTA: two CTAs share an SM and one CTA's softmax overlaps the
+// other's MMAs.  All waits are bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
 #include "tc_ptx.cuh"
 #include "tmap.h"
+
+#include <algorithm>
 
 namespace dh {
 namespace {
@@ -35,20 +39,24 @@ constexpr uint32_t kQBytes = kTile * kDh * 2;        // 16 KB
 constexpr uint32_t kKBytes = kTile * kDh * 2;        // 16 KB
 constexpr uint32_t kVBytes = kDh * kTile * 2;        // 16 KB (2 sub-tiles of 64 keys)
 constexpr uint32_t kPBytes = kTile * kTile * 2;      // 32 KB (2 sub-tiles of 64 keys)
-constexpr uint32_t kSmemBytes = 1024 + kQBytes + kKBytes + kVBytes + kPBytes + 256;
+constexpr uint32_t kKStages = 2;                      // K ring depth (S_{j+1} needs K_{j+1} early)
+constexpr uint32_t kVStages = 1;                      // V_{j+1} has a whole softmax to arrive
+constexpr uint32_t kSmemBytes = 1024 + kQBytes + kKStages * kKBytes + kVStages * kVBytes + kPBytes + 256;
 constexpr uint32_t kTmemCols = 256;                   // S: [0,128), O: [128,192)
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32<128, 128>();
 constexpr uint32_t kIdescO = tc::idesc_bf16_f32<128, 64>();
 
 struct AttnArgs {
-    uint32_t q_len, kv_len, kv_stride;
+    uint32_t sequences, q_len, kv_len, kv_stride;
     __nv_bfloat16* out;
     const uint32_t* run_flag;
 };
 
+// K / V barriers come in one copy per ring stage: kKFull + stage, etc.
 enum Bar : uint32_t {
-    kQFull = 0, kKFull, kKEmpty, kVFull, kVEmpty, kSFull, kSFree, kPFull, kPEmpty, kOFull, kOFree,
-    kDrain, kNumBars
+    kQFull = 0, kQEmpty, kKFull, kKEmpty = kKFull + kKStages, kVFull = kKEmpty + kKStages,
+    kVEmpty = kVFull + kVStages, kSFull = kVEmpty + kVStages, kSFree, kPFull, kPEmpty, kOFull,
+    kOFree, kDrain, kNumBars
 };
 
 DH_DEVINL void fence_proxy_async_smem() {
@@ -67,6 +75,25 @@ DH_DEVINL uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+
+struct Item {
+    uint32_t seq, head, q_tile, bh;
+};
+
+DH_DEVINL Item item_of(uint32_t w, uint32_t n_qt) {
+    Item it;
+    it.q_tile = w % n_qt;
+    it.bh = w / n_qt;
+    it.head = it.bh % kHeads;
+    it.seq = it.bh / kHeads;
+    return it;
+}
+
+// Persistent kernel: each CTA loops over work items w = (sequence, head,
+// 128-query tile), items of one head adjacent so concurrently running CTAs
+// share K / V in L2.  Every role walks the same (item, key tile) sequence; a
+// global key-tile counter g drives the ring / phase bookkeeping, so the next
+// item's Q and K loads overlap the current item's last tiles.
 __global__ void __launch_bounds__(kThreads, 2)
 attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const AttnArgs args) {
@@ -75,20 +102,20 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     uint8_t* q_s = smem;
-    uint8_t* k_s = q_s + kQBytes;
-    uint8_t* v_s = k_s + kKBytes;
-    uint8_t* p_s = v_s + kVBytes;
+    uint8_t* k_ring = q_s + kQBytes;                    // kKStages x 16 KB
+    uint8_t* v_ring = k_ring + kKStages * kKBytes;      // kVStages x 16 KB
+    uint8_t* p_s = v_ring + kVStages * kVBytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + kPBytes);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
     const uint32_t warp = warp_id(), lane = lane_id();
-    const uint32_t q_tile = blockIdx.x, head = blockIdx.y, seq = blockIdx.z;
-    const uint32_t bh = seq * kHeads + head;
     const uint32_t n_kv = args.kv_len / kTile;
+    const uint32_t n_qt = args.q_len / kTile;
+    const uint32_t total = args.sequences * kHeads * n_qt;
 
     if (warp == 0 && lane == 0) {
         for (uint32_t i = 0; i < kNumBars; ++i) {
-            const bool softmax_side = i == kSFree || i == kPFull;
+            const bool softmax_side = i == kSFree || i == kPFull || i == kOFree;
             tc::mbar_init(&bars[i], softmax_side ? 128u : 1u);
         }
         tc::fence_barrier_init();
@@ -103,62 +130,97 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     const uint32_t tmem = *tmem_holder;
 
     if (warp == 0) {
+        // ------------------------------------------------------------ TMA
         if (tc::elect_one()) {
-            tc::mbar_arrive_expect_tx(&bars[kQFull], kQBytes);
-            tc::tma_load_2d(q_s, &tq, &bars[kQFull], 0,
-                            static_cast<int32_t>(bh * args.q_len + q_tile * kTile));
-            for (uint32_t j = 0; j < n_kv; ++j) {
-                const uint32_t par = (j & 1u) ^ 1u;
-                if (!tc::mbar_wait(&bars[kKEmpty], par, tc::kErrTimeoutEmpty)) break;
-                tc::mbar_arrive_expect_tx(&bars[kKFull], kKBytes);
-                tc::tma_load_2d(k_s, &tk, &bars[kKFull], 0,
-                                static_cast<int32_t>(bh * args.kv_stride + j * kTile));
-                if (!tc::mbar_wait(&bars[kVEmpty], par, tc::kErrTimeoutEmpty)) break;
-                tc::mbar_arrive_expect_tx(&bars[kVFull], kVBytes);
-                tc::tma_load_2d(v_s, &tv, &bars[kVFull], static_cast<int32_t>(j * kTile),
-                                static_cast<int32_t>(bh * kDh));
-                tc::tma_load_2d(v_s + kVBytes / 2, &tv, &bars[kVFull],
-                                static_cast<int32_t>(j * kTile + 64), static_cast<int32_t>(bh * kDh));
+            uint32_t g = 0, it = 0;
+            bool ok = true;
+            for (uint32_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+                const Item item = item_of(w, n_qt);
+                if (!tc::mbar_wait(&bars[kQEmpty], (it & 1u) ^ 1u, tc::kErrTimeoutEmpty)) break;
+                tc::mbar_arrive_expect_tx(&bars[kQFull], kQBytes);
+                tc::tma_load_2d(q_s, &tq, &bars[kQFull], 0,
+                                static_cast<int32_t>(item.bh * args.q_len + item.q_tile * kTile));
+                for (uint32_t j = 0; j < n_kv; ++j, ++g) {
+                    const uint32_t ks = g % kKStages, vs_i = g % kVStages;
+                    if (!tc::mbar_wait(&bars[kKEmpty + ks], ((g / kKStages) & 1u) ^ 1u, tc::kErrTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&bars[kKFull + ks], kKBytes);
+                    tc::tma_load_2d(k_ring + ks * kKBytes, &tk, &bars[kKFull + ks], 0,
+                                    static_cast<int32_t>(item.bh * args.kv_stride + j * kTile));
+                    if (!tc::mbar_wait(&bars[kVEmpty + vs_i], ((g / kVStages) & 1u) ^ 1u, tc::kErrTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&bars[kVFull + vs_i], kVBytes);
+                    uint8_t* vs = v_ring + vs_i * kVBytes;
+                    tc::tma_load_2d(vs, &tv, &bars[kVFull + vs_i], static_cast<int32_t>(j * kTile),
+                                    static_cast<int32_t>(item.bh * kDh));
+                    tc::tma_load_2d(vs + kVBytes / 2, &tv, &bars[kVFull + vs_i],
+                                    static_cast<int32_t>(j * kTile + 64), static_cast<int32_t>(item.bh * kDh));
+                }
             }
-            // Drain the last K / V copies before exit.
-            if (n_kv > 0) {
-                tc::mbar_wait(&bars[kKFull], (n_kv - 1) & 1u, tc::kErrTimeoutFull);
-                tc::mbar_wait(&bars[kVFull], (n_kv - 1) & 1u, tc::kErrTimeoutFull);
-            }
+            // Drain: every copy this CTA issued has landed before it may exit.
+            if (it > 0) tc::mbar_wait(&bars[kQFull], (it - 1) & 1u, tc::kErrTimeoutFull);
+            for (uint32_t x = g > kKStages ? g - kKStages : 0; x < g; ++x)
+                tc::mbar_wait(&bars[kKFull + x % kKStages], (x / kKStages) & 1u, tc::kErrTimeoutFull);
+            for (uint32_t x = g > kVStages ? g - kVStages : 0; x < g; ++x)
+                tc::mbar_wait(&bars[kVFull + x % kVStages], (x / kVStages) & 1u, tc::kErrTimeoutFull);
         }
     } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA
         if (tc::elect_one()) {
             const uint32_t s_tmem = tmem, o_tmem = tmem + 128;
-            bool ok = tc::mbar_wait(&bars[kQFull], 0, tc::kErrTimeoutFull);
             const uint64_t q_desc = tc::smem_desc_sw128(q_s);
-            const uint64_t k_desc = tc::smem_desc_sw128(k_s);
-            for (uint32_t j = 0; j < n_kv && ok; ++j) {
-                const uint32_t full = j & 1u, empty = full ^ 1u;
-                ok = tc::mbar_wait(&bars[kKFull], full, tc::kErrTimeoutFull) &&
-                     tc::mbar_wait(&bars[kSFree], empty, tc::kErrTimeoutAccEmpty);
-                if (!ok) break;
+            // S_{g+1} is issued as soon as the softmax has read S_g, before
+            // PV_g, so the next tile's scores are ready when the softmax needs
+            // them (within an item; Q is single-buffered across items).
+            auto issue_s = [&](uint32_t g, bool last_of_item) -> bool {
+                const uint32_t ks = g % kKStages;
+                if (!tc::mbar_wait(&bars[kKFull + ks], (g / kKStages) & 1u, tc::kErrTimeoutFull) ||
+                    !tc::mbar_wait(&bars[kSFree], (g & 1u) ^ 1u, tc::kErrTimeoutAccEmpty))
+                    return false;
                 tc::tc_fence_after();
+                const uint64_t k_desc = tc::smem_desc_sw128(k_ring + ks * kKBytes);
 #pragma unroll
                 for (uint32_t kk = 0; kk < kDh / 16; ++kk)
-                    tc::mma_bf16(s_tmem, tc::desc_advance(q_desc, kk * 32),
-                                 tc::desc_advance(k_desc, kk * 32), kIdescS, kk != 0);
+                    tc::mma_bf16(s_tmem, tc::desc_advance(q_desc, kk * 32), tc::desc_advance(k_desc, kk * 32),
+                                 kIdescS, kk != 0);
                 tc::mma_commit(&bars[kSFull]);
-                tc::mma_commit(&bars[kKEmpty]);
-                ok = tc::mbar_wait(&bars[kPFull], full, tc::kErrTimeoutFull) &&
-                     tc::mbar_wait(&bars[kVFull], full, tc::kErrTimeoutFull);
-                if (!ok) break;
-                tc::tc_fence_after();
+                tc::mma_commit(&bars[kKEmpty + ks]);
+                if (last_of_item) tc::mma_commit(&bars[kQEmpty]);
+                return true;
+            };
+            uint32_t g = 0, it = 0;
+            bool ok = true;
+            for (uint32_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+                if (!tc::mbar_wait(&bars[kQFull], it & 1u, tc::kErrTimeoutFull)) break;
+                if (!issue_s(g, n_kv == 1)) break;
+                for (uint32_t j = 0; j < n_kv; ++j, ++g) {
+                    if (j + 1 < n_kv && !issue_s(g + 1, j + 2 == n_kv)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t vs_i = g % kVStages;
+                    ok = tc::mbar_wait(&bars[kPFull], g & 1u, tc::kErrTimeoutFull) &&
+                         tc::mbar_wait(&bars[kVFull + vs_i], (g / kVStages) & 1u, tc::kErrTimeoutFull) &&
+                         (j != 0 || tc::mbar_wait(&bars[kOFree], (it & 1u) ^ 1u, tc::kErrTimeoutAccEmpty));
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    uint8_t* vs = v_ring + vs_i * kVBytes;
 #pragma unroll
-                for (uint32_t kk = 0; kk < kTile / 16; ++kk) {
-                    const uint32_t sub = kk >> 2, off = (kk & 3u) * 32;
-                    tc::mma_bf16(o_tmem,
-                                 tc::desc_advance(tc::smem_desc_sw128(p_s + sub * (kPBytes / 2)), off),
-                                 tc::desc_advance(tc::smem_desc_sw128(v_s + sub * (kVBytes / 2)), off),
-                                 kIdescO, (kk | j) != 0);
+                    for (uint32_t kk = 0; kk < kTile / 16; ++kk) {
+                        const uint32_t sub = kk >> 2, off = (kk & 3u) * 32;
+                        tc::mma_bf16(o_tmem,
+                                     tc::desc_advance(tc::smem_desc_sw128(p_s + sub * (kPBytes / 2)), off),
+                                     tc::desc_advance(tc::smem_desc_sw128(vs + sub * (kVBytes / 2)), off),
+                                     kIdescO, (kk | j) != 0);
+                    }
+                    tc::mma_commit(&bars[kVEmpty + vs_i]);
+                    tc::mma_commit(&bars[kPEmpty]);
+                    if (j + 1 == n_kv) tc::mma_commit(&bars[kOFull]);
                 }
-                tc::mma_commit(&bars[kVEmpty]);
-                tc::mma_commit(&bars[kPEmpty]);
-                if (j + 1 == n_kv) tc::mma_commit(&bars[kOFull]);
             }
             tc::mma_commit(&bars[kDrain]);
             tc::mbar_wait(&bars[kDrain], 0, tc::kErrTimeoutAccFull);
@@ -174,104 +236,122 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         const uint32_t r = quad * 32 + lane;  // query row within the tile
         const uint32_t lane_base = (quad * 32u) << 16;
         const float c = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
-        float m = 0.f, l = 0.f;
+        uint32_t g = 0, it = 0;
         bool ok = true;
-        for (uint32_t j = 0; j < n_kv && ok; ++j) {
-            const uint32_t full = j & 1u, empty = full ^ 1u;
-            if (!tc::mbar_wait(&bars[kSFull], full, tc::kErrTimeoutAccFull)) { ok = false; break; }
-            tc::tc_fence_after();
-            uint32_t sv[128];
+        for (uint32_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
+            const Item item = item_of(w, n_qt);
+            float m = 0.f, l = 0.f;
+            for (uint32_t j = 0; j < n_kv; ++j, ++g) {
+                if (!tc::mbar_wait(&bars[kSFull], g & 1u, tc::kErrTimeoutAccFull)) { ok = false; break; }
+                tc::tc_fence_after();
+                uint32_t sv[128];
 #pragma unroll
-            for (uint32_t cc = 0; cc < 4; ++cc)
-                tc::tmem_ld_32x32b_x32(tmem + lane_base + cc * 32,
-                                       *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
+                for (uint32_t cc = 0; cc < 4; ++cc)
+                    tc::tmem_ld_32x32b_x32(tmem + lane_base + cc * 32,
+                                           *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
+                tc::tmem_ld_wait();
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bars[kSFree]);
+                // row max with 8 independent partial maxima (short dependency chains)
+                float pm[8];
+#pragma unroll
+                for (uint32_t q = 0; q < 8; ++q) pm[q] = __uint_as_float(sv[q]);
+#pragma unroll
+                for (uint32_t e = 8; e < 128; e += 16) {
+#pragma unroll
+                    for (uint32_t q = 0; q < 8; ++q) {
+                        const uint32_t i0 = e + q, i1 = e + 8 + q;
+                        if (i1 < 128) {
+                            float t3;
+                            asm("max.f32 %0, %1, %2, %3;" : "=f"(t3) : "f"(pm[q]), "f"(__uint_as_float(sv[i0])),
+                                "f"(__uint_as_float(sv[i1])));
+                            pm[q] = t3;
+                        } else {
+                            pm[q] = fmaxf(pm[q], __uint_as_float(sv[i0]));
+                        }
+                    }
+                }
+                const float tmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                         fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+                const float mt = tmax * c;
+                float alpha = 1.f;
+                bool need = false;
+                if (j == 0) {
+                    m = mt;
+                } else if (mt > m + 8.0f) {
+                    need = true;
+                    alpha = ex2_approx(m - mt);
+                    m = mt;
+                    l *= alpha;
+                }
+                const float2 c2 = make_float2(c, c);
+                const float2 nm2 = make_float2(-m, -m);
+                float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                                make_float2(0.f, 0.f)};
+                uint32_t pk[64];
+#pragma unroll
+                for (uint32_t e = 0; e < 64; ++e) {
+                    const float2 sv2 = make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1]));
+                    const float2 a = __ffma2_rn(sv2, c2, nm2);
+                    const float2 pe = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+                    ps[e & 3u] = __fadd2_rn(ps[e & 3u], pe);
+                    pk[e] = pack_bf16(pe.x, pe.y);
+                }
+                const float2 sum2 = __fadd2_rn(__fadd2_rn(ps[0], ps[1]), __fadd2_rn(ps[2], ps[3]));
+                // P buffer free and O stable: the previous PV finished.
+                if (!tc::mbar_wait(&bars[kPEmpty], (g & 1u) ^ 1u, tc::kErrTimeoutEmpty)) { ok = false; break; }
+                if (__any_sync(0xFFFFFFFFu, need)) {
+                    tc::tc_fence_after();
+#pragma unroll
+                    for (uint32_t h2 = 0; h2 < 2; ++h2) {
+                        uint32_t ov[32];
+                        tc::tmem_ld_32x32b_x32(tmem + lane_base + 128 + 32 * h2, ov);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (uint32_t d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+                        tc::tmem_st_32x32b_x32(tmem + lane_base + 128 + 32 * h2, ov);
+                    }
+                    tc::tmem_st_wait();
+                }
+                uint8_t* rowp = p_s + (r >> 3) * 1024 + (r & 7u) * 128;
+#pragma unroll
+                for (uint32_t gg = 0; gg < 16; ++gg) {  // 16 chunks of 8 keys
+                    const uint32_t sub = gg >> 3;
+                    const uint32_t chunk = (gg & 7u) ^ (r & 7u);
+                    *reinterpret_cast<uint4*>(rowp + sub * (kPBytes / 2) + chunk * 16) =
+                        make_uint4(pk[4 * gg], pk[4 * gg + 1], pk[4 * gg + 2], pk[4 * gg + 3]);
+                }
+                l += sum2.x + sum2.y;
+                fence_proxy_async_smem();
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bars[kPFull]);
+            }
+            if (!ok) break;
+            // item done: O = accumulated P V; normalise and store
+            if (!tc::mbar_wait(&bars[kOFull], it & 1u, tc::kErrTimeoutAccFull)) break;
+            tc::tc_fence_after();
+            uint32_t v0[32], v1[32];
+            tc::tmem_ld_32x32b_x32(tmem + lane_base + 128, v0);
+            tc::tmem_ld_32x32b_x32(tmem + lane_base + 160, v1);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
-            tc::mbar_arrive(&bars[kSFree]);
-            float tmax = __uint_as_float(sv[0]);
+            tc::mbar_arrive(&bars[kOFree]);
+            const float inv_l = 1.0f / l;
+            const uint64_t tok = static_cast<uint64_t>(item.seq) * args.q_len + item.q_tile * kTile + r;
+            __nv_bfloat16* dst = args.out + tok * (kHeads * kDh) + item.head * kDh;
 #pragma unroll
-            for (uint32_t e = 1; e < 127; e += 2) {
-                float t3;
-                asm("max.f32 %0, %1, %2, %3;" : "=f"(t3) : "f"(tmax), "f"(__uint_as_float(sv[e])),
-                    "f"(__uint_as_float(sv[e + 1])));
-                tmax = t3;
-            }
-            tmax = fmaxf(tmax, __uint_as_float(sv[127]));
-            const float mt = tmax * c;
-            float alpha = 1.f;
-            bool need = false;
-            if (j == 0) {
-                m = mt;
-            } else if (mt > m + 8.0f) {
-                need = true;
-                alpha = ex2_approx(m - mt);
-                m = mt;
-                l *= alpha;
-            }
-            const float2 c2 = make_float2(c, c);
-            const float2 nm2 = make_float2(-m, -m);
-            float2 sum2 = make_float2(0.f, 0.f);
-            uint32_t pk[64];
-#pragma unroll
-            for (uint32_t e = 0; e < 64; ++e) {
-                const float2 sv2 = make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1]));
-                const float2 a = __ffma2_rn(sv2, c2, nm2);
-                const float2 pe = make_float2(ex2_approx(a.x), ex2_approx(a.y));
-                sum2 = __fadd2_rn(sum2, pe);
-                pk[e] = pack_bf16(pe.x, pe.y);
-            }
-            // P buffer free and O stable: the previous PV finished.
-            if (!tc::mbar_wait(&bars[kPEmpty], empty, tc::kErrTimeoutEmpty)) { ok = false; break; }
-            if (__any_sync(0xFFFFFFFFu, need)) {
-                tc::tc_fence_after();
-#pragma unroll
-                for (uint32_t h2 = 0; h2 < 2; ++h2) {
-                    uint32_t ov[32];
-                    tc::tmem_ld_32x32b_x32(tmem + lane_base + 128 + 32 * h2, ov);
-                    tc::tmem_ld_wait();
-#pragma unroll
-                    for (uint32_t d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
-                    tc::tmem_st_32x32b_x32(tmem + lane_base + 128 + 32 * h2, ov);
-                }
-                tc::tmem_st_wait();
-            }
-            uint8_t* rowp = p_s + (r >> 3) * 1024 + (r & 7u) * 128;
-#pragma unroll
-            for (uint32_t g = 0; g < 16; ++g) {  // 16 chunks of 8 keys
-                const uint32_t sub = g >> 3;
-                const uint32_t chunk = (g & 7u) ^ (r & 7u);
-                *reinterpret_cast<uint4*>(rowp + sub * (kPBytes / 2) + chunk * 16) =
-                    make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-            }
-            l += sum2.x + sum2.y;
-            fence_proxy_async_smem();
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bars[kPFull]);
-        }
-        if (ok && n_kv > 0) {
-            if (tc::mbar_wait(&bars[kOFull], 0, tc::kErrTimeoutAccFull)) {
-                tc::tc_fence_after();
-                uint32_t v0[32], v1[32];
-                tc::tmem_ld_32x32b_x32(tmem + lane_base + 128, v0);
-                tc::tmem_ld_32x32b_x32(tmem + lane_base + 160, v1);
-                tc::tmem_ld_wait();
-                const float inv_l = 1.0f / l;
-                const uint64_t tok = static_cast<uint64_t>(seq) * args.q_len + q_tile * kTile + r;
-                __nv_bfloat16* dst = args.out + tok * (kHeads * kDh) + head * kDh;
-#pragma unroll
-                for (uint32_t d = 0; d < 32; d += 8) {
-                    uint4 a, b;
-                    a.x = pack_bf16(__uint_as_float(v0[d]) * inv_l, __uint_as_float(v0[d + 1]) * inv_l);
-                    a.y = pack_bf16(__uint_as_float(v0[d + 2]) * inv_l, __uint_as_float(v0[d + 3]) * inv_l);
-                    a.z = pack_bf16(__uint_as_float(v0[d + 4]) * inv_l, __uint_as_float(v0[d + 5]) * inv_l);
-                    a.w = pack_bf16(__uint_as_float(v0[d + 6]) * inv_l, __uint_as_float(v0[d + 7]) * inv_l);
-                    b.x = pack_bf16(__uint_as_float(v1[d]) * inv_l, __uint_as_float(v1[d + 1]) * inv_l);
-                    b.y = pack_bf16(__uint_as_float(v1[d + 2]) * inv_l, __uint_as_float(v1[d + 3]) * inv_l);
-                    b.z = pack_bf16(__uint_as_float(v1[d + 4]) * inv_l, __uint_as_float(v1[d + 5]) * inv_l);
-                    b.w = pack_bf16(__uint_as_float(v1[d + 6]) * inv_l, __uint_as_float(v1[d + 7]) * inv_l);
-                    *reinterpret_cast<uint4*>(dst + d) = a;
-                    *reinterpret_cast<uint4*>(dst + 32 + d) = b;
-                }
+            for (uint32_t d = 0; d < 32; d += 8) {
+                uint4 a, b;
+                a.x = pack_bf16(__uint_as_float(v0[d]) * inv_l, __uint_as_float(v0[d + 1]) * inv_l);
+                a.y = pack_bf16(__uint_as_float(v0[d + 2]) * inv_l, __uint_as_float(v0[d + 3]) * inv_l);
+                a.z = pack_bf16(__uint_as_float(v0[d + 4]) * inv_l, __uint_as_float(v0[d + 5]) * inv_l);
+                a.w = pack_bf16(__uint_as_float(v0[d + 6]) * inv_l, __uint_as_float(v0[d + 7]) * inv_l);
+                b.x = pack_bf16(__uint_as_float(v1[d]) * inv_l, __uint_as_float(v1[d + 1]) * inv_l);
+                b.y = pack_bf16(__uint_as_float(v1[d + 2]) * inv_l, __uint_as_float(v1[d + 3]) * inv_l);
+                b.z = pack_bf16(__uint_as_float(v1[d + 4]) * inv_l, __uint_as_float(v1[d + 5]) * inv_l);
+                b.w = pack_bf16(__uint_as_float(v1[d + 6]) * inv_l, __uint_as_float(v1[d + 7]) * inv_l);
+                *reinterpret_cast<uint4*>(dst + d) = a;
+                *reinterpret_cast<uint4*>(dst + 32 + d) = b;
             }
         }
     }
@@ -313,8 +393,14 @@ extern "C" uint32_t dh_attention(const void* q, const void* k, const void* vt, v
             return DH_ERR_CUDA;
         configured = true;
     }
-    AttnArgs a{q_len, kv_len, kv_stride, static_cast<__nv_bfloat16*>(out), run_flag};
-    dim3 grid(q_len / kTile, kHeads, sequences);
+    AttnArgs a{sequences, q_len, kv_len, kv_stride, static_cast<__nv_bfloat16*>(out), run_flag};
+    int sms = kNumSMs, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    }
+    const uint64_t items = static_cast<uint64_t>(sequences) * kHeads * (q_len / kTile);
+    const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(items, 2ull * sms));
     attention_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, a);
     DH_LAUNCH_CHECK();
     return DH_OK;
