@@ -226,7 +226,7 @@ def head_microbench(qm, peaks: dict, peaks_kind: str) -> dict:
     V = qm.config.vocab_size
 
     def run():
-        _lib.call("dh_head_argmax_i8", _lib.ptr(h), 768, _lib.ptr(wq), 768, rows, None, 768, V,
+        _lib.call("dh_head_argmax_i8", _lib.ptr(h), 768, _lib.ptr(wq), 768, rows, None, 768, V, 0,
                   qm.config.mask_token_id, 1, _lib.ptr(a_scale), _lib.ptr(w_scale), _lib.ptr(bias), None,
                   None, None, _lib.ptr(pos), _lib.ptr(key), None, 3, 0, 0, _lib.ptr(packed), None, None,
                   _lib.stream_handle())
@@ -263,6 +263,66 @@ def profile_forward(args) -> None:
         eng.head_argmax(eng.M, 1, rows_count=count, row_position=pos, row_key_hi=key, key_lo=0)
     torch.cuda.synchronize()
     print("profile-forward done", flush=True)
+
+
+def run_vocab_shard(args, world: int, rank: int) -> None:
+    """Single-sequence latency: every rank runs the same backbone forward and
+    projects its slice of the head; the packed (score, ~id) words are
+    MAX-reduced over NCCL every transition, so all ranks commit the same
+    tokens (identical to the unsharded head)."""
+    import torch
+
+    from diffusionhard_b200.distributed import vocab_shards
+    from diffusionhard_b200.engine import MDLMEngine
+    from diffusionhard_b200.model import MDLMConfig, build_quantized
+
+    cfg = MDLMConfig()
+    qm = build_quantized(cfg, seed=0)
+    L, S = args.seq_len, args.denoise_steps
+    eng = MDLMEngine(qm, 1, L)
+    if world > 1:
+        import torch.distributed as dist
+
+        v0, v1 = vocab_shards(cfg.vocab_size, world)[rank]
+        eng.shard_head(v0, v1, group=dist.group.WORLD)
+    ids = torch.full((1, L), cfg.mask_token_id, dtype=torch.int64, device="cuda")
+    for _ in range(args.warmup):
+        eng.generate(ids, steps=S, seed=0, graph=False)
+    torch.cuda.synchronize()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        eng.generate(ids, steps=S, seed=0, graph=False)
+    end.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    tokens_here = eng.tokens.clone()
+    if world > 1:
+        import torch.distributed as dist
+
+        gathered = [torch.empty_like(tokens_here) for _ in range(world)]
+        dist.all_gather(gathered, tokens_here)
+        consistent = all(torch.equal(g, tokens_here) for g in gathered)
+    else:
+        consistent = True
+    if rank == 0:
+        per = ms / args.steps
+        print(json.dumps({
+            "metric": "single-sequence generation latency, MDLM-169.6M int8, vocab-sharded head",
+            "value": round(L / (per * 1e-3), 1), "unit": "tok/s", "ms_per_generation": round(per, 3),
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"1 x L={L}, {S} ddpm_cache steps, head 768x50258 split over {world} GPU(s), "
+                                   "packed-u64 MAX all-reduce per transition", "global_batch": 1, "seq_len": L,
+                       "steps": S, "parallelism": f"vocab{world}"},
+            "ranks_agree_on_tokens": consistent,
+            "model_evaluations": eng.metadata(S)["model_evaluations"]}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_reference(args, world: int, rank: int) -> None:
@@ -303,6 +363,12 @@ def main() -> None:
     ap.add_argument("--seq-len", type=int, default=1024)
     ap.add_argument("--denoise-steps", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=0,
+                    help="split this many sequences over the ranks (strong scaling, e.g. 512 "
+                         "with --denoise-steps 32); default: --batch per GPU (weak scaling)")
+    ap.add_argument("--vocab-shard", action="store_true",
+                    help="single-sequence latency: backbone replicated, 768x50258 head split over "
+                         "the ranks, per-transition packed-max all-reduce (one line, impl ours)")
     ap.add_argument("--profile-forward", action="store_true",
                     help="run one warm-up forward, then one forward + one head call "
                          "(a short launch list for ncu)")
@@ -331,11 +397,21 @@ def main() -> None:
     if args.profile_forward:
         profile_forward(args)
         return
+    if args.vocab_shard:
+        run_vocab_shard(args, world, rank)
+        return
     cfg = MDLMConfig()
     qm = build_quantized(cfg, seed=0)
-    B, L, S = args.batch, args.seq_len, args.denoise_steps
+    L, S = args.seq_len, args.denoise_steps
+    if args.global_batch:
+        from diffusionhard_b200.distributed import shard_batch
+
+        offset, B = shard_batch(args.global_batch, world, rank)
+        scaling = "strong"
+    else:
+        B, offset, scaling = args.batch, rank * args.batch, "weak"
     eng = MDLMEngine(qm, B, L)
-    eng.seq_offset = rank * B
+    eng.seq_offset = offset
     ids_dev = torch.full((B, L), cfg.mask_token_id, dtype=torch.int64, device="cuda")
     host_ids = torch.full((B, L), cfg.mask_token_id, dtype=torch.int64).pin_memory()
 
@@ -357,7 +433,8 @@ def main() -> None:
         barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world)
     clock_info = clocks.summary()
-    tokens = world * B * L * args.steps
+    global_batch = args.global_batch or world * B
+    tokens = global_batch * L * args.steps
     value = tokens / (ms * 1e-3)
     meta = eng.metadata(S)
     masks_left = int((eng.tokens == cfg.mask_token_id).sum().item())
@@ -406,10 +483,13 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (random-init N(0,0.02) weights, all-masked canvases)",
-            "config": {"workload": "MDLM-169.6M W8A8, batch 32 x L=1024 per GPU, 64 ddpm_cache steps + final pass",
-                       "global_batch": world * B, "seq_len": L, "steps": S, "parallelism": f"dp{world} batch-sharded",
+            "config": {"workload": (f"MDLM-169.6M W8A8, batch {B} x L={L} per GPU, {S} ddpm_cache steps + final pass"
+                                    if scaling == "weak" else
+                                    f"MDLM-169.6M W8A8, {global_batch} x L={L} split over {world} GPU(s), "
+                                    f"{S} ddpm_cache steps + final pass"),
+                       "global_batch": global_batch, "seq_len": L, "steps": S, "parallelism": f"dp{world} batch-sharded",
                        "l2": "activations per forward (> 1 GB) exceed L2; no flush needed"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": B * L * 8,
                     "d2h_bytes_per_step": B * L * 8 + 3 * S * 4, "wall_ms_per_step": round(wall_e2e / args.steps, 3)},

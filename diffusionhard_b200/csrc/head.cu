@@ -38,7 +38,8 @@ enum HeadMode : uint32_t { kRequantQ20 = 0, kDequantNoisy = 1, kDequantGreedy = 
 
 struct HeadParams {
     uint32_t mode;
-    uint32_t vocab, mask_id;
+    uint32_t vocab, mask_id;   // vocab: columns of this weight slice; mask_id: global token id
+    uint32_t vocab_offset;     // global id of column 0 (vocab-sharded head), multiple of 4
     const float* a_scale;      // [rows]          (dequant modes)
     const float* w_scale;      // [vocab]
     const float* bias;         // [vocab] fp32
@@ -112,10 +113,10 @@ struct EpiHead : EpiBase {
 #pragma unroll
             for (uint32_t j = 0; j < 32; ++j) {
                 const uint32_t t = col0 + j;
-                if (t >= p.vocab || t == p.mask_id) continue;
+                if (t >= p.vocab || t + p.vocab_offset == p.mask_id) continue;
                 const float l = ref_logit(static_cast<int32_t>(v[j]), st.a_scale,
                                           __ldg(p.w_scale + t), __ldg(p.bias + t));
-                const unsigned long long pk = pack_float_id(l, t);
+                const unsigned long long pk = pack_float_id(l, t + p.vocab_offset);
                 best = pk > best ? pk : best;
             }
             st.best = best;
@@ -127,7 +128,8 @@ struct EpiHead : EpiBase {
             const uint32_t t0 = col0 + g;
             if (t0 >= p.vocab) break;
             Philox4 w{0, 0, 0, 0};
-            if (!p.noise) w = philox4x32_10(t0 >> 2, st.pos, st.ev, p.stream_id, p.key_lo, st.key_hi);
+            if (!p.noise)
+                w = philox4x32_10((t0 + p.vocab_offset) >> 2, st.pos, st.ev, p.stream_id, p.key_lo, st.key_hi);
             float ws[4] = {0.f, 0.f, 0.f, 0.f}, bs[4] = {0.f, 0.f, 0.f, 0.f};
             int32_t ms[4] = {0, 0, 0, 0}, bq[4] = {0, 0, 0, 0};
             if (p.mode == kRequantQ20) {
@@ -153,7 +155,7 @@ struct EpiHead : EpiBase {
 #pragma unroll
             for (uint32_t i = 0; i < 4; ++i) {
                 const uint32_t t = t0 + i;
-                if (t >= p.vocab || t == p.mask_id) continue;
+                if (t >= p.vocab || t + p.vocab_offset == p.mask_id) continue;
                 const int32_t acc = static_cast<int32_t>(v[g + i]);
                 const int32_t noise = p.noise ? p.noise[static_cast<uint64_t>(row) * p.vocab + t]
                                               : gumbel_q10(philox_lane(w, i), st.table);
@@ -162,7 +164,7 @@ struct EpiHead : EpiBase {
                     s = static_cast<int64_t>(requant_q20(acc, ms[i])) + bq[i] + noise;
                 else
                     s = static_cast<int64_t>(q10(ref_logit(acc, st.a_scale, ws[i], bs[i]))) + noise;
-                const unsigned long long pk = pack_score_id(sat_i32(s), t);
+                const unsigned long long pk = pack_score_id(sat_i32(s), t + p.vocab_offset);
                 best = pk > best ? pk : best;
             }
         }
@@ -224,8 +226,8 @@ extern "C" {
 
 uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_t* weights,
                            uint64_t ld_weights, uint32_t rows, const uint32_t* rows_count,
-                           uint32_t hidden_size, uint32_t vocabulary_size, uint32_t mask_token_id,
-                           uint32_t mode, const float* a_scale, const float* w_scale,
+                           uint32_t hidden_size, uint32_t vocabulary_size, uint32_t vocab_offset,
+                           uint32_t mask_token_id, uint32_t mode, const float* a_scale, const float* w_scale,
                            const float* bias, const int32_t* mult_q20, const int32_t* bias_q10,
                            const int32_t* noise, const uint32_t* row_position,
                            const uint32_t* row_key_hi, const uint32_t* row_eval,
@@ -233,16 +235,18 @@ uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_
                            uint64_t* packed, int32_t* out_ids, int32_t* out_scores, void* stream) {
     if (rows == 0) return DH_HEAD_INVALID_POSITION_COUNT;
     if (hidden_size == 0) return DH_HEAD_INVALID_HIDDEN_SIZE;
-    if (vocabulary_size == 0 || vocabulary_size > 65535) return DH_HEAD_INVALID_VOCABULARY_SIZE;
-    if (mask_token_id >= vocabulary_size) return DH_HEAD_INVALID_MASK_TOKEN;
-    if (mode > kDequantGreedy) return DH_ERR_INVALID_ARGUMENT;
+    if (vocabulary_size == 0 || vocab_offset + static_cast<uint64_t>(vocabulary_size) > 65535)
+        return DH_HEAD_INVALID_VOCABULARY_SIZE;
+    // the mask id is global and may lie outside this (shard's) row range
+    if (mask_token_id > 65535) return DH_HEAD_INVALID_MASK_TOKEN;
+    if (mode > kDequantGreedy || (vocab_offset & 3u)) return DH_ERR_INVALID_ARGUMENT;
     if (!packed) return DH_ERR_NULL_POINTER;
     if (mode == kRequantQ20 && (!mult_q20 || !bias_q10)) return DH_ERR_NULL_POINTER;
     if (mode != kRequantQ20 && (!a_scale || !w_scale || !bias)) return DH_ERR_NULL_POINTER;
     if ((reinterpret_cast<uintptr_t>(w_scale) | reinterpret_cast<uintptr_t>(bias)) & 15u)
         return DH_ERR_ALIGNMENT;
-    HeadParams hp{mode, vocabulary_size, mask_token_id, a_scale, w_scale, bias, mult_q20, bias_q10,
-                  noise, row_position, row_key_hi, row_eval, const_eval, 0u, key_lo, stream_id,
+    HeadParams hp{mode, vocabulary_size, mask_token_id, vocab_offset, a_scale, w_scale, bias, mult_q20,
+                  bias_q10, noise, row_position, row_key_hi, row_eval, const_eval, 0u, key_lo, stream_id,
                   reinterpret_cast<unsigned long long*>(packed)};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     uint32_t s = launch_head(hidden, ld_hidden, weights, ld_weights, rows, rows_count, hidden_size,
@@ -276,7 +280,7 @@ uint32_t dh_output_head_int8(const int8_t* hidden, const int8_t* weights,
     if (mask_token_id >= vocabulary_size) return DH_HEAD_INVALID_MASK_TOKEN;
     if (!requant_multiplier_q20 || !bias || !candidate_ids || !workspace) return DH_ERR_NULL_POINTER;
     if (hidden_size % 16 != 0) return DH_ERR_ALIGNMENT;
-    HeadParams hp{kRequantQ20, vocabulary_size, mask_token_id, nullptr, nullptr, nullptr,
+    HeadParams hp{kRequantQ20, vocabulary_size, mask_token_id, 0u, nullptr, nullptr, nullptr,
                   requant_multiplier_q20, bias, noise, nullptr, nullptr, nullptr, evaluation_id,
                   seed_high, seed_low, stream_id, reinterpret_cast<unsigned long long*>(workspace)};
     cudaStream_t st = static_cast<cudaStream_t>(stream);

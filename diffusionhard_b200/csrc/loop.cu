@@ -6,8 +6,9 @@
 //           forward runs (fwd_rows = B*L) iff some sequence refills.
 //   select  reveal decision of every active position, word
 //           philox((p/4, 0, k, 1), (seed, b))[p%4] < threshold_k, compacted
-//           into a row list with the row's noise counter fields
-//           (position p, key_hi b, eval = transition of b's last evaluation).
+//           in position-major order into a row list with the row's noise
+//           counter fields (position p, key_hi b, eval = transition of b's
+//           last evaluation).
 //   [head]  candidates for the selected rows only (head.cu)
 //   commit  tokens <- candidates, clear active bits, mark changed sequences.
 //
@@ -66,21 +67,29 @@ loop_plan_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t final_pass,
     }
 }
 
-// One CTA per sequence.  Warp-level compaction (ballot) then one atomicAdd per
-// warp reserves contiguous slots in the global row list.
-__global__ void __launch_bounds__(256)
-loop_select_kernel(uint32_t L, uint32_t step, uint32_t seed, uint32_t seq_offset, uint64_t threshold,
-                   uint32_t final_pass, const uint64_t* __restrict__ active,
+// One CTA compacts the revealed rows of the whole batch in position-major
+// order (ballot + block scan, no atomics), so the row list is a deterministic
+// function of the state: replicated ranks of the vocab-sharded head reduce
+// their per-row results slot by slot.
+__global__ void __launch_bounds__(1024)
+loop_select_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t seed, uint32_t seq_offset,
+                   uint64_t threshold, uint32_t final_pass, const uint64_t* __restrict__ active,
                    const uint32_t* __restrict__ eval_id, uint32_t* __restrict__ sel_rows,
                    uint32_t* __restrict__ sel_pos, uint32_t* __restrict__ sel_key,
                    uint32_t* __restrict__ sel_eval, uint32_t* __restrict__ sel_count) {
-    const uint32_t b = blockIdx.x;
+    __shared__ uint32_t warp_off[32];
+    __shared__ uint32_t iter_total, base;
     const uint32_t W = (L + 63) / 64;
-    const uint32_t ev = eval_id[b];
-    for (uint32_t p0 = warp_id() * 32; p0 < L; p0 += blockDim.x) {
-        const uint32_t p = p0 + lane_id();
+    const uint64_t total = static_cast<uint64_t>(B) * L;
+    if (threadIdx.x == 0) base = 0;
+    __syncthreads();
+    for (uint64_t start = 0; start < total; start += blockDim.x) {
+        const uint64_t idx = start + threadIdx.x;
         bool take = false;
-        if (p < L) {
+        uint32_t b = 0, p = 0;
+        if (idx < total) {
+            b = static_cast<uint32_t>(idx / L);
+            p = static_cast<uint32_t>(idx % L);
             const bool act = (active[static_cast<uint64_t>(b) * W + (p >> 6)] >> (p & 63u)) & 1ull;
             if (act) {
                 if (final_pass) {
@@ -92,18 +101,33 @@ loop_select_kernel(uint32_t L, uint32_t step, uint32_t seed, uint32_t seq_offset
             }
         }
         const uint32_t mask = __ballot_sync(0xFFFFFFFFu, take);
-        if (!mask) continue;
-        uint32_t base = 0;
-        if (lane_id() == 0) base = atomicAdd(sel_count, __popc(mask));
-        base = __shfl_sync(0xFFFFFFFFu, base, 0);
+        if (lane_id() == 0) warp_off[warp_id()] = __popc(mask);
+        __syncthreads();
+        if (warp_id() == 0) {
+            const uint32_t nw = blockDim.x / 32;
+            const uint32_t c = lane_id() < nw ? warp_off[lane_id()] : 0u;
+            uint32_t inc = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+                if (lane_id() >= static_cast<uint32_t>(o)) inc += t;
+            }
+            if (lane_id() < nw) warp_off[lane_id()] = inc - c;
+            if (lane_id() == 31) iter_total = inc;
+        }
+        __syncthreads();
         if (take) {
-            const uint32_t slot = base + __popc(mask & ((1u << lane_id()) - 1u));
+            const uint32_t slot = base + warp_off[warp_id()] + __popc(mask & ((1u << lane_id()) - 1u));
             sel_rows[slot] = b * L + p;
             sel_pos[slot] = p;
             sel_key[slot] = seq_offset + b;
-            sel_eval[slot] = ev;
+            sel_eval[slot] = eval_id[b];
         }
+        __syncthreads();
+        if (threadIdx.x == 0) base += iter_total;
+        __syncthreads();
     }
+    if (threadIdx.x == 0) *sel_count = base;
 }
 
 __global__ void loop_commit_kernel(uint32_t L, uint32_t step, uint32_t final_pass,
@@ -204,9 +228,9 @@ uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, u
     if (!active || !eval_id || !sel_rows || !sel_pos || !sel_key || !sel_eval || !sel_count)
         return DH_ERR_NULL_POINTER;
     if (sequences == 0 || positions == 0) return DH_ERR_INVALID_ARGUMENT;
-    loop_select_kernel<<<sequences, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        positions, step, seed, seq_offset, threshold_q32, final_pass, active, eval_id, sel_rows, sel_pos,
-        sel_key, sel_eval, sel_count);
+    loop_select_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+        sequences, positions, step, seed, seq_offset, threshold_q32, final_pass, active, eval_id,
+        sel_rows, sel_pos, sel_key, sel_eval, sel_count);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }

@@ -106,8 +106,26 @@ class MDLMEngine:
         self.sel_eval = torch.empty(M, dtype=u32, device=d)
         self.counters: Optional[Any] = None
         self.seq_offset = 0  # global index of local sequence 0 (Philox key_hi)
+        self.head_vocab_offset = 0  # global id of the first head row held here (vocab-sharded head)
+        self.head_group = None      # process group reducing the sharded head, or None
+        self.head_reduce = None     # callable(packed) merging shard results (testing / custom groups)
         self._graphs: Dict[Any, Any] = {}
         self.launches_per_forward = 1 + 9 * len(self.blocks)
+
+    def shard_head(self, v0: int, v1: int, group: Any = None, reduce: Any = None) -> None:
+        """Keep only head rows [v0, v1) (vocab-sharded head).  After every head
+        launch the packed per-row results are MAX-reduced over `group` (or
+        passed to `reduce`), so each rank commits the unsharded argmax."""
+        if v0 % 4:
+            raise ValueError("shard start must be a multiple of 4")
+        h = self.head
+        h.w = h.w[v0:v1].contiguous()
+        h.w_scale = h.w_scale[v0:v1].contiguous()
+        h.bias = h.bias[v0:v1].contiguous()
+        h.out_features = v1 - v0
+        self.head_vocab_offset = v0
+        self.head_group = group
+        self.head_reduce = reduce
 
     @staticmethod
     def kv_cache(qm: QuantizedMDLM, batch: int, kv_stride: int, device: Any = "cuda") -> List[tuple]:
@@ -178,8 +196,8 @@ class MDLMEngine:
         s = _lib.stream_handle()
         h = self.head
         _lib.call("dh_head_argmax_i8", self._p(self.head_q), 768, self._p(h.w), 768, rows,
-                  self._p(rows_count) if rows_count is not None else None, 768, self.cfg.vocab_size,
-                  self.cfg.mask_token_id, mode, self._p(self.head_scale), self._p(h.w_scale),
+                  self._p(rows_count) if rows_count is not None else None, 768, h.out_features,
+                  self.head_vocab_offset, self.cfg.mask_token_id, mode, self._p(self.head_scale), self._p(h.w_scale),
                   self._p(h.bias), None, None, None, self._p(row_position), self._p(row_key_hi),
                   self._p(row_eval), const_eval, key_lo, 0, self._p(self.packed), self._p(out_ids),
                   self._p(out_scores), s)
@@ -203,6 +221,12 @@ class MDLMEngine:
         self.final_hidden_q(self.sel_rows, self.sel_count)
         self.head_argmax(self.M, 2 if final else 1, rows_count=self.sel_count, row_position=self.sel_pos,
                          row_key_hi=self.sel_key, row_eval=self.sel_eval, key_lo=seed)
+        if self.head_reduce is not None:
+            self.head_reduce(self.packed)
+        elif self.head_group is not None:
+            from .distributed import all_reduce_packed_max_
+
+            all_reduce_packed_max_(self.packed, self.head_group)
         call("dh_loop_commit", B, L, kk, steps, final, p(self.packed), p(self.sel_rows), p(self.sel_count),
              p(self.tokens), p(self.active), p(self.need_eval), p(self.counters), s)
 

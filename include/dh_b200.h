@@ -282,11 +282,17 @@ uint32_t dh_attention(const void* q, const void* k, const void* vt, void* out, u
  * philox((v/4, row_position[r], row_eval[r] or const_eval, stream_id),
  * (key_lo, row_key_hi[r]))[v%4].  rows_count (device, may be NULL) limits the
  * rows processed, for data-dependent row sets.  Mask token skipped.
+ * Vocab-sharded head: `weights` / `w_scale` / `bias` hold the rows of global
+ * tokens [vocab_offset, vocab_offset + vocabulary_size) (vocab_offset a
+ * multiple of 4); ids, noise counters and the mask test use global ids (the
+ * mask id may lie outside the shard), so a
+ * MAX reduction of the packed words over shards gives the unsharded result
+ * (the tie rule of ordered_noisy_argmax_reducer.sv:106-133 included).
  * Status: head family codes, then DH_ERR_*. */
 uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_t* weights,
                            uint64_t ld_weights, uint32_t rows, const uint32_t* rows_count,
-                           uint32_t hidden_size, uint32_t vocabulary_size, uint32_t mask_token_id,
-                           uint32_t mode, const float* a_scale, const float* w_scale,
+                           uint32_t hidden_size, uint32_t vocabulary_size, uint32_t vocab_offset,
+                           uint32_t mask_token_id, uint32_t mode, const float* a_scale, const float* w_scale,
                            const float* bias, const int32_t* mult_q20, const int32_t* bias_q10,
                            const int32_t* noise, const uint32_t* row_position,
                            const uint32_t* row_key_hi, const uint32_t* row_eval,

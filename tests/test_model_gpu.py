@@ -78,7 +78,7 @@ def _head(torch, hq, hs, qm, mode, pos=None, key=None, ev=None, key_lo=0):
     dev = lambda a: None if a is None else torch.from_numpy(np.asarray(a, np.int32)).cuda()  # noqa: E731
     p_, k_, e_ = dev(pos), dev(key), dev(ev)
     _lib.call("dh_head_argmax_i8", _lib.ptr(hq), 768, _lib.ptr(wq), 768, rows, None, 768,
-              qm.config.vocab_size, qm.config.mask_token_id, mode, _lib.ptr(hs), _lib.ptr(ws), _lib.ptr(bias),
+              qm.config.vocab_size, 0, qm.config.mask_token_id, mode, _lib.ptr(hs), _lib.ptr(ws), _lib.ptr(bias),
               None, None, None, _lib.ptr(p_), _lib.ptr(k_), _lib.ptr(e_), 0, key_lo, 0, _lib.ptr(packed),
               _lib.ptr(ids), _lib.ptr(sc), None)
     torch.cuda.synchronize()
@@ -208,6 +208,7 @@ def test_loop_teacher_forced_bit_exact(cuda, small_model):
         torch.cuda.synchronize()
         n = int(eng.sel_count.item())
         rows = eng.sel_rows[:n].cpu().numpy()
+        assert np.all(np.diff(rows.astype(np.int64)) > 0)  # deterministic position-major order
         active = tokens_before == mask
         if k < steps:
             for b in range(B):
@@ -287,4 +288,41 @@ def test_prefix_cached_suffix_matches_oracle(cuda, small_model):
     ref_x = rec_s[f"x{SMALL.blocks - 1}"]
     assert ((got_x - ref_x).norm() / ref_x.norm()).item() < 1e-2
     del h
+    assert _device_error() == 0
+
+
+def test_vocab_sharded_head_equals_unsharded(cuda):
+    """Head rows split into 4 slices (global ids via vocab_offset); the MAX of
+    the packed words equals the unsharded head, ids and scores, both modes."""
+    torch = cuda
+    from diffusionhard_b200.distributed import decode_packed, to_signed_, vocab_shards
+
+    V, rows, mask = 50258, 257, 50257
+    rng = np.random.default_rng(42)
+    W = torch.from_numpy(np.clip(np.round(rng.normal(0, 40, (V, 768))), -127, 127).astype(np.int8)).cuda()
+    ws = torch.from_numpy(rng.uniform(0.5e-3, 2e-3, V).astype(np.float32)).cuda()
+    bias = torch.from_numpy(rng.normal(0, 0.02, V).astype(np.float32)).cuda()
+    h = torch.from_numpy(rng.integers(-127, 128, (rows, 768)).astype(np.int8)).cuda()
+    a = torch.from_numpy(rng.uniform(0.01, 0.05, rows).astype(np.float32)).cuda()
+    pos = torch.from_numpy(rng.integers(0, 1024, rows).astype(np.int32)).cuda()
+
+    def run(v0, v1, mode):
+        packed = torch.zeros(rows, dtype=torch.int64, device="cuda")
+        wsl, wss, bsl = W[v0:v1].contiguous(), ws[v0:v1].contiguous(), bias[v0:v1].contiguous()
+        _lib.call("dh_head_argmax_i8", _lib.ptr(h), 768, _lib.ptr(wsl), 768, rows, None, 768, v1 - v0, v0, mask,
+                  mode, _lib.ptr(a), _lib.ptr(wss), _lib.ptr(bsl), None, None, None, _lib.ptr(pos), None, None,
+                  9, 3, 0, _lib.ptr(packed), None, None, None)
+        torch.cuda.synchronize()
+        return packed
+
+    for mode in (1, 2):
+        full = run(0, V, mode)
+        merged = None
+        for v0, v1 in vocab_shards(V, 4):
+            part = to_signed_(run(v0, v1, mode))
+            merged = part if merged is None else torch.maximum(merged, part)
+        to_signed_(merged)
+        assert torch.equal(merged, full), mode
+        ids, _ = decode_packed(full)
+        assert not (ids == mask).any()
     assert _device_error() == 0
