@@ -66,6 +66,7 @@ DH_DEVINL uint32_t pack_bf16x2(float a, float b) {
 // its Q / K block is 4 KB contiguous and its V^T block is 64 runs of 64 bytes:
 // both are written through the warp's staging buffer with full-line stores.
 struct EpiQKV : EpiBase {
+    static constexpr uint32_t kStages = 3;  // leaves L1 room for the per-column / rotary tables
     static constexpr uint32_t kChunk = 64;
     static constexpr uint32_t kStagingPerWarp = 32 * 128;
     struct Params {
@@ -169,7 +170,9 @@ struct EpiQKV : EpiBase {
 // x[row, col] += acc * (a_scale * w_scale) + bias  (attention out, MLP down).
 // The residual read-modify-write goes through the staging buffer with one
 // 128-byte row segment per warp instruction.
-struct EpiResidual : EpiBase {
+template <uint32_t kStages_>
+struct EpiResidualT : EpiBase {
+    static constexpr uint32_t kStages = kStages_;
     static constexpr uint32_t kChunk = 32;
     static constexpr uint32_t kStagingPerWarp = 32 * 128;
     struct Params {
@@ -179,9 +182,26 @@ struct EpiResidual : EpiBase {
         float* x;
         uint32_t n;
     };
-    struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
-    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
+    // x of the next chunk is loaded one chunk ahead (the first chunk before
+    // the accumulator is ready): lane -> (row i*4 + lane/8, 4 columns).
+    struct TileState {
+        float4 xv[8];
+        uint32_t col_end;
+    };
+    static DH_DEVINL void load_x(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0) {
+        const uint32_t cq = (ctx.lane & 7u) * 4;
+#pragma unroll
+        for (uint32_t i = 0; i < 8; ++i) {
+            const uint32_t rr = i * 4 + (ctx.lane >> 3);
+            if (ctx.row0 + rr < ctx.m_eff)
+                st.xv[i] = *reinterpret_cast<const float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq);
+        }
+    }
+    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
+        st.col_end = col_start + 128;
+        load_x(p, st, ctx, col_start);
+    }
+    static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
         const float ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
         const uint32_t lane = ctx.lane;
@@ -195,32 +215,27 @@ struct EpiResidual : EpiBase {
                             dequant(v[j + 2], ab, w.z, bb.z), dequant(v[j + 3], ab, w.w, bb.w));
         }
         __syncwarp();
-        // lane -> (row i*4 + lane/8, columns 4*(lane%8) .. +3): 4 rows x 128 B per instruction
         const uint32_t cq = (lane & 7u) * 4;
-        float4 xv[8];
+        float4 out[8];
+#pragma unroll
+        for (uint32_t i = 0; i < 8; ++i) {
+            const uint32_t rr = i * 4 + (lane >> 3);
+            const float4 y = *reinterpret_cast<const float4*>(ctx.stage + swz128(rr, lane & 7u));
+            out[i] = make_float4(st.xv[i].x + y.x, st.xv[i].y + y.y, st.xv[i].z + y.z, st.xv[i].w + y.w);
+        }
+        __syncwarp();
+        if (col0 + 32 < st.col_end) load_x(p, st, ctx, col0 + 32);  // next chunk, in flight during the stores
 #pragma unroll
         for (uint32_t i = 0; i < 8; ++i) {
             const uint32_t rr = i * 4 + (lane >> 3);
             if (ctx.row0 + rr < ctx.m_eff)
-                xv[i] = *reinterpret_cast<const float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq);
+                *reinterpret_cast<float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq) = out[i];
         }
-#pragma unroll
-        for (uint32_t i = 0; i < 8; ++i) {
-            const uint32_t rr = i * 4 + (lane >> 3);
-            if (ctx.row0 + rr < ctx.m_eff) {
-                const float4 y = *reinterpret_cast<const float4*>(ctx.stage + swz128(rr, lane & 7u));
-                float4 o = xv[i];
-                o.x += y.x;
-                o.y += y.y;
-                o.z += y.z;
-                o.w += y.w;
-                *reinterpret_cast<float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq) = o;
-            }
-        }
-        __syncwarp();
     }
     static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
+using EpiResidual = EpiResidualT<3>;      // K = 768
+using EpiResidualDeep = EpiResidualT<4>;  // K = 3072: deeper TMA pipeline
 
 DH_DEVINL float gelu_tanh(float x) {
     // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))   (nn.GELU(approx="tanh"))
@@ -233,6 +248,7 @@ DH_DEVINL float gelu_tanh(float x) {
 // out[row, col] = bf16(gelu_tanh(acc * (a_scale * w_scale) + bias) * out_scale)
 // (MLP up), stored as 64-byte row segments, two rows per warp instruction.
 struct EpiGelu : EpiBase {
+    static constexpr uint32_t kStages = 3;
     static constexpr uint32_t kChunk = 32;
     static constexpr uint32_t kStagingPerWarp = 32 * 64;
     struct Params {
@@ -368,9 +384,14 @@ extern "C" uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, cons
     EpiResidual::Params p{a_scale, w_scale, bias, x, n};
     GemmShape shape{m, n, k, run_rows};
     const uint32_t tiles = ((m + 127) / 128) * (n / 256);
-    if (launch_gemm_i8<256, EpiResidual>(ta, tb, shape, p, tiles,
-                                         static_cast<cudaStream_t>(stream)) != cudaSuccess)
-        return DH_ERR_CUDA;
+    cudaError_t e;
+    if (k > 1024) {
+        EpiResidualDeep::Params pd{a_scale, w_scale, bias, x, n};
+        e = launch_gemm_i8<256, EpiResidualDeep>(ta, tb, shape, pd, tiles, static_cast<cudaStream_t>(stream));
+    } else {
+        e = launch_gemm_i8<256, EpiResidual>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream));
+    }
+    if (e != cudaSuccess) return DH_ERR_CUDA;
     return DH_OK;
 }
 

@@ -27,6 +27,7 @@ namespace dh {
 // Default hooks for epilogue policies: extra shared memory (bytes, placed
 // after the pipeline stages) initialised once per CTA by all threads.
 struct EpiBase {
+    static constexpr uint32_t kStages = 4;          // TMA pipeline depth
     static constexpr uint32_t kExtraSmem = 0;      // shared by the CTA
     static constexpr uint32_t kStagingPerWarp = 0;  // private to each epilogue warp
     template <class P>
@@ -51,10 +52,10 @@ struct GemmShape {
     const uint32_t* m_count;     // optional device row count (M_eff = min(M, *m_count))
 };
 
-template <uint32_t BN_>
+template <uint32_t BN_, uint32_t STAGES_ = 4>
 struct GemmCfg {
     static constexpr uint32_t BM = 128, BN = BN_, BK = 128;
-    static constexpr uint32_t STAGES = BN == 256 ? 4 : 6;
+    static constexpr uint32_t STAGES = STAGES_;
     static constexpr uint32_t A_BYTES = BM * BK;
     static constexpr uint32_t B_BYTES = BN * BK;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -74,11 +75,11 @@ struct GemmCfg {
 };
 
 template <uint32_t BN, class Epi>
-__global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, Epi::kStages>::THREADS, 1)
 gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_b, GemmShape shape,
                   const __grid_constant__ typename Epi::Params ep) {
-    using Cfg = GemmCfg<BN>;
+    using Cfg = GemmCfg<BN, Epi::kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -208,15 +209,17 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
         for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x) {
             const uint32_t m0 = (tile / n_tiles) * Cfg::BM;
             const uint32_t n0 = (tile % n_tiles) * BN;
-            if (!tc::mbar_wait(&accf_bar[acc], acc_phase, tc::kErrTimeoutAccFull)) break;
-            tc::tc_fence_after();
             const uint32_t row = m0 + row_in_tile;
             const bool row_ok = row < m_eff;
             const EpiCtx ctx{row, row_ok, m0 + quad * 32, m_eff, lane,
                              extra_smem + Epi::kExtraSmem + (warp - 2) * Epi::kStagingPerWarp,
                              extra_smem};
             typename Epi::TileState st;
+            // tile_begin runs before the accumulator is ready: a policy may
+            // start loads that do not depend on it (row metadata, residual).
             Epi::tile_begin(ep, st, ctx, n0 + half * kHalf);
+            if (!tc::mbar_wait(&accf_bar[acc], acc_phase, tc::kErrTimeoutAccFull)) break;
+            tc::tc_fence_after();
 #pragma unroll 1
             for (uint32_t c = 0; c < kHalf; c += kChunk) {
                 const uint32_t col_in_tile = half * kHalf + c;
@@ -252,7 +255,7 @@ template <uint32_t BN, class Epi>
 inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
                                   const GemmShape& shape, const typename Epi::Params& ep,
                                   uint32_t tiles_hint, cudaStream_t stream) {
-    using Cfg = GemmCfg<BN>;
+    using Cfg = GemmCfg<BN, Epi::kStages>;
     auto kernel = gemm_i8_tc_kernel<BN, Epi>;
     static bool configured = false;
     if (!configured) {

@@ -153,6 +153,50 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
     if (lane_id() == 0) scale[r] = sc;
 }
 
+// Wide rows (3072): two streaming passes instead of holding the row in
+// registers -- pass 1 takes the row amax, pass 2 re-reads the row (L1 / L2
+// resident, just read by this warp) and quantises.  Few registers, so many
+// rows are in flight per SM.
+__global__ void __launch_bounds__(kRowWarps * 32)
+quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __restrict__ out,
+                            float* __restrict__ scale, uint32_t rows, uint32_t cols,
+                            const uint32_t* __restrict__ run_flag) {
+    if (run_flag && *run_flag == 0u) return;
+    const uint32_t r = blockIdx.x * kRowWarps + warp_id();
+    if (r >= rows) return;
+    const uint32_t nvec = cols / 8;
+    const uint4* src = reinterpret_cast<const uint4*>(in + static_cast<uint64_t>(r) * cols);
+    __nv_bfloat162 m2 = __float2bfloat162_rn(0.f);
+#pragma unroll 4
+    for (uint32_t j = lane_id(); j < nvec; j += 32) {
+        const uint4 raw = src[j];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
+    }
+    float amax = warp_max_f32(fmaxf(__low2float(m2), __high2float(m2)));
+    const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
+    const float inv = 1.0f / sc;
+    uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * cols);
+#pragma unroll 4
+    for (uint32_t j = lane_id(); j < nvec; j += 32) {
+        const uint4 raw = __ldcs(src + j);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        uint32_t packed[2];
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            const int32_t q0 = __float2int_rn(fminf(fmaxf(f.x * inv, -127.f), 127.f));
+            const int32_t q1 = __float2int_rn(fminf(fmaxf(f.y * inv, -127.f), 127.f));
+            const uint32_t b2 = (static_cast<uint32_t>(q0) & 0xFFu) | ((static_cast<uint32_t>(q1) & 0xFFu) << 8);
+            if (e & 1u) packed[e >> 1] |= b2 << 16;
+            else packed[e >> 1] = b2;
+        }
+        dst[j] = make_uint2(packed[0], packed[1]);
+    }
+    if (lane_id() == 0) scale[r] = sc;
+}
+
 }  // namespace
 }  // namespace dh
 
@@ -200,9 +244,12 @@ uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out
     if (cols == 768)
         quant_rows_bf16_kernel<768><<<grid, kRowWarps * 32, 0, st>>>(src, inv_smooth, out, scale,
                                                                      rows, run_flag);
-    else if (cols == 3072)
+    else if (cols == 3072 && inv_smooth)
         quant_rows_bf16_kernel<3072><<<grid, kRowWarps * 32, 0, st>>>(src, inv_smooth, out, scale,
                                                                       rows, run_flag);
+    else if (cols == 3072)
+        quant_rows_bf16_wide_kernel<<<grid, kRowWarps * 32, 0, st>>>(src, out, scale, rows, cols,
+                                                                    run_flag);
     else
         return DH_ERR_UNSUPPORTED_SHAPE;
     DH_LAUNCH_CHECK();
