@@ -43,7 +43,7 @@ def run_ddpm_candidate_cache_sampler(model: MDLMEngine, input_ids: Any, *, mask_
     ids_dev = input_ids.to(model.device, non_blocking=True)
     out, _ = model.generate(ids_dev, steps=steps, seed=seed, sampling_epsilon=sampling_epsilon, graph=graph)
     ids = out.to(torch.int64).to(src_device)
-    return ids, [], model.metadata(steps)
+    return ids, model.measurements(steps, sampling_epsilon), model.metadata(steps)
 
 
 def run_ddpm_cache_sampler(model: MDLMEngine, input_ids: Any, *, mask_token_id: int, steps: int,

@@ -1,0 +1,231 @@
+"""Command line of the B200 path: the reference's subcommands for this path
+(src/diffusion_accel/cli.py) with their names and flags, backed by the
+device kernels.
+
+  trace-mdlm                  cli.py:375-396, 1209-1245 (mdlm.run_mdlm_trace)
+  validate-candidate-cache    cli.py:552-563
+  validate-rng-gumbel         cli.py:666-682
+  analyze-mdlm-prefix-drift   cli.py:724-739
+  generate-mdlm-conditioned   cli.py:769-787
+
+Differences, all forced by what a run here has:
+- no checkpoint: --model-id / --revision / --local-files-only are recorded
+  but the weights are the seeded random-init stand-in (--weights-seed);
+- no tokenizer: text is not decoded and --prefix-text is refused, while
+  --prefix-tokens takes a seeded synthetic prefix;
+- no dataset: windows are seeded synthetic ids;
+- trace-mdlm offers the two candidate-cache samplers the device loop
+  implements, and writes a JSON trace rather than the reference's
+  workload-trace IR.
+Lengths are multiples of 32 (the kernels' granule).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+from typing import Any, List, Optional
+
+DEFAULT_MODEL_ID = "kuleshov-group/mdlm-owt"
+DEFAULT_REVISION = "d0958fa851335ece6c15260ce0025f030673c0fb"
+
+
+def build_parser() -> argparse.ArgumentParser:
+    parser = argparse.ArgumentParser(prog="diffusionhard-b200")
+    sub = parser.add_subparsers(dest="command", required=True)
+
+    mdlm = sub.add_parser("trace-mdlm", help="run the MDLM candidate-cache loop on the GPU and write a trace")
+    mdlm.add_argument("--out", type=Path, required=True)
+    mdlm.add_argument("--model-id", default=DEFAULT_MODEL_ID)
+    mdlm.add_argument("--revision", default=DEFAULT_REVISION)
+    mdlm.add_argument("--device", default="cuda")
+    mdlm.add_argument("--canvas-tokens", type=int, default=64)
+    mdlm.add_argument("--steps", type=int, default=64)
+    mdlm.add_argument("--warmup", type=int, default=1)
+    mdlm.add_argument("--seed", type=int, default=0)
+    mdlm.add_argument("--sampler", choices=["ddpm-cache", "ddpm-candidate-cache"], default="ddpm-cache")
+    mdlm.add_argument("--local-files-only", action="store_true")
+    mdlm.add_argument("--batch", type=int, default=1)
+    mdlm.add_argument("--weights-seed", type=int, default=0)
+
+    cand = sub.add_parser("validate-candidate-cache",
+                          help="validate compact candidate caching against DDPM transition sampling")
+    cand.add_argument("--positions", type=int, default=64)
+    cand.add_argument("--vocabulary-size", type=int, default=50_258)
+    cand.add_argument("--probability-bits", type=int, default=16)
+    cand.add_argument("--analytic-vocabulary-size", type=int, default=257)
+    cand.add_argument("--transitions", type=int, default=16)
+    cand.add_argument("--monte-carlo-trials", type=int, default=200_000)
+    cand.add_argument("--monte-carlo-vocabulary-size", type=int, default=16)
+    cand.add_argument("--seed", type=int, default=0)
+    cand.add_argument("--maximum-total-variation", type=float, default=0.01)
+    cand.add_argument("--out", type=Path)
+    cand.add_argument("--device", default="cuda")
+
+    rng = sub.add_parser("validate-rng-gumbel", help="validate Philox vectors and the Gumbel race")
+    rng.add_argument("--distribution-trials", type=int, default=200_000)
+    rng.add_argument("--distribution-vocabulary-size", type=int, default=16)
+    rng.add_argument("--full-vocabulary-size", type=int, default=50_258)
+    rng.add_argument("--full-vocabulary-batches", type=int, default=16)
+    rng.add_argument("--full-vocabulary-batch-size", type=int, default=64)
+    rng.add_argument("--mantissa-bits", nargs="+", type=int, default=[4, 6, 8])
+    rng.add_argument("--fraction-bits", type=int, default=10)
+    rng.add_argument("--seed", type=int, default=0)
+    rng.add_argument("--maximum-distribution-tv", type=float, default=0.01)
+    rng.add_argument("--minimum-full-vocabulary-agreement", type=float, default=0.995)
+    rng.add_argument("--out", type=Path)
+    rng.add_argument("--device", default="cuda")
+
+    drift = sub.add_parser("analyze-mdlm-prefix-drift",
+                           help="measure per-layer prefix K/V drift after a suffix edit")
+    drift.add_argument("--out", type=Path)
+    drift.add_argument("--model-id", default=DEFAULT_MODEL_ID)
+    drift.add_argument("--revision", default=DEFAULT_REVISION)
+    drift.add_argument("--device", default="cuda")
+    drift.add_argument("--prefix-text")
+    drift.add_argument("--prefix-tokens", type=int, default=64)
+    drift.add_argument("--suffix-tokens", type=int, default=32)
+    drift.add_argument("--changed-suffix-tokens", type=int, default=1)
+    drift.add_argument("--warmup", type=int, default=1)
+    drift.add_argument("--timing-repeats", type=int, default=5)
+    drift.add_argument("--seed", type=int, default=0)
+    drift.add_argument("--local-files-only", action="store_true")
+    drift.add_argument("--weights-seed", type=int, default=0)
+
+    cond = sub.add_parser("generate-mdlm-conditioned",
+                          help="compare conditioned DDPM generation with retained prefix K/V")
+    cond.add_argument("--out", type=Path)
+    cond.add_argument("--model-id", default=DEFAULT_MODEL_ID)
+    cond.add_argument("--revision", default=DEFAULT_REVISION)
+    cond.add_argument("--device", default="cuda")
+    cond.add_argument("--prefix-tokens", type=int, default=64)
+    cond.add_argument("--suffix-tokens", type=int, default=32)
+    cond.add_argument("--samples", type=int, default=3)
+    cond.add_argument("--steps", type=int, default=64)
+    cond.add_argument("--seed", type=int, default=0)
+    cond.add_argument("--local-files-only", action="store_true")
+    cond.add_argument("--weights-seed", type=int, default=0)
+    return parser
+
+
+def _emit(result: Any, out: Optional[Path]) -> None:
+    rendered = json.dumps(result, indent=2, sort_keys=True)
+    if out is not None:
+        out.parent.mkdir(parents=True, exist_ok=True)
+        out.write_text(rendered + "\n", encoding="utf-8")
+    print(rendered)
+
+
+def _checkpoint_note(args: argparse.Namespace) -> dict:
+    return {"model_id": args.model_id, "revision": args.revision,
+            "weights": f"random-init N(0, 0.02) stand-in, seed {args.weights_seed} (no checkpoint on this host)"}
+
+
+def run_trace_mdlm(args: argparse.Namespace) -> dict:
+    import torch
+
+    from .api import load_mdlm, run_ddpm_cache_sampler, run_ddpm_candidate_cache_sampler
+    from .model import MDLMConfig
+
+    if args.canvas_tokens <= 0 or args.steps <= 0 or args.warmup < 0 or args.batch <= 0:
+        raise ValueError("canvas_tokens/steps/batch must be positive and warmup non-negative")
+    cfg = MDLMConfig()
+    if args.canvas_tokens > cfg.max_positions:
+        raise ValueError(f"canvas_tokens exceeds the model context length {cfg.max_positions}")
+    engine = load_mdlm(args.batch, args.canvas_tokens, seed=args.weights_seed, device=args.device)
+    mask = cfg.mask_token_id
+    ids = torch.full((args.batch, args.canvas_tokens), mask, dtype=torch.long)
+    sampler = run_ddpm_cache_sampler if args.sampler == "ddpm-cache" else run_ddpm_candidate_cache_sampler
+    for _ in range(args.warmup):
+        sampler(engine, ids, mask_token_id=mask, steps=args.steps, seed=args.seed)
+    out_ids, measurements, meta = sampler(engine, ids, mask_token_id=mask, steps=args.steps, seed=args.seed)
+    decoded = out_ids.tolist()
+    trace = {
+        "metadata": {
+            **meta, **_checkpoint_note(args),
+            "sampler": {"ddpm-cache": "official-ddpm-cache",
+                        "ddpm-candidate-cache": "distribution-equivalent-candidate-cache"}[args.sampler],
+            "device": torch.cuda.get_device_name(engine.device),
+            "parameter_count": cfg.parameter_count(),
+            "canvas_tokens": args.canvas_tokens,
+            "batch": args.batch,
+            "generated_token_ids": decoded[0] if args.batch == 1 else decoded,
+            "all_tokens_committed": not any(mask in row for row in decoded),
+            "generated_text": None,
+            "generation_device_ms": engine.generation_ms(),
+        },
+        "steps": [vars(m) for m in measurements],
+    }
+    args.out.parent.mkdir(parents=True, exist_ok=True)
+    args.out.write_text(json.dumps(trace, indent=2) + "\n", encoding="utf-8")
+    return {
+        "trace": str(args.out),
+        "steps": len(measurements),
+        "sampling_transitions": meta.get("sampling_transitions", len(measurements)),
+        "model_evaluations": meta.get("model_evaluations", len(measurements)),
+        "probability_cache_hits": meta.get("probability_cache_hits", 0),
+        "device": trace["metadata"]["device"],
+        "parameter_count": cfg.parameter_count(),
+        "all_tokens_committed": trace["metadata"]["all_tokens_committed"],
+        "generated_text": None,
+        "measured_latency_ms": sum(m.elapsed_s for m in measurements) * 1e3,
+    }
+
+
+def main(argv: Optional[List[str]] = None) -> int:
+    args = build_parser().parse_args(argv)
+    if args.command == "trace-mdlm":
+        _emit(run_trace_mdlm(args), None)
+        return 0
+    if args.command == "validate-candidate-cache":
+        from .validation import validate_candidate_cache_equivalence
+
+        result = validate_candidate_cache_equivalence(
+            positions=args.positions, vocabulary_size=args.vocabulary_size,
+            probability_bits=args.probability_bits, analytic_vocabulary_size=args.analytic_vocabulary_size,
+            transitions=args.transitions, monte_carlo_trials=args.monte_carlo_trials,
+            monte_carlo_vocabulary_size=args.monte_carlo_vocabulary_size, seed=args.seed,
+            maximum_total_variation=args.maximum_total_variation, device=args.device)
+        _emit(result, args.out)
+        return 0 if result["passed"] else 1
+    if args.command == "validate-rng-gumbel":
+        from .validation import validate_rng_and_gumbel
+
+        result = validate_rng_and_gumbel(
+            distribution_trials=args.distribution_trials,
+            distribution_vocabulary_size=args.distribution_vocabulary_size,
+            full_vocabulary_size=args.full_vocabulary_size, full_vocabulary_batches=args.full_vocabulary_batches,
+            full_vocabulary_batch_size=args.full_vocabulary_batch_size, mantissa_bits=args.mantissa_bits,
+            fraction_bits=args.fraction_bits, seed=args.seed, maximum_distribution_tv=args.maximum_distribution_tv,
+            minimum_full_vocabulary_agreement=args.minimum_full_vocabulary_agreement, device=args.device)
+        _emit(result, args.out)
+        return 0 if result["passed"] else 1
+    if args.command == "analyze-mdlm-prefix-drift":
+        if args.prefix_text is not None:
+            raise SystemExit("--prefix-text needs the GPT-2 tokenizer, which this host does not have; "
+                             "use --prefix-tokens N for a seeded synthetic prefix")
+        from .prefix import analyze_mdlm_prefix_drift
+
+        result = analyze_mdlm_prefix_drift(
+            prefix_tokens=args.prefix_tokens, suffix_tokens=args.suffix_tokens,
+            changed_suffix_tokens=args.changed_suffix_tokens, warmup=args.warmup,
+            timing_repeats=args.timing_repeats, seed=args.seed, weights_seed=args.weights_seed,
+            device=args.device)
+        result.update(_checkpoint_note(args))
+        _emit(result, args.out)
+        return 0
+    if args.command == "generate-mdlm-conditioned":
+        from .conditioned import evaluate_conditioned_mdlm_ddpm
+
+        result = evaluate_conditioned_mdlm_ddpm(
+            prefix_tokens=args.prefix_tokens, suffix_tokens=args.suffix_tokens, samples=args.samples,
+            steps=args.steps, seed=args.seed, weights_seed=args.weights_seed, device=args.device)
+        result.update(_checkpoint_note(args))
+        _emit(result, args.out)
+        return 0
+    raise AssertionError(args.command)  # argparse restricts the choices
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

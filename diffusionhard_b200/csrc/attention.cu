@@ -109,8 +109,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
     const uint32_t warp = warp_id(), lane = lane_id();
-    const uint32_t n_kv = args.kv_len / kTile;
-    const uint32_t n_qt = args.q_len / kTile;
+    const uint32_t n_kv = (args.kv_len + kTile - 1) / kTile;
+    const uint32_t n_qt = (args.q_len + kTile - 1) / kTile;
+    // keys of the last tile that exist (kTile when kv_len is a multiple of it)
+    const uint32_t kv_rem = args.kv_len - (n_kv - 1) * kTile;
     const uint32_t total = args.sequences * kHeads * n_qt;
 
     if (warp == 0 && lane == 0) {
@@ -252,6 +254,14 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                 tc::tmem_ld_wait();
                 tc::tc_fence_before();
                 tc::mbar_arrive(&bars[kSFree]);
+                // ragged key tail: keys past kv_len score -inf (p = 0); their
+                // K rows are whatever the tile read, V rows are finite (zero
+                // padding or other rows), so 0 * V adds nothing.
+                if (j + 1 == n_kv && kv_rem != kTile) {
+#pragma unroll
+                    for (uint32_t e = 0; e < 128; ++e)
+                        if (e >= kv_rem) sv[e] = 0xFF800000u;
+                }
                 // row max with 8 independent partial maxima (short dependency chains)
                 float pm[8];
 #pragma unroll
@@ -337,6 +347,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[kOFree]);
             const float inv_l = 1.0f / l;
+            if (item.q_tile * kTile + r >= args.q_len) continue;  // ragged query tail
             const uint64_t tok = static_cast<uint64_t>(item.seq) * args.q_len + item.q_tile * kTile + r;
             __nv_bfloat16* dst = args.out + tok * (kHeads * kDh) + item.head * kDh;
 #pragma unroll
@@ -374,7 +385,7 @@ extern "C" uint32_t dh_attention(const void* q, const void* k, const void* vt, v
     if (!q || !k || !vt || !out) return DH_ERR_NULL_POINTER;
     if (sequences == 0 || q_len == 0 || kv_len == 0 || kv_stride < kv_len)
         return DH_ERR_INVALID_ARGUMENT;
-    if (q_len % kTile != 0 || kv_len % kTile != 0 || kv_stride % 8 != 0)
+    if (q_len % 32 != 0 || kv_len % 32 != 0 || kv_stride % 8 != 0)
         return DH_ERR_UNSUPPORTED_SHAPE;
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
          reinterpret_cast<uintptr_t>(vt) | reinterpret_cast<uintptr_t>(out)) & 15u)
@@ -399,7 +410,7 @@ extern "C" uint32_t dh_attention(const void* q, const void* k, const void* vt, v
         int v = 0;
         if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
     }
-    const uint64_t items = static_cast<uint64_t>(sequences) * kHeads * (q_len / kTile);
+    const uint64_t items = static_cast<uint64_t>(sequences) * kHeads * ((q_len + kTile - 1) / kTile);
     const uint32_t grid = static_cast<uint32_t>(std::min<uint64_t>(items, 2ull * sms));
     attention_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, a);
     DH_LAUNCH_CHECK();

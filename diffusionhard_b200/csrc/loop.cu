@@ -73,7 +73,7 @@ loop_plan_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t final_pass,
 // their per-row results slot by slot.
 __global__ void __launch_bounds__(1024)
 loop_select_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t seed, uint32_t seq_offset,
-                   uint64_t threshold, uint32_t final_pass, const uint64_t* __restrict__ active,
+                   uint32_t position_offset, uint64_t threshold, uint32_t final_pass, const uint64_t* __restrict__ active,
                    const uint32_t* __restrict__ eval_id, uint32_t* __restrict__ sel_rows,
                    uint32_t* __restrict__ sel_pos, uint32_t* __restrict__ sel_key,
                    uint32_t* __restrict__ sel_eval, uint32_t* __restrict__ sel_count) {
@@ -95,8 +95,9 @@ loop_select_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t seed, uint32_
                 if (final_pass) {
                     take = true;
                 } else {
-                    Philox4 r = philox4x32_10(p >> 2, 0u, step, 1u, seed, seq_offset + b);
-                    take = static_cast<uint64_t>(philox_lane(r, p & 3u)) < threshold;
+                    const uint32_t gp = position_offset + p;  // canvas position
+                    Philox4 r = philox4x32_10(gp >> 2, 0u, step, 1u, seed, seq_offset + b);
+                    take = static_cast<uint64_t>(philox_lane(r, gp & 3u)) < threshold;
                 }
             }
         }
@@ -119,7 +120,7 @@ loop_select_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t seed, uint32_
         if (take) {
             const uint32_t slot = base + warp_off[warp_id()] + __popc(mask & ((1u << lane_id()) - 1u));
             sel_rows[slot] = b * L + p;
-            sel_pos[slot] = p;
+            sel_pos[slot] = position_offset + p;
             sel_key[slot] = seq_offset + b;
             sel_eval[slot] = eval_id[b];
         }
@@ -221,7 +222,7 @@ uint32_t dh_loop_plan(uint32_t sequences, uint32_t positions, uint32_t step, uin
 }
 
 uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t seed,
-                        uint32_t seq_offset, uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
+                        uint32_t seq_offset, uint32_t position_offset, uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
                         const uint32_t* eval_id, uint32_t* sel_rows, uint32_t* sel_pos,
                         uint32_t* sel_key, uint32_t* sel_eval, uint32_t* sel_count, void* stream) {
     if (threshold_q32 > DH_REVEAL_PROBABILITY_ONE_Q32) return DH_CAND_INVALID_THRESHOLD;
@@ -229,7 +230,8 @@ uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, u
         return DH_ERR_NULL_POINTER;
     if (sequences == 0 || positions == 0) return DH_ERR_INVALID_ARGUMENT;
     loop_select_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
-        sequences, positions, step, seed, seq_offset, threshold_q32, final_pass, active, eval_id,
+        sequences, positions, step, seed, seq_offset, position_offset, threshold_q32, final_pass, active,
+        eval_id,
         sel_rows, sel_pos, sel_key, sel_eval, sel_count);
     DH_LAUNCH_CHECK();
     return DH_OK;

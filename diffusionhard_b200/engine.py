@@ -22,7 +22,7 @@ import numpy as np
 
 from . import _lib
 from .model import MDLMConfig, QuantizedMDLM
-from .sampler import hardware_candidate_cache_bytes, reveal_thresholds_q32
+from .sampler import NOISE_EPSILON, MDLMStepMeasurement, hardware_candidate_cache_bytes, reveal_thresholds_q32
 
 
 class _DevLinear:
@@ -57,8 +57,8 @@ class MDLMEngine:
         if cfg.hidden != 768 or cfg.heads != 12 or cfg.head_dim != 64 or cfg.mlp != 3072:
             raise ValueError("the kernels are specialised for d=768, 12x64 heads, MLP 3072")
         kv_len = seq_len if kv_len is None else kv_len
-        if seq_len % 128 or kv_len % 128:
-            raise ValueError("seq_len and kv_len must be multiples of 128")
+        if seq_len % 32 or kv_len % 32 or kv_offset % 32:
+            raise ValueError("seq_len, kv_len and kv_offset must be multiples of 32")
         if pos_offset + seq_len > cfg.max_positions or kv_offset + seq_len > max(kv_len, kv_offset + seq_len):
             raise ValueError("rotary positions exceed the model length")
         self.cfg, self.qm = cfg, qm
@@ -79,8 +79,10 @@ class MDLMEngine:
         self.act_scale = torch.empty(M, dtype=torch.float32, device=d)
         self.q = torch.empty((batch, H, seq_len, 64), dtype=bf16, device=d)
         if kv_buffers is None:
-            k = torch.empty((batch, H, kv_len, 64), dtype=bf16, device=d)
-            vt = torch.empty((batch, H, 64, kv_len), dtype=bf16, device=d)
+            # zeros: attention reads whole 128-key tiles and needs finite V
+            # past kv_len (the keys there are masked)
+            k = torch.zeros((batch, H, kv_len, 64), dtype=bf16, device=d)
+            vt = torch.zeros((batch, H, 64, kv_len), dtype=bf16, device=d)
             kv_buffers = [(k, vt)] * len(self.blocks)
         self.kv_buffers = kv_buffers
         self.kv_stride = kv_buffers[0][0].shape[2]
@@ -109,7 +111,9 @@ class MDLMEngine:
         self.head_vocab_offset = 0  # global id of the first head row held here (vocab-sharded head)
         self.head_group = None      # process group reducing the sharded head, or None
         self.head_reduce = None     # callable(packed) merging shard results (testing / custom groups)
+        self.pre_forward = None     # callable(fwd_rows) enqueued before each transition's forward
         self._graphs: Dict[Any, Any] = {}
+        self._events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         self.launches_per_forward = 1 + 9 * len(self.blocks)
 
     def shard_head(self, v0: int, v1: int, group: Any = None, reduce: Any = None) -> None:
@@ -129,11 +133,12 @@ class MDLMEngine:
 
     @staticmethod
     def kv_cache(qm: QuantizedMDLM, batch: int, kv_stride: int, device: Any = "cuda") -> List[tuple]:
-        """Per-block K [B, 12, kv_stride, 64] and V^T [B, 12, 64, kv_stride] (bf16)."""
+        """Per-block K [B, 12, kv_stride, 64] and V^T [B, 12, 64, kv_stride]
+        (bf16, zero-filled: positions not yet written must hold finite V)."""
         import torch
 
-        return [(torch.empty((batch, 12, kv_stride, 64), dtype=torch.bfloat16, device=device),
-                 torch.empty((batch, 12, 64, kv_stride), dtype=torch.bfloat16, device=device))
+        return [(torch.zeros((batch, 12, kv_stride, 64), dtype=torch.bfloat16, device=device),
+                 torch.zeros((batch, 12, 64, kv_stride), dtype=torch.bfloat16, device=device))
                 for _ in qm.blocks]
 
     # ------------------------------------------------------------ forward
@@ -190,6 +195,23 @@ class MDLMEngine:
                   self._p(rows_count) if rows_count is not None else None, None, s)
         return self.head_q, self.head_scale
 
+    def logits(self) -> Any:
+        """fp32 logits [B, L, V] of the last forward: a debug / drift-analysis
+        path (the samplers never materialise logits).  int32 accumulators of
+        the int8 head from the tensor-core GEMM, then the reference dequant
+        out = fp32(acc * fp64(a_scale * w_scale) + bias)
+        (fixed_mlp.quantized_linear, fixed_mlp.py:120-136)."""
+        torch = self.torch
+        hq, hs = self.final_hidden_q()
+        h = self.head
+        V = h.out_features
+        acc = torch.empty((self.M, V), dtype=torch.int32, device=self.device)
+        _lib.call("dh_gemm_i8_s32", self._p(hq), 768, self._p(h.w), 768, self._p(acc), V, self.M, V, 768,
+                  _lib.stream_handle())
+        combined = (hs[:, None] * h.w_scale[None, :]).double()
+        out = (acc.double() * combined + h.bias.double()[None, :]).float()
+        return out.view(self.B, self.L, V)
+
     def head_argmax(self, rows: int, mode: int, rows_count: Any = None, row_position: Any = None,
                     row_key_hi: Any = None, row_eval: Any = None, key_lo: int = 0,
                     out_ids: Any = None, out_scores: Any = None, const_eval: int = 0) -> None:
@@ -214,8 +236,11 @@ class MDLMEngine:
         kk = min(k, steps - 1)
         call("dh_loop_plan", B, L, kk, steps, final, p(self.active), p(self.need_eval), p(self.eval_id),
              p(self.fwd_rows), p(self.sel_count), p(self.counters), s)
+        if self.pre_forward is not None:
+            self.pre_forward(self.fwd_rows)
         self.forward(run_rows=self.fwd_rows)
-        call("dh_loop_select", B, L, kk, seed, self.seq_offset, 0 if final else threshold_q32, final,
+        call("dh_loop_select", B, L, kk, seed, self.seq_offset, self.pos_offset, 0 if final else threshold_q32,
+             final,
              p(self.active), p(self.eval_id), p(self.sel_rows), p(self.sel_pos), p(self.sel_key),
              p(self.sel_eval), p(self.sel_count), s)
         self.final_hidden_q(self.sel_rows, self.sel_count)
@@ -270,10 +295,42 @@ class MDLMEngine:
                 with torch.cuda.graph(g):
                     self._enqueue_generation(steps, seed, thresholds)
                 self._graphs[key] = g
+            self._events[0].record()
             g.replay()
+            self._events[1].record()
         else:
+            self._events[0].record()
             self._enqueue_generation(steps, seed, thresholds)
+            self._events[1].record()
         return self.tokens.view(self.B, self.L), {}
+
+    def generation_ms(self) -> float:
+        """Device time of the last generate() (the loop only, CUDA events)."""
+        self._events[1].synchronize()
+        return float(self._events[0].elapsed_time(self._events[1]))
+
+    def measurements(self, steps: int, sampling_epsilon: float = 1e-5) -> list:
+        """The reference's per-evaluation records of the last generation
+        (mdlm.py:1133-1200): one MDLMStepMeasurement per transition that ran a
+        model evaluation, then the final greedy pass when masks remained.
+        sigma_t = -log1p(-(1 - 1e-3) t_k) in float32 as the reference computes
+        it.  The loop runs as one device program, so elapsed_s is the
+        generation's device time divided evenly over the evaluations."""
+        torch = self.torch
+        meta = self.metadata(steps)
+        counters = self.counters.view(steps, 3).cpu().tolist()
+        n = meta["sampling_transitions"]
+        t = torch.linspace(1.0, sampling_epsilon, steps + 1)
+        sigma = (-torch.log1p(-(1 - NOISE_EPSILON) * t)).tolist()
+        evaluations = max(1, meta["model_evaluations"])
+        per_eval = self.generation_ms() / 1e3 / evaluations
+        out = [MDLMStepMeasurement(k, counters[k][0], counters[k][1], per_eval, float(sigma[k]))
+               for k in range(n) if counters[k][2]]
+        remaining = counters[n - 1][0] - counters[n - 1][1] if n else 0
+        if remaining > 0:
+            final_sigma = float(-torch.log1p(-(1 - NOISE_EPSILON) * torch.tensor([sampling_epsilon])).item())
+            out.append(MDLMStepMeasurement(n, remaining, remaining, per_eval, final_sigma))
+        return out
 
     def metadata(self, steps: int) -> dict:
         counters = self.counters.view(steps, 3).cpu().tolist()

@@ -181,3 +181,77 @@ def run_candidate_cache_sampler_f32(
         "candidate_id_bytes": id_bytes,
     }
     return ids, [], metadata
+
+
+def _u32(x: Any, device: Any) -> Any:
+    """uint32 values (python ints / numpy / torch) as a device int32 tensor of
+    the same bit patterns."""
+    import numpy as np
+    import torch
+
+    if isinstance(x, torch.Tensor):
+        x = x.cpu().numpy()
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.int64).astype(np.uint32).view(np.int32))
+    return torch.from_numpy(a).to(device)
+
+
+def philox4x32_10(counters: Any, keys: Any, device: Any = "cuda") -> Any:
+    """Philox4x32-10 blocks on the GPU (dh_philox4x32_10): counters [n, 4] and
+    keys [n, 2] of uint32 values -> int64 tensor [n, 4] of the output words."""
+    import torch
+
+    c = _u32(counters, device).reshape(-1, 4).contiguous()
+    k = _u32(keys, device).reshape(-1, 2).contiguous()
+    if c.shape[0] != k.shape[0]:
+        raise ValueError("one key per counter")
+    out = torch.empty_like(c)
+    n = c.shape[0]
+    for i in range(0, n, 1 << 30):
+        j = min(n, i + (1 << 30))
+        _lib.call("dh_philox4x32_10", _lib.ptr(c[i:j]), _lib.ptr(k[i:j]), _lib.ptr(out[i:j]), j - i,
+                  _lib.stream_handle())
+    return out.to(torch.int64) & 0xFFFFFFFF
+
+
+def noisy_argmax_f32(logits: Any, mask_token_id: int, *, row_position: Any, row_key_hi: Any,
+                     row_eval: Any, key_lo: int, stream_id: int = 0) -> Any:
+    """Gumbel-max race of fp32 logit rows on the GPU (dh_noisy_argmax_f32):
+    the token with the largest round(logit * 1024) + Gumbel_Q10(word), word =
+    philox((v/4, row_position, row_eval, stream_id), (key_lo, row_key_hi))[v%4],
+    the mask token excluded, lowest id on ties.  Any number of rows (calls of
+    at most 65,535 rows).  Returns int32 ids [rows] on the logits' device."""
+    import torch
+
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_cuda:
+        raise ValueError("logits must be a CUDA float32 [rows, vocab] tensor")
+    logits = logits.contiguous()
+    rows, vocab = logits.shape
+    dev = logits.device
+    pos, khi, ev = (_u32(a, dev) for a in (row_position, row_key_hi, row_eval))
+    if not (pos.numel() == khi.numel() == ev.numel() == rows):
+        raise ValueError("one position / key / evaluation per row")
+    ids = torch.empty(rows, dtype=torch.int32, device=dev)
+    chunk = 65535
+    ws_bytes = int(_lib.lib().dh_noisy_argmax_workspace_size(min(rows, chunk), vocab))
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    for i in range(0, rows, chunk):
+        j = min(rows, i + chunk)
+        _lib.call("dh_noisy_argmax_f32", _lib.ptr(logits[i:j]), vocab, j - i, vocab, mask_token_id,
+                  _lib.ptr(pos[i:j]), _lib.ptr(khi[i:j]), _lib.ptr(ev[i:j]), key_lo & 0xFFFFFFFF, stream_id,
+                  _lib.ptr(ids[i:j]), None, _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+    return ids
+
+
+def reveal_words(sequences: int, positions: int, step: int, seed: int, seq_offset: int = 0,
+                 device: Any = "cuda") -> Any:
+    """Reveal words of the loop, philox((p/4, 0, step, 1), (seed, b))[p%4], as
+    int64 [sequences, positions] (computed on the GPU)."""
+    import numpy as np
+
+    groups = (positions + 3) // 4
+    b = np.repeat(np.arange(sequences, dtype=np.int64) + seq_offset, groups)
+    g = np.tile(np.arange(groups, dtype=np.int64), sequences)
+    counters = np.stack([g, np.zeros_like(g), np.full_like(g, step), np.ones_like(g)], axis=1)
+    keys = np.stack([np.full_like(g, seed), b], axis=1)
+    words = philox4x32_10(counters, keys, device)
+    return words.view(sequences, groups * 4)[:, :positions]

@@ -262,7 +262,10 @@ uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
 /* Bidirectional attention softmax(Q K^T / 8) V (K5) over the first kv_len
  * keys of K / V^T buffers of kv_stride rows per (sequence, head); bf16 in,
  * fp32 softmax, bf16 out [sequences * q_len, 768].  q_len, kv_len multiples
- * of 128, kv_stride a multiple of 8. */
+ * of 32, kv_stride a multiple of 8.  Keys are read in tiles of 128: when
+ * kv_len is not a multiple of 128, the V^T columns from kv_len up to the next
+ * multiple of 128 that lie inside kv_stride must hold finite values (zero-fill
+ * the buffers once); those keys are masked. */
 uint32_t dh_attention(const void* q, const void* k, const void* vt, void* out, uint32_t sequences,
                       uint32_t q_len, uint32_t kv_len, uint32_t kv_stride, const uint32_t* run_flag,
                       void* stream);
@@ -326,6 +329,9 @@ uint32_t dh_output_head_int8(const int8_t* hidden, const int8_t* weights,
  * dh_ln_smooth_quant (gathering sel_rows) -> dh_head_argmax_i8 (mode 1, rows
  * limited by sel_count) -> dh_loop_commit.  final_pass = 1 runs the greedy
  * pass of mdlm.py:1177-1200 over every still-masked position.
+ * Randomness is keyed by the global sequence (seq_offset + b) and the canvas
+ * position (position_offset + p): a suffix-only loop over positions
+ * [P, P + S) draws the same words as a loop over the whole [0, P + S) canvas.
  */
 uint32_t dh_loop_init(const int32_t* input_ids, uint32_t sequences, uint32_t positions,
                       uint32_t mask_token_id, uint32_t steps, int32_t* tokens, uint64_t* active,
@@ -335,7 +341,7 @@ uint32_t dh_loop_plan(uint32_t sequences, uint32_t positions, uint32_t step, uin
                       uint32_t* eval_id, uint32_t* fwd_rows, uint32_t* sel_count,
                       int32_t* counters, void* stream);
 uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t seed,
-                        uint32_t seq_offset, uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
+                        uint32_t seq_offset, uint32_t position_offset, uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
                         const uint32_t* eval_id, uint32_t* sel_rows, uint32_t* sel_pos,
                         uint32_t* sel_key, uint32_t* sel_eval, uint32_t* sel_count, void* stream);
 uint32_t dh_loop_commit(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t steps,

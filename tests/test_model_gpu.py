@@ -42,10 +42,11 @@ def _ids(B, L, seed, mask_every=3, vocab=999):
     return ids
 
 
-def test_forward_matches_oracle(cuda, small_model):
+@pytest.mark.parametrize("L", [256, 64, 96])
+def test_forward_matches_oracle(cuda, small_model, L):
     torch = cuda
     qm = small_model
-    B, L = 2, 256
+    B = 2
     eng = MDLMEngine(qm, B, L)
     ids = _ids(B, L, 3)
     eng.tokens.copy_(ids.view(-1).to(torch.int32))
@@ -188,13 +189,47 @@ def test_attention_matches_sdpa(cuda):
     assert _device_error() == 0
 
 
-def test_loop_teacher_forced_bit_exact(cuda, small_model):
+@pytest.mark.parametrize("Lq,P", [(64, 0), (96, 0), (160, 0), (96, 32), (64, 96)])
+def test_attention_ragged_lengths(cuda, Lq, P):
+    """q_len / kv_len multiples of 32 but not of 128: keys past kv_len are
+    masked (they are set huge here, so a leak would show), rows past q_len
+    are not written (a guard region after the output stays untouched)."""
+    torch = cuda
+    import torch.nn.functional as F
+
+    B, H = 3, 12
+    kv_len = P + Lq
+    kv_stride = ((kv_len + 127) // 128) * 128 + 32  # padding inside the stride
+    g = torch.Generator(device="cuda").manual_seed(Lq + P)
+    q = torch.randn((B, H, Lq, 64), device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn((B, H, kv_stride, 64), device="cuda", generator=g).to(torch.bfloat16)
+    vt = torch.randn((B, H, 64, kv_stride), device="cuda", generator=g).to(torch.bfloat16)
+    k[:, :, kv_len:] = 50.0  # would dominate every softmax row if not masked
+    vt[:, :, :, kv_len:] = 1000.0
+    guard = 4096
+    buf = torch.full((B * Lq * 768 + guard,), 7.0, dtype=torch.bfloat16, device="cuda")
+    out = buf[: B * Lq * 768].view(B * Lq, 768)
+    _lib.call("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt), _lib.ptr(out), B, Lq, kv_len,
+              kv_stride, None, None)
+    torch.cuda.synchronize()
+    ref = F.scaled_dot_product_attention(q.float(), k[:, :, :kv_len].float(),
+                                         vt[:, :, :, :kv_len].float().transpose(-1, -2))
+    got = out.float().view(B, Lq, H, 64).transpose(1, 2)
+    assert ((got - ref).norm() / ref.norm()).item() < 1e-2
+    assert bool((buf[B * Lq * 768:] == 7.0).all())
+    assert _device_error() == 0
+    assert _lib.raw("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt), _lib.ptr(out), B, 48, kv_len,
+                    kv_stride, None, None) == 103
+
+
+@pytest.mark.parametrize("L", [256, 96])
+def test_loop_teacher_forced_bit_exact(cuda, small_model, L):
     """Each transition: the revealed row set equals the oracle's reveal
     decision on the GPU's state, and every revealed row's candidate equals the
     oracle's noisy argmax on the GPU's own int8 hidden row."""
     torch = cuda
     qm = small_model
-    B, L, steps, seed = 2, 256, 12, 5
+    B, steps, seed = 2, 12, 5
     eng = MDLMEngine(qm, B, L)
     eng.seq_offset = 3
     mask = SMALL.mask_token_id
