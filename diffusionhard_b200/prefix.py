@@ -31,13 +31,14 @@ def tensor_drift_metrics(reference: Any, changed: Any) -> Dict[str, object]:
 
     if tuple(reference.shape) != tuple(changed.shape):
         raise ValueError("drift tensors must have the same shape")
-    reference = reference.detach().float().cpu()
-    changed = changed.detach().float().cpu()
+    # computed where the tensors live (fp32), so large device tensors stay put
+    reference = reference.detach().float()
+    changed = changed.detach().float().to(reference.device)
     difference = changed - reference
     reference_rms = reference.square().mean().sqrt()
     rmse = difference.square().mean().sqrt()
     denominator = reference.flatten().norm() * changed.flatten().norm()
-    cosine = torch.tensor(1.0)
+    cosine = torch.tensor(1.0, device=reference.device)
     if float(denominator.item()) > 0:
         cosine = (torch.dot(reference.flatten(), changed.flatten()) / denominator).clamp(-1.0, 1.0)
     return {
