@@ -5,6 +5,7 @@
 // src/diffusion_accel/fixed_mlp.py:55-62; the 4x8x32 HLS MAC tile,
 // hls/tensor_engine/int8_mac_tile.cpp:7-41) -- bit-exact by construction.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "gemm_tc.cuh"
 #include "tmap.h"
@@ -82,7 +83,7 @@ struct EpiQKV : EpiBase {
         uint32_t kv_offset;     // where this forward's rows go in K / V
         __nv_bfloat16* q;
         __nv_bfloat16* k;
-        __nv_bfloat16* vt;
+        __half* vt;  // V^T, f16
     };
     struct TileState {};
     static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
@@ -156,11 +157,11 @@ struct EpiQKV : EpiBase {
             // V^T: for each channel d the warp's 32 consecutive tokens form
             // one 64-byte run, so lane = token stores are already coalesced.
             if (ctx.row_ok) {
-                __nv_bfloat16* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride +
+                __half* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride +
                                      t + p.kv_offset;
 #pragma unroll
                 for (uint32_t d = 0; d < 64; ++d)
-                    dst[static_cast<uint64_t>(d) * p.kv_stride] = __float2bfloat16_rn(y[d]);
+                    dst[static_cast<uint64_t>(d) * p.kv_stride] = __float2half_rn(y[d]);
             }
         }
     }
@@ -360,7 +361,7 @@ extern "C" uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, cons
     if (st != DH_OK) return st;
     EpiQKV::Params p{a_scale, w_scale, bias, rope_cos, rope_sin, v_scale, seq_len, pos_offset, kv_stride,
                      kv_offset, static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k),
-                     static_cast<__nv_bfloat16*>(vt)};
+                     static_cast<__half*>(vt)};
     GemmShape shape{m, 2304, 768, run_rows};
     const uint32_t tiles = ((m + 127) / 128) * 9;
     if (launch_gemm_i8<256, EpiQKV>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=

@@ -123,6 +123,12 @@ DH_DEVINL void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 
+DH_DEVINL uint32_t tmem_ld_32x32b_x1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+    return r;
+}
+
 DH_DEVINL void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 16 consecutive columns (stores) -- used to stage P for attention.
@@ -184,6 +190,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32() {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// kind::f16 with f16 A and B, f32 accumulate.
+template <uint32_t M, uint32_t N>
+__host__ __device__ constexpr uint32_t idesc_f16_f32() {
+    return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, one instruction (M x N x 32 for i8,
 // M x N x 16 for bf16).  Issued by a single thread.
 DH_DEVINL void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -207,6 +219,19 @@ DH_DEVINL void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint3
 }
 
 // Arrive on `bar` when all previously issued tcgen05 ops of this thread finish.
+// D[tmem] (+)= A[tmem] * B[smem]^T (kind::f16): A is M x 16 with row m in
+// TMEM lane m and its 16 elements packed two per column in 8 consecutive
+// columns starting at a_tmem.  Issued by a single thread.
+DH_DEVINL void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 DH_DEVINL void mma_commit(uint64_t* bar) {
     asm volatile(
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(

@@ -82,7 +82,7 @@ class MDLMEngine:
             # zeros: attention reads whole 128-key tiles and needs finite V
             # past kv_len (the keys there are masked)
             k = torch.zeros((batch, H, kv_len, 64), dtype=bf16, device=d)
-            vt = torch.zeros((batch, H, 64, kv_len), dtype=bf16, device=d)
+            vt = torch.zeros((batch, H, 64, kv_len), dtype=torch.float16, device=d)
             kv_buffers = [(k, vt)] * len(self.blocks)
         self.kv_buffers = kv_buffers
         self.kv_stride = kv_buffers[0][0].shape[2]
@@ -133,12 +133,12 @@ class MDLMEngine:
 
     @staticmethod
     def kv_cache(qm: QuantizedMDLM, batch: int, kv_stride: int, device: Any = "cuda") -> List[tuple]:
-        """Per-block K [B, 12, kv_stride, 64] and V^T [B, 12, 64, kv_stride]
-        (bf16, zero-filled: positions not yet written must hold finite V)."""
+        """Per-block K [B, 12, kv_stride, 64] bf16 and V^T [B, 12, 64, kv_stride]
+        f16 (zero-filled: positions not yet written must hold finite V)."""
         import torch
 
         return [(torch.zeros((batch, 12, kv_stride, 64), dtype=torch.bfloat16, device=device),
-                 torch.zeros((batch, 12, 64, kv_stride), dtype=torch.bfloat16, device=device))
+                 torch.zeros((batch, 12, 64, kv_stride), dtype=torch.float16, device=device))
                 for _ in qm.blocks]
 
     # ------------------------------------------------------------ forward

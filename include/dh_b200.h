@@ -233,8 +233,8 @@ uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out
 
 /* QKV projection (K4): [m, 768] x [2304, 768]^T, dequant, rotate-half rotary
  * on q and k at position (row % seq_len) + pos_offset (mlx_mdlm.py:298-329),
- * written as bf16 Q [B, 12, seq_len, 64], K [B, 12, kv_stride, 64] and V^T
- * [B, 12, 64, kv_stride] at key offset kv_offset -- the layout of a cached
+ * written as bf16 Q [B, 12, seq_len, 64] and K [B, 12, kv_stride, 64] and f16
+ * V^T [B, 12, 64, kv_stride] at key offset kv_offset -- the layout of a cached
  * prefix followed by the active rows (prefix_drift.py:155-238).
  * rope_cos / rope_sin: [positions, 32] fp32.  v_scale (768, may be NULL)
  * multiplies V per channel: with the SmoothQuant 1/s of the attention-out
@@ -260,8 +260,8 @@ uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
                       uint32_t k, const uint32_t* run_rows, void* stream);
 
 /* Bidirectional attention softmax(Q K^T / 8) V (K5) over the first kv_len
- * keys of K / V^T buffers of kv_stride rows per (sequence, head); bf16 in,
- * fp32 softmax, bf16 out [sequences * q_len, 768].  q_len, kv_len multiples
+ * keys of K / V^T buffers of kv_stride rows per (sequence, head); Q, K bf16,
+ * V^T f16, fp32 scores and row sums, P in f16, bf16 out [sequences * q_len, 768].  q_len, kv_len multiples
  * of 32, kv_stride a multiple of 8.  Keys are read in tiles of 128: when
  * kv_len is not a multiple of 128, the V^T columns from kv_len up to the next
  * multiple of 128 that lie inside kv_stride must hold finite values (zero-fill

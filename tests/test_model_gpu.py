@@ -175,7 +175,7 @@ def test_attention_matches_sdpa(cuda):
     g = torch.Generator(device="cuda").manual_seed(0)
     q = torch.randn((B, H, Lq, 64), device="cuda", generator=g).to(torch.bfloat16)
     k = torch.randn((B, H, kv_stride, 64), device="cuda", generator=g).to(torch.bfloat16)
-    vt = torch.randn((B, H, 64, kv_stride), device="cuda", generator=g).to(torch.bfloat16)
+    vt = torch.randn((B, H, 64, kv_stride), device="cuda", generator=g).to(torch.float16)
     k[:, :, :P] *= 3  # a prefix with larger scores exercises the rescale path
     for kv_len in (Lq, kv_stride):
         out = torch.empty((B * Lq, 768), dtype=torch.bfloat16, device="cuda")
@@ -203,7 +203,7 @@ def test_attention_ragged_lengths(cuda, Lq, P):
     g = torch.Generator(device="cuda").manual_seed(Lq + P)
     q = torch.randn((B, H, Lq, 64), device="cuda", generator=g).to(torch.bfloat16)
     k = torch.randn((B, H, kv_stride, 64), device="cuda", generator=g).to(torch.bfloat16)
-    vt = torch.randn((B, H, 64, kv_stride), device="cuda", generator=g).to(torch.bfloat16)
+    vt = torch.randn((B, H, 64, kv_stride), device="cuda", generator=g).to(torch.float16)
     k[:, :, kv_len:] = 50.0  # would dominate every softmax row if not masked
     vt[:, :, :, kv_len:] = 1000.0
     guard = 4096
