@@ -125,7 +125,7 @@ DH_DEVINL float2 exp2_poly2(float2 x) {
 
 // Pairs of P computed on the FMA pipe instead of the MUFU: pair q of each
 // group of 4 (8 keys) uses the polynomial when bit q of this mask is set.
-constexpr uint32_t kPolyPairMask = 0x0u;
+constexpr uint32_t kPolyPairMask = 0x1u;
 
 // Hardware base-2 exponential of two f16 values at once (MUFU).
 DH_DEVINL uint32_t ex2_f16x2(uint32_t x) {

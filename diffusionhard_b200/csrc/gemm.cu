@@ -42,6 +42,30 @@ struct EpiStoreI32 : EpiBase {
     static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
 
+// 16-byte global -> shared copy that bypasses the registers (cp.async).
+DH_DEVINL void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+                 "l"(gmem)
+                 : "memory");
+}
+DH_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// 128 consecutive floats from each of up to three per-column vectors (the
+// warp's columns; a null source leaves its 512-byte slot unset) into dst.
+// Issued when a tile starts, so the chunks read them from shared memory
+// instead of each issuing broadcast global loads.
+DH_DEVINL void stage_columns(uint8_t* dst, uint32_t lane, const float* a, const float* b, const float* c) {
+    __syncwarp();  // the previous tile's chunks finished reading the slots
+    if (a) cp_async16(dst + lane * 16, a + lane * 4);
+    if (b) cp_async16(dst + 512 + lane * 16, b + lane * 4);
+    if (c) cp_async16(dst + 1024 + lane * 16, c + lane * 4);
+    cp_async_wait_all();
+    __syncwarp();
+}
+
+// Barrier of the two epilogue warps that cover lane quadrant q (ids 1-4).
+DH_DEVINL void pair_sync(uint32_t q) { asm volatile("bar.sync %0, 64;" ::"r"(q + 1u) : "memory"); }
+
 // y = acc * (a_scale[row] * w_scale[col]) + bias[col]   (fp32)
 DH_DEVINL float dequant(uint32_t acc, float ab, float w, float b) {
     return __fmaf_rn(static_cast<float>(static_cast<int32_t>(acc)), ab * w, b);
@@ -67,9 +91,15 @@ DH_DEVINL uint32_t pack_bf16x2(float a, float b) {
 // its Q / K block is 4 KB contiguous and its V^T block is 64 runs of 64 bytes:
 // both are written through the warp's staging buffer with full-line stores.
 struct EpiQKV : EpiBase {
-    static constexpr uint32_t kStages = 3;  // leaves L1 room for the per-column / rotary tables
+    static constexpr uint32_t kStages = 3;
     static constexpr uint32_t kChunk = 64;
-    static constexpr uint32_t kStagingPerWarp = 32 * 128;
+    // per warp: output staging (4 KB), then its 128 columns' w_scale, bias and
+    // v_scale (512 B each)
+    static constexpr uint32_t kStagingPerWarp = 32 * 128 + 3 * 512;
+    // Rotary rows of each lane quadrant's 32 positions, shared by the two
+    // warps that cover that quadrant's rows: [quadrant][cos 4 KB | sin 4 KB],
+    // row r's 16-byte piece c at swz128(r, c).
+    static constexpr uint32_t kExtraSmem = 4 * 8192;
     struct Params {
         const float* a_scale;
         const float* w_scale;
@@ -85,21 +115,51 @@ struct EpiQKV : EpiBase {
         __nv_bfloat16* k;
         __half* vt;  // V^T, f16
     };
-    struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
-    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
+    struct TileState {
+        float ab;  // a_scale of this thread's row
+    };
+    // Row scale; for q / k tiles, the quadrant's 32 rotary rows (positions
+    // t0 .. t0+31, contiguous in the tables) are copied into shared memory
+    // with coalesced asynchronous copies -- one warp of the pair copies the
+    // cos rows, the other the sin rows -- instead of per-lane row loads in
+    // every chunk.  Both halves of a 256-column tile are q, k or v alike, so
+    // the pair agrees on the branch and on the named barriers.
+    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
+        st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        // the warp's 128 columns of w_scale / bias (/ v_scale, indexed from 0 at the v block)
+        stage_columns(ctx.stage + 4096, ctx.lane, p.w_scale + col_start, p.bias + col_start,
+                      col_start >= 1536u && p.v_scale ? p.v_scale + (col_start - 1536u) : nullptr);
+        if (col_start >= 1536u) return;
+        const uint32_t quad = (ctx.row0 / 32u) & 3u;
+        const uint32_t half = static_cast<uint32_t>(ctx.stage - ctx.extra - kExtraSmem) / kStagingPerWarp / 4u;
+        uint8_t* buf = ctx.extra + quad * 8192u + half * 4096u;
+        pair_sync(quad);  // the pair finished reading the previous tile's rows
+        if (ctx.row0 < ctx.m_eff) {
+            const float* table = (half == 0 ? p.rope_cos : p.rope_sin) +
+                                 static_cast<uint64_t>(ctx.row0 % p.seq_len + p.pos_offset) * 32;
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {  // 256 pieces of 16 B, 32 per instruction
+                const uint32_t piece = i * 32 + ctx.lane;
+                cp_async16(buf + swz128(piece >> 3, piece & 7u), table + piece * 4);
+            }
+        }
+        cp_async_wait_all();
+        pair_sync(quad);  // both tables landed
+    }
+    static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
         constexpr uint32_t heads = 12;
-        const float ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        const float ab = st.ab;
         const uint32_t which = col0 / 768u;
         const uint32_t h = (col0 % 768u) / 64u;
         const uint32_t t = ctx.row % p.seq_len;
         float y[64];
-        const float4* w4 = reinterpret_cast<const float4*>(p.w_scale + col0);
-        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+        const uint32_t cw = (col0 % 128u) * 4u;  // byte offset of this chunk in the warp's parameters
+        const float4* w4 = reinterpret_cast<const float4*>(ctx.stage + 4096 + cw);
+        const float4* b4 = reinterpret_cast<const float4*>(ctx.stage + 4096 + 512 + cw);
 #pragma unroll
         for (uint32_t j = 0; j < 16; ++j) {
-            const float4 w = __ldg(w4 + j), bb = __ldg(b4 + j);
+            const float4 w = w4[j], bb = b4[j];
             y[4 * j] = dequant(v[4 * j], ab, w.x, bb.x);
             y[4 * j + 1] = dequant(v[4 * j + 1], ab, w.y, bb.y);
             y[4 * j + 2] = dequant(v[4 * j + 2], ab, w.z, bb.z);
@@ -109,11 +169,11 @@ struct EpiQKV : EpiBase {
         const uint32_t t0 = ctx.row0 % p.seq_len;
         const uint32_t lane = ctx.lane;
         if (which < 2) {
-            const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + static_cast<uint64_t>(t + p.pos_offset) * 32);
-            const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + static_cast<uint64_t>(t + p.pos_offset) * 32);
+            const uint8_t* rope = ctx.extra + ((ctx.row0 / 32u) & 3u) * 8192u;
 #pragma unroll
             for (uint32_t i4 = 0; i4 < 8; ++i4) {
-                const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+                const float4 c4 = *reinterpret_cast<const float4*>(rope + swz128(lane, i4));
+                const float4 s4 = *reinterpret_cast<const float4*>(rope + 4096 + swz128(lane, i4));
                 const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
                 const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
@@ -144,10 +204,10 @@ struct EpiQKV : EpiBase {
             __syncwarp();
         } else {
             if (p.v_scale) {
-                const float4* vs4 = reinterpret_cast<const float4*>(p.v_scale + h * 64);
+                const float4* vs4 = reinterpret_cast<const float4*>(ctx.stage + 4096 + 1024 + cw);
 #pragma unroll
                 for (uint32_t j = 0; j < 16; ++j) {
-                    const float4 f = __ldg(vs4 + j);
+                    const float4 f = vs4[j];
                     y[4 * j] *= f.x;
                     y[4 * j + 1] *= f.y;
                     y[4 * j + 2] *= f.z;
@@ -175,7 +235,8 @@ template <uint32_t kStages_>
 struct EpiResidualT : EpiBase {
     static constexpr uint32_t kStages = kStages_;
     static constexpr uint32_t kChunk = 32;
-    static constexpr uint32_t kStagingPerWarp = 32 * 128;
+    // per warp: dequant staging (4 KB), then its 128 columns' w_scale and bias
+    static constexpr uint32_t kStagingPerWarp = 32 * 128 + 2 * 512;
     struct Params {
         const float* a_scale;
         const float* w_scale;
@@ -188,6 +249,7 @@ struct EpiResidualT : EpiBase {
     struct TileState {
         float4 xv[8];
         uint32_t col_end;
+        float ab;
     };
     static DH_DEVINL void load_x(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0) {
         const uint32_t cq = (ctx.lane & 7u) * 4;
@@ -200,17 +262,21 @@ struct EpiResidualT : EpiBase {
     }
     static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
         st.col_end = col_start + 128;
+        st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
         load_x(p, st, ctx, col_start);
+        stage_columns(ctx.stage + 4096, ctx.lane, p.w_scale + col_start, p.bias ? p.bias + col_start : nullptr,
+                      nullptr);
     }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
-        const float ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        const float ab = st.ab;
         const uint32_t lane = ctx.lane;
+        const uint8_t* prm = ctx.stage + 4096 + (col0 % 128u) * 4u;
 #pragma unroll
         for (uint32_t j = 0; j < 32; j += 4) {
-            const float4 w = __ldg(reinterpret_cast<const float4*>(p.w_scale + col0 + j));
+            const float4 w = *reinterpret_cast<const float4*>(prm + j * 4);
             float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p.bias) bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+            if (p.bias) bb = *reinterpret_cast<const float4*>(prm + 512 + j * 4);
             *reinterpret_cast<float4*>(ctx.stage + swz128(lane, j / 4)) =
                 make_float4(dequant(v[j], ab, w.x, bb.x), dequant(v[j + 1], ab, w.y, bb.y),
                             dequant(v[j + 2], ab, w.z, bb.z), dequant(v[j + 3], ab, w.w, bb.w));
@@ -236,7 +302,7 @@ struct EpiResidualT : EpiBase {
     static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
 using EpiResidual = EpiResidualT<3>;      // K = 768
-using EpiResidualDeep = EpiResidualT<4>;  // K = 3072: deeper TMA pipeline
+using EpiResidualDeep = EpiResidualT<3>;  // K = 3072 (4 stages plus the staging would exceed shared memory)
 
 DH_DEVINL float gelu_tanh(float x) {
     // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))   (nn.GELU(approx="tanh"))
@@ -251,7 +317,8 @@ DH_DEVINL float gelu_tanh(float x) {
 struct EpiGelu : EpiBase {
     static constexpr uint32_t kStages = 3;
     static constexpr uint32_t kChunk = 32;
-    static constexpr uint32_t kStagingPerWarp = 32 * 64;
+    // per warp: output staging (2 KB), then its 128 columns' w_scale, bias, out_scale
+    static constexpr uint32_t kStagingPerWarp = 32 * 64 + 3 * 512;
     struct Params {
         const float* a_scale;
         const float* w_scale;
@@ -260,20 +327,27 @@ struct EpiGelu : EpiBase {
         __nv_bfloat16* out;
         uint32_t n;
     };
-    struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
-    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
+    struct TileState {
+        float ab;
+    };
+    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
+        st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        stage_columns(ctx.stage + 2048, ctx.lane, p.w_scale + col_start, p.bias + col_start,
+                      p.out_scale ? p.out_scale + col_start : nullptr);
+    }
+    static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
-        const float ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        const float ab = st.ab;
         const uint32_t lane = ctx.lane;
         uint32_t pk[16];
-        const float4* w4 = reinterpret_cast<const float4*>(p.w_scale + col0);
-        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
-        const float4* o4 = reinterpret_cast<const float4*>(p.out_scale + col0);
+        const uint8_t* prm = ctx.stage + 2048 + (col0 % 128u) * 4u;
+        const float4* w4 = reinterpret_cast<const float4*>(prm);
+        const float4* b4 = reinterpret_cast<const float4*>(prm + 512);
+        const float4* o4 = reinterpret_cast<const float4*>(prm + 1024);
 #pragma unroll
         for (uint32_t q = 0; q < 8; ++q) {
-            const float4 w = __ldg(w4 + q), bb = __ldg(b4 + q);
-            const float4 os = p.out_scale ? __ldg(o4 + q) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 w = w4[q], bb = b4[q];
+            const float4 os = p.out_scale ? o4[q] : make_float4(1.f, 1.f, 1.f, 1.f);
             const float a0 = gelu_tanh(dequant(v[4 * q], ab, w.x, bb.x)) * os.x;
             const float a1 = gelu_tanh(dequant(v[4 * q + 1], ab, w.y, bb.y)) * os.y;
             const float a2 = gelu_tanh(dequant(v[4 * q + 2], ab, w.z, bb.z)) * os.z;
