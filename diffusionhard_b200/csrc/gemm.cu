@@ -50,18 +50,23 @@ DH_DEVINL void cp_async16(void* smem, const void* gmem) {
 }
 DH_DEVINL void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// 128 consecutive floats from each of up to three per-column vectors (the
-// warp's columns; a null source leaves its 512-byte slot unset) into dst.
-// Issued when a tile starts, so the chunks read them from shared memory
-// instead of each issuing broadcast global loads.
-DH_DEVINL void stage_columns(uint8_t* dst, uint32_t lane, const float* a, const float* b, const float* c) {
+// `count` (<= 128, a multiple of 4) consecutive floats from each of up to
+// three per-column vectors (the warp's columns; a null source leaves its
+// 512-byte slot unset) into dst.  Issued when a tile starts, so the chunks
+// read them from shared memory instead of each issuing broadcast global loads.
+DH_DEVINL void stage_columns(uint8_t* dst, uint32_t lane, const float* a, const float* b, const float* c,
+                             uint32_t count = 128) {
     __syncwarp();  // the previous tile's chunks finished reading the slots
-    if (a) cp_async16(dst + lane * 16, a + lane * 4);
-    if (b) cp_async16(dst + 512 + lane * 16, b + lane * 4);
-    if (c) cp_async16(dst + 1024 + lane * 16, c + lane * 4);
+    if (lane * 4 < count) {
+        if (a) cp_async16(dst + lane * 16, a + lane * 4);
+        if (b) cp_async16(dst + 512 + lane * 16, b + lane * 4);
+        if (c) cp_async16(dst + 1024 + lane * 16, c + lane * 4);
+    }
     cp_async_wait_all();
     __syncwarp();
 }
+
+DH_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Barrier of the two epilogue warps that cover lane quadrant q (ids 1-4).
 DH_DEVINL void pair_sync(uint32_t q) { asm volatile("bar.sync %0, 64;" ::"r"(q + 1u) : "memory"); }
@@ -231,9 +236,10 @@ struct EpiQKV : EpiBase {
 // x[row, col] += acc * (a_scale * w_scale) + bias  (attention out, MLP down).
 // The residual read-modify-write goes through the staging buffer with one
 // 128-byte row segment per warp instruction.
-template <uint32_t kStages_>
+template <uint32_t kStages_, uint32_t kHalfCols_>
 struct EpiResidualT : EpiBase {
     static constexpr uint32_t kStages = kStages_;
+    static constexpr uint32_t kHalfCols = kHalfCols_;  // columns per epilogue warp (half the tile)
     static constexpr uint32_t kChunk = 32;
     // per warp: dequant staging (4 KB), then its 128 columns' w_scale and bias
     static constexpr uint32_t kStagingPerWarp = 32 * 128 + 2 * 512;
@@ -261,17 +267,17 @@ struct EpiResidualT : EpiBase {
         }
     }
     static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
-        st.col_end = col_start + 128;
+        st.col_end = col_start + kHalfCols;
         st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
         load_x(p, st, ctx, col_start);
         stage_columns(ctx.stage + 4096, ctx.lane, p.w_scale + col_start, p.bias ? p.bias + col_start : nullptr,
-                      nullptr);
+                      nullptr, kHalfCols);
     }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
         const float ab = st.ab;
         const uint32_t lane = ctx.lane;
-        const uint8_t* prm = ctx.stage + 4096 + (col0 % 128u) * 4u;
+        const uint8_t* prm = ctx.stage + 4096 + (col0 % kHalfCols) * 4u;
 #pragma unroll
         for (uint32_t j = 0; j < 32; j += 4) {
             const float4 w = *reinterpret_cast<const float4*>(prm + j * 4);
@@ -301,8 +307,11 @@ struct EpiResidualT : EpiBase {
     }
     static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
 };
-using EpiResidual = EpiResidualT<3>;      // K = 768
-using EpiResidualDeep = EpiResidualT<3>;  // K = 3072 (4 stages plus the staging would exceed shared memory)
+// N = 768 runs as 4 column tiles of 192: 1,024 tiles fill 6.9 waves of 148 SMs
+// (128 x 256 tiles would leave the 6th wave 19% full).
+using EpiResidual = EpiResidualT<3, 96>;      // K = 768
+using EpiResidualDeep = EpiResidualT<4, 96>;  // K = 3072: deeper TMA pipeline
+using EpiResidual256 = EpiResidualT<3, 128>;  // other N, multiples of 256
 
 DH_DEVINL float gelu_tanh(float x) {
     // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))   (nn.GELU(approx="tanh"))
@@ -313,13 +322,19 @@ DH_DEVINL float gelu_tanh(float x) {
 }
 
 // out[row, col] = bf16(gelu_tanh(acc * (a_scale * w_scale) + bias) * out_scale)
-// (MLP up), stored as 64-byte row segments, two rows per warp instruction.
+// (MLP up).  Each 32 x 32 chunk is written into a 64-byte-swizzled shared
+// buffer and stored by the TMA unit; reading the buffer back through the
+// registers would double the epilogue's shared-memory traffic, which competes
+// with the tensor core's operand reads.  Two epilogue warp groups.
 struct EpiGelu : EpiBase {
     static constexpr uint32_t kStages = 3;
+    static constexpr uint32_t kGroups = 2;
     static constexpr uint32_t kChunk = 32;
-    // per warp: output staging (2 KB), then its 128 columns' w_scale, bias, out_scale
-    static constexpr uint32_t kStagingPerWarp = 32 * 64 + 3 * 512;
+    // per warp: a 2 KB store source, then its 128 columns' w_scale, bias,
+    // out_scale (a 2 KB slot); 1 KB multiples keep the source swizzle-aligned
+    static constexpr uint32_t kStagingPerWarp = 2 * 2048;
     struct Params {
+        CUtensorMap out_map;  // out as [m, n] bf16, box 32 x 32, 64-byte swizzle
         const float* a_scale;
         const float* w_scale;
         const float* bias;
@@ -344,33 +359,67 @@ struct EpiGelu : EpiBase {
         const float4* w4 = reinterpret_cast<const float4*>(prm);
         const float4* b4 = reinterpret_cast<const float4*>(prm + 512);
         const float4* o4 = reinterpret_cast<const float4*>(prm + 1024);
+        // two columns per packed fp32x2 instruction:
+        //   x = acc * (a_scale * w_scale) + bias
+        //   u = k c x^3 + k x                (k = sqrt(2/pi), c = 0.044715)
+        //   g = h tanh(u) + h,  h = x * (out_scale / 2)
+        const float2 ab2 = make_float2(ab, ab);
+        const float2 kc2 = make_float2(0.7978845608028654f * 0.044715f, 0.7978845608028654f * 0.044715f);
+        const float2 k2 = make_float2(0.7978845608028654f, 0.7978845608028654f);
+        const float2 half2 = make_float2(0.5f, 0.5f);
 #pragma unroll
         for (uint32_t q = 0; q < 8; ++q) {
             const float4 w = w4[q], bb = b4[q];
             const float4 os = p.out_scale ? o4[q] : make_float4(1.f, 1.f, 1.f, 1.f);
-            const float a0 = gelu_tanh(dequant(v[4 * q], ab, w.x, bb.x)) * os.x;
-            const float a1 = gelu_tanh(dequant(v[4 * q + 1], ab, w.y, bb.y)) * os.y;
-            const float a2 = gelu_tanh(dequant(v[4 * q + 2], ab, w.z, bb.z)) * os.z;
-            const float a3 = gelu_tanh(dequant(v[4 * q + 3], ab, w.w, bb.w)) * os.w;
-            pk[2 * q] = pack_bf16x2(a0, a1);
-            pk[2 * q + 1] = pack_bf16x2(a2, a3);
+#pragma unroll
+            for (uint32_t hh = 0; hh < 2; ++hh) {
+                const float2 wv = hh ? make_float2(w.z, w.w) : make_float2(w.x, w.y);
+                const float2 bv = hh ? make_float2(bb.z, bb.w) : make_float2(bb.x, bb.y);
+                const float2 ov = hh ? make_float2(os.z, os.w) : make_float2(os.x, os.y);
+                const float2 acc = make_float2(static_cast<float>(static_cast<int32_t>(v[4 * q + 2 * hh])),
+                                               static_cast<float>(static_cast<int32_t>(v[4 * q + 2 * hh + 1])));
+                const float2 x = __ffma2_rn(acc, __fmul2_rn(ab2, wv), bv);
+                const float2 t1 = __fmul2_rn(__fmul2_rn(x, x), kc2);
+                const float2 u = __ffma2_rn(t1, x, __fmul2_rn(x, k2));
+                float2 t;
+                asm("tanh.approx.f32 %0, %1;" : "=f"(t.x) : "f"(u.x));
+                asm("tanh.approx.f32 %0, %1;" : "=f"(t.y) : "f"(u.y));
+                const float2 h = __fmul2_rn(x, __fmul2_rn(ov, half2));
+                const float2 g = __ffma2_rn(h, t, h);
+                pk[2 * q + hh] = pack_bf16x2(g.x, g.y);
+            }
         }
+        uint8_t* src = ctx.stage;
+        if (lane == 0) tc::tma_store_wait_read<0>();  // the previous chunk's store has read `src`
+        __syncwarp();
 #pragma unroll
         for (uint32_t w = 0; w < 16; w += 4)
-            *reinterpret_cast<uint4*>(ctx.stage + swz64(lane, w / 4)) = make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
-        __syncwarp();
-        // lane -> (row i*8 + lane/4, 16-byte piece lane%4): 8 rows x 64 B per instruction
+            *reinterpret_cast<uint4*>(src + swz64(lane, w / 4)) = make_uint4(pk[w], pk[w + 1], pk[w + 2], pk[w + 3]);
+        if (ctx.row0 + 32 <= ctx.m_eff) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tc::tma_store_2d(&p.out_map, src, static_cast<int32_t>(col0), static_cast<int32_t>(ctx.row0));
+                tc::tma_store_commit();
+            }
+        } else {
+            // ragged last rows: store only the valid ones through the registers
+            __syncwarp();
 #pragma unroll
-        for (uint32_t i = 0; i < 4; ++i) {
-            const uint32_t rr = i * 8 + (lane >> 2);
-            const uint32_t r = ctx.row0 + rr;
-            if (r < ctx.m_eff)
-                *reinterpret_cast<uint4*>(p.out + static_cast<uint64_t>(r) * p.n + col0 + (lane & 3u) * 8) =
-                    *reinterpret_cast<const uint4*>(ctx.stage + swz64(rr, lane & 3u));
+            for (uint32_t i = 0; i < 4; ++i) {
+                const uint32_t rr = i * 8 + (lane >> 2);
+                const uint32_t r = ctx.row0 + rr;
+                if (r < ctx.m_eff)
+                    *reinterpret_cast<uint4*>(p.out + static_cast<uint64_t>(r) * p.n + col0 + (lane & 3u) * 8) =
+                        *reinterpret_cast<const uint4*>(src + swz64(rr, lane & 3u));
+            }
+            __syncwarp();
         }
-        __syncwarp();
     }
     static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
+    static DH_DEVINL void finish(uint32_t lane) {
+        if (lane == 0) tc::tma_store_wait_all();
+    }
 };
 
 }  // namespace
@@ -449,22 +498,24 @@ extern "C" uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, cons
                                      uint32_t n, uint32_t k, const uint32_t* run_rows,
                                      void* stream) {
     if (!a_scale || !w_scale || !x) return DH_ERR_NULL_POINTER;
-    if (n % 256 != 0) return DH_ERR_UNSUPPORTED_SHAPE;
+    if (n % 192 != 0 && n % 256 != 0) return DH_ERR_UNSUPPORTED_SHAPE;
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_scale) |
          reinterpret_cast<uintptr_t>(bias)) & 15u)
         return DH_ERR_ALIGNMENT;
+    const uint32_t bn = n % 192 == 0 ? 192u : 256u;
     CUtensorMap ta, tb;
-    uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, 256);
+    uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, bn);
     if (st != DH_OK) return st;
-    EpiResidual::Params p{a_scale, w_scale, bias, x, n};
     GemmShape shape{m, n, k, run_rows};
-    const uint32_t tiles = ((m + 127) / 128) * (n / 256);
+    const uint32_t tiles = ((m + 127) / 128) * (n / bn);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    if (k > 1024) {
-        EpiResidualDeep::Params pd{a_scale, w_scale, bias, x, n};
-        e = launch_gemm_i8<256, EpiResidualDeep>(ta, tb, shape, pd, tiles, static_cast<cudaStream_t>(stream));
+    if (bn == 256) {
+        e = launch_gemm_i8<256, EpiResidual256>(ta, tb, shape, {a_scale, w_scale, bias, x, n}, tiles, s);
+    } else if (k > 1024) {
+        e = launch_gemm_i8<192, EpiResidualDeep>(ta, tb, shape, {a_scale, w_scale, bias, x, n}, tiles, s);
     } else {
-        e = launch_gemm_i8<256, EpiResidual>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream));
+        e = launch_gemm_i8<192, EpiResidual>(ta, tb, shape, {a_scale, w_scale, bias, x, n}, tiles, s);
     }
     if (e != cudaSuccess) return DH_ERR_CUDA;
     return DH_OK;
@@ -482,7 +533,16 @@ extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const in
     CUtensorMap ta, tb;
     uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, 256);
     if (st != DH_OK) return st;
-    EpiGelu::Params p{a_scale, w_scale, bias, out_scale, static_cast<__nv_bfloat16*>(out), n};
+    EpiGelu::Params p{};
+    if (!make_tmap_2d_sw64(&p.out_map, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, n,
+                           static_cast<uint64_t>(n) * 2, 32, 32))
+        return DH_ERR_CUDA;
+    p.a_scale = a_scale;
+    p.w_scale = w_scale;
+    p.bias = bias;
+    p.out_scale = out_scale;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.n = n;
     GemmShape shape{m, n, k, run_rows};
     const uint32_t tiles = ((m + 127) / 128) * (n / 256);
     if (launch_gemm_i8<256, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=

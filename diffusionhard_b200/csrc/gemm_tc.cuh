@@ -28,10 +28,17 @@ namespace dh {
 // after the pipeline stages) initialised once per CTA by all threads.
 struct EpiBase {
     static constexpr uint32_t kStages = 4;          // TMA pipeline depth
+    // epilogue warp groups of 8: with 2, group g takes the tiles accumulated
+    // in TMEM buffer g, so two tiles' epilogues run at once (4 warps per
+    // scheduler instead of 2), at a register cap of ~112 per thread
+    static constexpr uint32_t kGroups = 1;
     static constexpr uint32_t kExtraSmem = 0;      // shared by the CTA
     static constexpr uint32_t kStagingPerWarp = 0;  // private to each epilogue warp
     template <class P>
     static DH_DEVINL void init_smem(const P&, uint8_t*) {}
+    // after the warp's last tile (e.g. drain asynchronous stores that read
+    // shared memory before the CTA exits)
+    static DH_DEVINL void finish(uint32_t /*lane*/) {}
 };
 
 // What an epilogue thread knows about its place in the tile.  All 32 lanes of
@@ -52,20 +59,24 @@ struct GemmShape {
     const uint32_t* m_count;     // optional device row count (M_eff = min(M, *m_count))
 };
 
-template <uint32_t BN_, uint32_t STAGES_ = 4>
+template <uint32_t BN_, uint32_t STAGES_ = 4, uint32_t GROUPS_ = 1>
 struct GemmCfg {
     static constexpr uint32_t BM = 128, BN = BN_, BK = 128;
     static constexpr uint32_t STAGES = STAGES_;
     static constexpr uint32_t A_BYTES = BM * BK;
     static constexpr uint32_t B_BYTES = BN * BK;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr uint32_t TMEM_COLS = 2 * BN;
-    static constexpr uint32_t EPI_WARPS = 8;
+    // two accumulator buffers of BN columns; the allocation is a power of 2
+    static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256u : 512u;
+    static constexpr uint32_t GROUPS = GROUPS_;
+    static constexpr uint32_t EPI_WARPS = 8 * GROUPS;
     static constexpr uint32_t EPI_THREADS = 32 * EPI_WARPS;
     static constexpr uint32_t THREADS = 64 + EPI_THREADS;
     // barriers + TMEM address, rounded so the epilogue buffers after it stay
     // 128-byte aligned
-    static constexpr uint32_t BAR_BYTES = ((8 * (2 * STAGES + 5) + 16) + 127) / 128 * 128;
+    // rounded to 1 KB so the epilogue region that follows can hold swizzled
+    // TMA store sources
+    static constexpr uint32_t BAR_BYTES = ((8 * (2 * STAGES + 5) + 16) + 1023) / 1024 * 1024;
     static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
     template <class Epi>
     static constexpr uint32_t smem_bytes() {
@@ -75,11 +86,11 @@ struct GemmCfg {
 };
 
 template <uint32_t BN, class Epi>
-__global__ void __launch_bounds__(GemmCfg<BN, Epi::kStages>::THREADS, 1)
+__global__ void __launch_bounds__(GemmCfg<BN, Epi::kStages, Epi::kGroups>::THREADS, 1)
 gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                   const __grid_constant__ CUtensorMap tmap_b, GemmShape shape,
                   const __grid_constant__ typename Epi::Params ep) {
-    using Cfg = GemmCfg<BN, Epi::kStages>;
+    using Cfg = GemmCfg<BN, Epi::kStages, Epi::kGroups>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -102,7 +113,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
         for (uint32_t b = 0; b < 2; ++b) {
             tc::mbar_init(&accf_bar[b], 1);
-            tc::mbar_init(&acce_bar[b], Cfg::EPI_THREADS);
+            tc::mbar_init(&acce_bar[b], 8 * 32);  // one group of 8 warps drains a buffer
         }
         tc::mbar_init(drain_bar, 1);
         tc::fence_barrier_init();
@@ -199,20 +210,23 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
     } else {
         // --------------------------------------------------------- epilogue
+        const uint32_t ew = warp - 2;  // epilogue warp index
+        const uint32_t group = ew / 8u;
         const uint32_t quad = warp & 3u;
-        const uint32_t half = (warp - 2) >> 2;
+        const uint32_t half = (ew >> 2) & 1u;
         const uint32_t row_in_tile = quad * 32 + lane;
         constexpr uint32_t kHalf = BN / 2;
         constexpr uint32_t kChunk = Epi::kChunk;
         static_assert(kHalf % kChunk == 0, "chunk must divide the half tile");
-        uint32_t acc = 0, acc_phase = 0;
-        for (uint32_t tile = blockIdx.x; tile < total; tile += gridDim.x) {
+        // tile k of this CTA is accumulated in TMEM buffer k % 2
+        uint32_t acc = group, acc_phase = 0;
+        for (uint32_t tile = blockIdx.x + group * gridDim.x; tile < total; tile += Cfg::GROUPS * gridDim.x) {
             const uint32_t m0 = (tile / n_tiles) * Cfg::BM;
             const uint32_t n0 = (tile % n_tiles) * BN;
             const uint32_t row = m0 + row_in_tile;
             const bool row_ok = row < m_eff;
             const EpiCtx ctx{row, row_ok, m0 + quad * 32, m_eff, lane,
-                             extra_smem + Epi::kExtraSmem + (warp - 2) * Epi::kStagingPerWarp,
+                             extra_smem + Epi::kExtraSmem + ew * Epi::kStagingPerWarp,
                              extra_smem};
             typename Epi::TileState st;
             // tile_begin runs before the accumulator is ready: a policy may
@@ -236,11 +250,14 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             Epi::tile_end(ep, st, ctx);
             tc::tc_fence_before();
             tc::mbar_arrive(&acce_bar[acc]);
-            if (++acc == 2) {
+            if (Cfg::GROUPS == 2) {
+                acc_phase ^= 1;
+            } else if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1;
             }
         }
+        Epi::finish(lane);
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -255,7 +272,7 @@ template <uint32_t BN, class Epi>
 inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
                                   const GemmShape& shape, const typename Epi::Params& ep,
                                   uint32_t tiles_hint, cudaStream_t stream) {
-    using Cfg = GemmCfg<BN, Epi::kStages>;
+    using Cfg = GemmCfg<BN, Epi::kStages, Epi::kGroups>;
     auto kernel = gemm_i8_tc_kernel<BN, Epi>;
     static bool configured = false;
     if (!configured) {

@@ -67,6 +67,22 @@ DH_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
 
 // ------------------------------------------------------------------- TMA
 
+// Tiled store shared -> global (bulk-group completion, no multicast).  x is
+// the innermost coordinate; x * element size must be a multiple of 16 bytes
+// and no coordinate may be negative.
+DH_DEVINL void tma_store_2d(const void* tmap, const void* smem_src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+DH_DEVINL void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed store groups still read their shared source.
+template <int N>
+DH_DEVINL void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+// Wait until every committed store group completed.
+DH_DEVINL void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 DH_DEVINL void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int32_t x, int32_t y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"

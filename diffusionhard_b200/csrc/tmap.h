@@ -47,4 +47,24 @@ inline bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
     return r == CUDA_SUCCESS;
 }
 
+// Same, for a box whose rows are 64 bytes, with 64-byte swizzle: 16-byte
+// piece c of box row r sits at piece c ^ ((r >> 1) & 3) of that row -- the
+// layout of a TMA store source staged row by row without bank conflicts.
+inline bool make_tmap_2d_sw64(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                              uint32_t elem_bytes, uint64_t rows, uint64_t cols,
+                              uint64_t row_stride_bytes, uint32_t box_rows, uint32_t box_cols) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_stride_bytes & 15u) != 0) return false;
+    if (box_cols * elem_bytes != 64 || box_rows == 0 || box_rows > 256) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace dh
