@@ -123,9 +123,10 @@ DH_DEVINL float2 exp2_poly2(float2 x) {
                        __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
-// Pairs of P computed on the FMA pipe instead of the MUFU: pair q of each
-// group of 4 (8 keys) uses the polynomial when bit q of this mask is set.
-constexpr uint32_t kPolyPairMask = 0x1u;
+// Pairs of P computed on the FMA pipe instead of the MUFU: pair e of a row
+// uses the polynomial when bit (e % 8) of this mask is set (a quarter of
+// them: the MUFU stays the busier unit, the FMA pipe takes the rest).
+constexpr uint32_t kPolyPairMask = 0x11u;
 
 // Hardware base-2 exponential of two f16 values at once (MUFU).
 DH_DEVINL uint32_t ex2_f16x2(uint32_t x) {
@@ -374,7 +375,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                 for (uint32_t e = 0; e < 32; ++e) {
                     const float2 sv2 = make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1]));
                     const float2 a = __ffma2_rn(sv2, c2, nm2);
-                    if ((kPolyPairMask >> (e & 3u)) & 1u) {
+                    if ((kPolyPairMask >> (e & 7u)) & 1u) {
                         const float2 y = exp2_poly2(a);
                         pk[e] = pack_f16x2(y.x, y.y);
                     } else {

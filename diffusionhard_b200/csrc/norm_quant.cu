@@ -18,11 +18,23 @@ namespace {
 constexpr uint32_t kD = 768;
 constexpr uint32_t kRowWarps = 8;
 
-DH_DEVINL int8_t quant_i8(float v, float inv_scale) {
-    float q = rintf(v * inv_scale);
-    q = fminf(fmaxf(q, -127.0f), 127.0f);
-    return static_cast<int8_t>(q);
+// Round to nearest even by the 1.5 * 2^23 shifter: for |v| <= 2^22 the low
+// bits of the sum's encoding are rint(v) in two's complement, so the low byte
+// is the int8 value when |v| <= 127.  One FADD instead of a float-to-integer
+// conversion on the (quarter-rate) XU pipe; the result equals rintf / cvt.rni.
+DH_DEVINL uint32_t rint_bits(float v) { return __float_as_uint(__fadd_rn(v, 12582912.0f)); }
+
+// int8 of clamp(v * inv_scale, +-127), rounded half to even (the clamp after
+// rounding of the reference is the same thing, 127 being an integer).
+DH_DEVINL uint32_t q8_bits(float v, float inv_scale) {
+    return rint_bits(fminf(fmaxf(v * inv_scale, -127.0f), 127.0f));
 }
+
+// four int8 (low bytes of a, b, c, d) into one word, a lowest
+DH_DEVINL uint32_t pack4_i8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 
 __global__ void __launch_bounds__(kRowWarps * 32)
 embed_gather_kernel(const int32_t* __restrict__ tokens, const float* __restrict__ embed,
@@ -82,11 +94,11 @@ ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ inv_smoot
     amax = warp_max_f32(amax);
     const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
     const float inv = 1.0f / sc;
-    char4* dst = reinterpret_cast<char4*>(out + static_cast<uint64_t>(i) * kD);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(out + static_cast<uint64_t>(i) * kD);
 #pragma unroll
     for (uint32_t j = 0; j < kD / 128; ++j)
-        dst[lane_id() + 32 * j] = make_char4(quant_i8(v[j].x, inv), quant_i8(v[j].y, inv),
-                                             quant_i8(v[j].z, inv), quant_i8(v[j].w, inv));
+        dst[lane_id() + 32 * j] = pack4_i8(q8_bits(v[j].x, inv), q8_bits(v[j].y, inv), q8_bits(v[j].z, inv),
+                                           q8_bits(v[j].w, inv));
     if (lane_id() == 0) scale[i] = sc;
 }
 
@@ -140,13 +152,9 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
         uint32_t packed[2];
 #pragma unroll
-        for (uint32_t e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            const int32_t q0 = __float2int_rn(fminf(fmaxf(f.x * inv, -127.f), 127.f));
-            const int32_t q1 = __float2int_rn(fminf(fmaxf(f.y * inv, -127.f), 127.f));
-            const uint32_t b2 = (static_cast<uint32_t>(q0) & 0xFFu) | ((static_cast<uint32_t>(q1) & 0xFFu) << 8);
-            if (e & 1u) packed[e >> 1] |= b2 << 16;
-            else packed[e >> 1] = b2;
+        for (uint32_t e = 0; e < 4; e += 2) {
+            const float2 f0 = __bfloat1622float2(h[e]), f1 = __bfloat1622float2(h[e + 1]);
+            packed[e >> 1] = pack4_i8(q8_bits(f0.x, inv), q8_bits(f0.y, inv), q8_bits(f1.x, inv), q8_bits(f1.y, inv));
         }
         dst[lane_id() + 32 * j] = make_uint2(packed[0], packed[1]);
     }
@@ -184,13 +192,9 @@ quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __rest
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
         uint32_t packed[2];
 #pragma unroll
-        for (uint32_t e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            const int32_t q0 = __float2int_rn(fminf(fmaxf(f.x * inv, -127.f), 127.f));
-            const int32_t q1 = __float2int_rn(fminf(fmaxf(f.y * inv, -127.f), 127.f));
-            const uint32_t b2 = (static_cast<uint32_t>(q0) & 0xFFu) | ((static_cast<uint32_t>(q1) & 0xFFu) << 8);
-            if (e & 1u) packed[e >> 1] |= b2 << 16;
-            else packed[e >> 1] = b2;
+        for (uint32_t e = 0; e < 4; e += 2) {
+            const float2 f0 = __bfloat1622float2(h[e]), f1 = __bfloat1622float2(h[e + 1]);
+            packed[e >> 1] = pack4_i8(q8_bits(f0.x, inv), q8_bits(f0.y, inv), q8_bits(f1.x, inv), q8_bits(f1.y, inv));
         }
         dst[j] = make_uint2(packed[0], packed[1]);
     }
