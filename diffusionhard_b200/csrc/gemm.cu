@@ -8,6 +8,9 @@
 #include <cuda_fp16.h>
 
 #include "gemm_tc.cuh"
+
+#include <algorithm>
+#include <climits>
 #include "tmap.h"
 
 namespace dh {
@@ -422,6 +425,101 @@ struct EpiGelu : EpiBase {
     }
 };
 
+// Integer requantisation of the int32 accumulators, the RTL form of
+// fixed_mlp.hardware_requantized_linear (fixed_mlp.py:139-224):
+//   mult = rint(double(fp32(a_scale[r] * w_scale[c])) * 2^(shift + frac))   (mode 0)
+//   mult = (token_factor[r] * output_factor[c] + 2^(fs-1)) >> fs              (mode 1,
+//          the factorised multipliers of fixed_mlp.factorize_up_requant_scales, :327-392)
+//   p = acc * mult (int64);  q = sign(p) * ((|p| + 2^(shift-1)) >> shift)
+//   out = clamp(q + bias_q[c], lo, hi)   (int32)
+// Statistics (accumulator range, saturated outputs, largest multiplier) are
+// merged into stats[4] with one atomic per warp and chunk.
+struct EpiRequantQ : EpiBase {
+    static constexpr uint32_t kChunk = 32;
+    struct Params {
+        uint32_t mode;
+        const float* a_scale;
+        uint32_t a_scale_stride;  // 1: per row, 0: one tensor scale
+        const float* w_scale;
+        const int32_t* token_factor;
+        const int32_t* output_factor;
+        uint32_t factor_shift;
+        const int32_t* bias_q;
+        double mult_scale;  // 2^(shift + frac)
+        uint32_t shift;
+        long long lo, hi;
+        int32_t* out;
+        uint32_t n;
+        long long* stats;  // [min acc, max acc, saturated count, max multiplier]
+    };
+    struct TileState {};
+    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
+    static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
+                                const uint32_t* v) {
+        long long acc_min = LLONG_MAX, acc_max = LLONG_MIN, sat = 0, mult_max = 0;
+        if (ctx.row_ok) {
+            const float as = p.a_scale ? p.a_scale[p.a_scale_stride ? ctx.row : 0u] : 0.f;
+            const long long tf = p.token_factor ? p.token_factor[ctx.row] : 0;
+            int32_t* dst = p.out + static_cast<uint64_t>(ctx.row) * p.n;
+            const long long half = 1ll << (p.shift - 1);
+            for (uint32_t j = 0; j < 32; ++j) {
+                const uint32_t c = col0 + j;
+                if (c >= p.n) break;
+                long long mult;
+                if (p.mode == 0) {
+                    const float prod = __fmul_rn(as, p.w_scale[c]);
+                    mult = __double2ll_rn(static_cast<double>(prod) * p.mult_scale);
+                } else {
+                    mult = (tf * static_cast<long long>(p.output_factor[c]) + (1ll << (p.factor_shift - 1))) >>
+                           p.factor_shift;
+                }
+                const long long acc = static_cast<int32_t>(v[j]);
+                const long long prd = acc * mult;
+                const long long mag = ((prd < 0 ? -prd : prd) + half) >> p.shift;
+                long long o = (prd < 0 ? -mag : mag) + p.bias_q[c];
+                if (o < p.lo || o > p.hi) {
+                    ++sat;
+                    o = o < p.lo ? p.lo : p.hi;
+                }
+                dst[c] = static_cast<int32_t>(o);
+                acc_min = acc < acc_min ? acc : acc_min;
+                acc_max = acc > acc_max ? acc : acc_max;
+                mult_max = mult > mult_max ? mult : mult_max;
+            }
+        }
+        // warp merge, then one atomic per statistic
+        for (int o = 16; o > 0; o >>= 1) {
+            acc_min = min(acc_min, __shfl_xor_sync(0xFFFFFFFFu, acc_min, o));
+            acc_max = max(acc_max, __shfl_xor_sync(0xFFFFFFFFu, acc_max, o));
+            sat += __shfl_xor_sync(0xFFFFFFFFu, sat, o);
+            mult_max = max(mult_max, __shfl_xor_sync(0xFFFFFFFFu, mult_max, o));
+        }
+        if (ctx.lane == 0 && p.stats && acc_min <= acc_max) {
+            atomicMin(p.stats, acc_min);
+            atomicMax(p.stats + 1, acc_max);
+            atomicAdd(reinterpret_cast<unsigned long long*>(p.stats + 2), static_cast<unsigned long long>(sat));
+            atomicMax(p.stats + 3, mult_max);
+        }
+    }
+    static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
+};
+
+// The RTL Q5.10 GELU (fixed_mlp.hardware_gelu_q10, fixed_mlp.py:227-247):
+// lut[clamp((q + 8192) >> 4, 0, 1023)], 0 at or below -8192, q itself at or
+// above 8192.  The 1024-entry table comes from the caller.
+__global__ void gelu_q10_kernel(const int32_t* __restrict__ in, int32_t* __restrict__ out, uint64_t count,
+                                const int32_t* __restrict__ lut) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const int32_t q = in[i];
+        int32_t r;
+        if (q <= -8192) r = 0;
+        else if (q >= 8192) r = q;
+        else r = lut[(q + 8192) >> 4];
+        out[i] = r;
+    }
+}
+
 }  // namespace
 
 // Shared validation + tensor maps for an int8 K-major operand pair.
@@ -548,5 +646,41 @@ extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const in
     if (launch_gemm_i8<256, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=
         cudaSuccess)
         return DH_ERR_CUDA;
+    return DH_OK;
+}
+
+extern "C" uint32_t dh_gemm_i8_requant(const int8_t* a, const int8_t* w, uint32_t m, uint32_t n, uint32_t k,
+                                      uint32_t mode, const float* a_scale, uint32_t a_scale_stride,
+                                      const float* w_scale, const int32_t* token_factor,
+                                      const int32_t* output_factor, uint32_t factor_shift, const int32_t* bias_q,
+                                      uint32_t right_shift, uint32_t frac_bits, uint32_t output_width,
+                                      int32_t* out, int64_t* stats, void* stream) {
+    if (!out || !bias_q) return DH_ERR_NULL_POINTER;
+    if (mode == 0 && (!a_scale || !w_scale)) return DH_ERR_NULL_POINTER;
+    if (mode == 1 && (!token_factor || !output_factor)) return DH_ERR_NULL_POINTER;
+    if (mode > 1 || a_scale_stride > 1 || right_shift == 0 || right_shift > 40 || output_width > 32 ||
+        output_width <= frac_bits + 1 || (mode == 1 && (factor_shift == 0 || factor_shift > 40)))
+        return DH_ERR_INVALID_ARGUMENT;
+    if (right_shift + frac_bits > 62) return DH_ERR_INVALID_ARGUMENT;
+    CUtensorMap ta, tb;
+    uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, 256);
+    if (st != DH_OK) return st;
+    EpiRequantQ::Params p{mode, a_scale, a_scale_stride, w_scale, token_factor, output_factor, factor_shift,
+                          bias_q, static_cast<double>(1ull << (right_shift + frac_bits)), right_shift,
+                          -(1ll << (output_width - 1)), (1ll << (output_width - 1)) - 1, out, n,
+                          reinterpret_cast<long long*>(stats)};
+    GemmShape shape{m, n, k, nullptr};
+    const uint32_t tiles = ((m + 127) / 128) * ((n + 255) / 256);
+    if (launch_gemm_i8<256, EpiRequantQ>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return DH_ERR_CUDA;
+    return DH_OK;
+}
+
+extern "C" uint32_t dh_gelu_q10(const int32_t* in, int32_t* out, uint64_t count, const int32_t* lut, void* stream) {
+    if (!in || !out || !lut) return DH_ERR_NULL_POINTER;
+    if (count == 0) return DH_OK;
+    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((count + 255) / 256, 148ull * 8));
+    gelu_q10_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(in, out, count, lut);
+    DH_LAUNCH_CHECK();
     return DH_OK;
 }

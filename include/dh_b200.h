@@ -204,6 +204,31 @@ uint32_t dh_sampler_finalize_f32(const float* logits, uint32_t sequences, uint32
 uint32_t dh_gemm_i8_s32(const int8_t* a, uint64_t lda, const int8_t* w, uint64_t ldw, int32_t* c,
                         uint64_t ldc, uint32_t m, uint32_t n, uint32_t k, void* stream);
 
+/* Integer requantisation on the tensor engine, the RTL arithmetic of
+ * fixed_mlp.hardware_requantized_linear (fixed_mlp.py:139-224): C = A . W^T
+ * (int8, K-major, k a multiple of 16) and per output
+ *   mode 0: mult = rint(double(fp32(a_scale[r] * w_scale[c])) * 2^(right_shift + frac_bits))
+ *   mode 1: mult = (token_factor[r] * output_factor[c] + 2^(factor_shift-1)) >> factor_shift
+ *           (the factorised multipliers of factorize_up_requant_scales, fixed_mlp.py:327-392)
+ *   p = C * mult (int64),  q = sign(p) * ((|p| + 2^(right_shift-1)) >> right_shift)
+ *   out = clamp(q + bias_q[c], -2^(output_width-1), 2^(output_width-1) - 1)   (int32 [m, n])
+ * a_scale_stride 1: one scale per row (token granularity); 0: a_scale[0] for
+ * every row (tensor granularity).  stats (may be NULL; int64[4], initialised by
+ * the caller to {INT64_MAX, INT64_MIN, 0, 0}) receives the accumulator minimum
+ * and maximum, the number of saturated outputs and the largest multiplier; the
+ * caller checks the multiplier width (the reference rejects wider ones). */
+uint32_t dh_gemm_i8_requant(const int8_t* a, const int8_t* w, uint32_t m, uint32_t n, uint32_t k,
+                            uint32_t mode, const float* a_scale, uint32_t a_scale_stride,
+                            const float* w_scale, const int32_t* token_factor,
+                            const int32_t* output_factor, uint32_t factor_shift, const int32_t* bias_q,
+                            uint32_t right_shift, uint32_t frac_bits, uint32_t output_width,
+                            int32_t* out, int64_t* stats, void* stream);
+
+/* RTL Q5.10 GELU lookup (fixed_mlp.hardware_gelu_q10, fixed_mlp.py:227-247):
+ * out = 0 for in <= -8192, in for in >= 8192, else lut[(in + 8192) >> 4];
+ * lut holds the 1024 table entries. */
+uint32_t dh_gelu_q10(const int32_t* in, int32_t* out, uint64_t count, const int32_t* lut, void* stream);
+
 /* ------------------------------------------------------- DDiT forward path */
 /* W8A8 convention (fixed_mlp.quantized_linear, fixed_mlp.py:65-136, with static
  * SmoothQuant scales s per input channel): an activation row a is quantised as
