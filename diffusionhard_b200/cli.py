@@ -7,6 +7,8 @@ device kernels.
   validate-rng-gumbel         cli.py:666-682
   analyze-mdlm-prefix-drift   cli.py:724-739
   generate-mdlm-conditioned   cli.py:769-787
+  benchmark-mdlm-event        cli.py:397-409 (benchmark-mdlm-apple, apple_mdlm.py:203-390),
+                              also accepted under the reference's name
 
 Differences, all forced by what a run here has:
 - no checkpoint: --model-id / --revision / --local-files-only are recorded
@@ -92,6 +94,18 @@ def build_parser() -> argparse.ArgumentParser:
     drift.add_argument("--seed", type=int, default=0)
     drift.add_argument("--local-files-only", action="store_true")
     drift.add_argument("--weights-seed", type=int, default=0)
+
+    event = sub.add_parser("benchmark-mdlm-event", aliases=["benchmark-mdlm-apple"],
+                           help="benchmark the event-driven selected-row MDLM sampler against the candidate cache")
+    event.add_argument("--out", type=Path)
+    event.add_argument("--model-id", default=DEFAULT_MODEL_ID)
+    event.add_argument("--revision", default=DEFAULT_REVISION)
+    event.add_argument("--device", default="cuda")
+    event.add_argument("--canvas-tokens", type=int, default=64)
+    event.add_argument("--steps", type=int, default=64)
+    event.add_argument("--seeds", nargs="+", type=int, default=[0, 1, 2])
+    event.add_argument("--local-files-only", action="store_true")
+    event.add_argument("--weights-seed", type=int, default=0)
 
     cond = sub.add_parser("generate-mdlm-conditioned",
                           help="compare conditioned DDPM generation with retained prefix K/V")
@@ -212,6 +226,15 @@ def main(argv: Optional[List[str]] = None) -> int:
             changed_suffix_tokens=args.changed_suffix_tokens, warmup=args.warmup,
             timing_repeats=args.timing_repeats, seed=args.seed, weights_seed=args.weights_seed,
             device=args.device)
+        result.update(_checkpoint_note(args))
+        _emit(result, args.out)
+        return 0
+    if args.command in ("benchmark-mdlm-event", "benchmark-mdlm-apple"):
+        from .event import benchmark_event_sampler
+
+        result = benchmark_event_sampler(canvas_tokens=args.canvas_tokens, steps=args.steps,
+                                         seeds=tuple(args.seeds), weights_seed=args.weights_seed,
+                                         device=args.device)
         result.update(_checkpoint_note(args))
         _emit(result, args.out)
         return 0

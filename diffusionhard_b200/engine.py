@@ -212,6 +212,31 @@ class MDLMEngine:
         out = (acc.double() * combined + h.bias.double()[None, :]).float()
         return out.view(self.B, self.L, V)
 
+    def selected_logits(self, input_ids: Any, selected: Any) -> Any:
+        """fp32 logits [n, V] of the selected positions of a single-sequence
+        canvas (apple_mdlm._AppleSelectedLogits, apple_mdlm.py:159-200): the
+        forward over the whole canvas, then the final LayerNorm, quantisation
+        and head GEMM of the selected rows only, dequantised as
+        fixed_mlp.quantized_linear (fixed_mlp.py:120-136)."""
+        torch = self.torch
+        if self.B != 1 or input_ids.numel() != self.L:
+            raise ValueError("selected_logits takes one sequence of the engine's length")
+        self.tokens.copy_(input_ids.reshape(-1).to(device=self.device, dtype=torch.int32))
+        self.forward()
+        rows = selected.reshape(-1).to(device=self.device, dtype=torch.int32).contiguous()
+        n = rows.numel()
+        if n == 0 or int(rows.min()) < 0 or int(rows.max()) >= self.L:
+            raise ValueError("selected positions must be non-empty and inside the canvas")
+        cnt = torch.tensor([n], dtype=torch.int32, device=self.device)
+        hq, hs = self.final_hidden_q(rows, cnt)
+        h = self.head
+        V = h.out_features
+        acc = torch.empty((n, V), dtype=torch.int32, device=self.device)
+        _lib.call("dh_gemm_i8_s32", self._p(hq), 768, self._p(h.w), 768, self._p(acc), V, n, V, 768,
+                  _lib.stream_handle())
+        combined = (hs[:n, None] * h.w_scale[None, :]).double()
+        return (acc.double() * combined + h.bias.double()[None, :]).float()
+
     def head_argmax(self, rows: int, mode: int, rows_count: Any = None, row_position: Any = None,
                     row_key_hi: Any = None, row_eval: Any = None, key_lo: int = 0,
                     out_ids: Any = None, out_scores: Any = None, const_eval: int = 0) -> None:
@@ -303,6 +328,82 @@ class MDLMEngine:
             self._enqueue_generation(steps, seed, thresholds)
             self._events[1].record()
         return self.tokens.view(self.B, self.L), {}
+
+    # ------------------------------------------------- event-driven loop
+
+    def _load_schedule(self, sched: Any) -> Any:
+        """Copy a host EventSchedule into the selected-row buffers: rows,
+        canvas positions, Philox key_hi and per-transition counts."""
+        torch = self.torch
+        if (sched.sequences, sched.positions) != (self.B, self.L):
+            raise ValueError(f"schedule must cover [{self.B}, {self.L}]")
+        n = int(sched.order.numel())
+        order = sched.order
+        b = order // self.L
+        p = order % self.L
+        host = torch.stack([order, self.pos_offset + p, self.seq_offset + b]).to(torch.int32)
+        if n:
+            self.sel_rows[:n].copy_(host[0])
+            self.sel_pos[:n].copy_(host[1])
+            self.sel_key[:n].copy_(host[2])
+        counts = getattr(self, "_event_counts", None)
+        if counts is None or counts.numel() != sched.steps + 1:
+            counts = torch.empty(sched.steps + 1, dtype=torch.int32, device=self.device)
+            self._event_counts = counts
+        counts.copy_(torch.tensor([sched.count(k) for k in range(sched.steps + 1)], dtype=torch.int32))
+        return counts
+
+    def _enqueue_event_generation(self, sched: Any, seed: int, counts: Any) -> None:
+        s = _lib.stream_handle()
+        B, L, steps = self.B, self.L, sched.steps
+        p = self._p
+        for k in range(steps + 1):
+            if sched.count(k) == 0:
+                continue
+            off = sched.offsets[k]
+            final = 1 if k == steps else 0
+            rows, cnt = self.sel_rows[off:], counts[k:k + 1]
+            self.forward()
+            self.final_hidden_q(rows, cnt)
+            self.head_argmax(self.M, 2 if final else 1, rows_count=cnt, row_position=self.sel_pos[off:],
+                             row_key_hi=self.sel_key[off:], const_eval=k, key_lo=seed)
+            if self.head_reduce is not None:
+                self.head_reduce(self.packed)
+            elif self.head_group is not None:
+                from .distributed import all_reduce_packed_max_
+
+                all_reduce_packed_max_(self.packed, self.head_group)
+            _lib.call("dh_loop_commit", B, L, min(k, steps - 1), steps, final, p(self.packed), p(rows), p(cnt),
+                      p(self.tokens), p(self.active), p(self.need_eval), p(self.counters), s)
+
+    def generate_event_driven(self, input_ids: Any, sched: Any, *, seed: int = 0,
+                              graph: bool = False) -> Any:
+        """Event-driven generation (apple_mdlm.py:62-156, batched): only the
+        transitions of `sched` (an event.EventSchedule over [B, L]) that reveal
+        a row run a forward, and the head projects only those rows; the final
+        pass takes the greedy argmax.  Returns device int32 ids [B, L]."""
+        torch = self.torch
+        self.init_loop(input_ids, sched.steps)
+        counts = self._load_schedule(sched)
+        if graph:
+            key = ("event", sched.steps, seed, self.seq_offset, tuple(sched.offsets))
+            g = self._graphs.get(key)
+            if g is None:
+                self._enqueue_event_generation(sched, seed, counts)
+                self.init_loop(input_ids, sched.steps)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._enqueue_event_generation(sched, seed, counts)
+                self._graphs[key] = g
+            self._events[0].record()
+            g.replay()
+            self._events[1].record()
+        else:
+            self._events[0].record()
+            self._enqueue_event_generation(sched, seed, counts)
+            self._events[1].record()
+        return self.tokens.view(self.B, self.L)
 
     def generation_ms(self) -> float:
         """Device time of the last generate() (the loop only, CUDA events)."""

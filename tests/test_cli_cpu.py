@@ -17,7 +17,7 @@ def _flags(sub):
     return {o for a in action.choices[sub]._actions for o in a.option_strings if o.startswith("--")}
 
 
-# flags of the reference subcommands (cli.py:375-396, 552-563, 666-682, 724-739, 769-787)
+# flags of the reference subcommands (cli.py:375-409, 552-563, 666-682, 724-739, 769-787)
 REFERENCE_FLAGS = {
     "trace-mdlm": {"--out", "--model-id", "--revision", "--device", "--canvas-tokens", "--steps", "--warmup",
                    "--seed", "--sampler", "--local-files-only"},
@@ -33,6 +33,8 @@ REFERENCE_FLAGS = {
                                   "--seed", "--local-files-only"},
     "generate-mdlm-conditioned": {"--out", "--model-id", "--revision", "--device", "--prefix-tokens",
                                   "--suffix-tokens", "--samples", "--steps", "--seed", "--local-files-only"},
+    "benchmark-mdlm-apple": {"--out", "--model-id", "--revision", "--device", "--canvas-tokens", "--steps",
+                             "--seeds", "--local-files-only"},
 }
 
 
@@ -48,6 +50,8 @@ def test_defaults_match_the_reference():
         (64, 50258, 16, 200000, 0.01)
     a = p.parse_args(["validate-rng-gumbel"])
     assert a.mantissa_bits == [4, 6, 8] and a.full_vocabulary_batches == 16 and a.distribution_trials == 200000
+    a = p.parse_args(["benchmark-mdlm-apple"])
+    assert (a.canvas_tokens, a.steps, a.seeds) == (64, 64, [0, 1, 2])
     a = p.parse_args(["trace-mdlm", "--out", "x.json"])
     assert (a.canvas_tokens, a.steps, a.sampler) == (64, 64, "ddpm-cache")
 
