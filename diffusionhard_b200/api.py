@@ -23,9 +23,26 @@ from .model import MDLMConfig, QuantizedMDLM, build_quantized
 
 
 def load_mdlm(batch: int, seq_len: int = 1024, *, seed: int = 0, config: Optional[MDLMConfig] = None,
-              device: str = "cuda", quantized: Optional[QuantizedMDLM] = None) -> MDLMEngine:
-    """Random-init MDLM-169.6M (N(0, 0.02)), folded, W8A8-quantised, on `device`."""
-    qm = quantized if quantized is not None else build_quantized(config or MDLMConfig(), seed=seed)
+              device: str = "cuda", quantized: Optional[QuantizedMDLM] = None, checkpoint: Any = None,
+              package: Any = None, alpha: float = 0.5) -> MDLMEngine:
+    """MDLM-169.6M on `device`, W8A8-quantised with SmoothQuant (alpha) from
+    the seeded calibration batch.  Weights, in order of precedence:
+    `quantized`; `checkpoint` (an HF-layout state dict or file,
+    checkpoint.load_checkpoint); `package` (a hardware package directory,
+    checkpoint.load_hardware_package); else the random-init N(0, 0.02)
+    stand-in of `seed`."""
+    if quantized is not None:
+        qm = quantized
+    elif checkpoint is not None or package is not None:
+        from .checkpoint import load_checkpoint, load_hardware_package
+        from .model import quantize
+
+        cfg = config or MDLMConfig()
+        folded = load_checkpoint(checkpoint, cfg) if checkpoint is not None else \
+            load_hardware_package(package, config=cfg)
+        qm = quantize(folded, alpha)
+    else:
+        qm = build_quantized(config or MDLMConfig(), seed=seed, alpha=alpha)
     return MDLMEngine(qm, batch, seq_len, device)
 
 

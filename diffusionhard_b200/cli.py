@@ -7,6 +7,10 @@ device kernels.
   validate-rng-gumbel         cli.py:666-682
   analyze-mdlm-prefix-drift   cli.py:724-739
   generate-mdlm-conditioned   cli.py:769-787
+  export-mdlm-hardware-package    cli.py:155-163, 856-880
+  validate-mdlm-hardware-package  cli.py:165-169, 882-885
+  validate-hardware-fixed-mlp     cli.py:187-200, 905-917
+  sweep-hardware-fixed-mlp        cli.py:202-213
   benchmark-mdlm-event        cli.py:397-409 (benchmark-mdlm-apple, apple_mdlm.py:203-390),
                               also accepted under the reference's name
 
@@ -106,6 +110,36 @@ def build_parser() -> argparse.ArgumentParser:
     event.add_argument("--seeds", nargs="+", type=int, default=[0, 1, 2])
     event.add_argument("--local-files-only", action="store_true")
     event.add_argument("--weights-seed", type=int, default=0)
+
+    export = sub.add_parser("export-mdlm-hardware-package",
+                            help="export 64-token goldens and constant-folded FP16 weights")
+    export.add_argument("--out-dir", type=Path, required=True)
+    export.add_argument("--model-id", default=DEFAULT_MODEL_ID)
+    export.add_argument("--revision", default=DEFAULT_REVISION)
+    export.add_argument("--device", default="cpu")
+    export.add_argument("--local-files-only", action="store_true")
+    export.add_argument("--checkpoint", type=Path, help="HF-layout model.safetensors (default: the stand-in)")
+    export.add_argument("--weights-seed", type=int, default=0)
+
+    vpkg = sub.add_parser("validate-mdlm-hardware-package",
+                          help="verify package hashes, safetensors metadata, and aligned DDR layout")
+    vpkg.add_argument("--package-dir", type=Path, required=True)
+
+    hfm = sub.add_parser("validate-hardware-fixed-mlp",
+                         help="validate one package MLP through RTL-equivalent requant and GELU on the GPU")
+    hfm.add_argument("--package-dir", type=Path, required=True)
+    hfm.add_argument("--block", type=int, default=0)
+    hfm.add_argument("--activation-granularity", choices=["tensor", "token"], default="token")
+    hfm.add_argument("--down-activation-granularity", choices=["tensor", "token"])
+    hfm.add_argument("--smoothquant-alpha", type=float, default=0.75)
+    hfm.add_argument("--out", type=Path)
+
+    sfm = sub.add_parser("sweep-hardware-fixed-mlp",
+                         help="run the RTL-equivalent fixed MLP validation across all 12 blocks")
+    sfm.add_argument("--package-dir", type=Path, required=True)
+    sfm.add_argument("--activation-granularity", choices=["tensor", "token"], default="token")
+    sfm.add_argument("--down-activation-granularity", choices=["tensor", "token"])
+    sfm.add_argument("--out", type=Path)
 
     cond = sub.add_parser("generate-mdlm-conditioned",
                           help="compare conditioned DDPM generation with retained prefix K/V")
@@ -237,6 +271,48 @@ def main(argv: Optional[List[str]] = None) -> int:
                                          device=args.device)
         result.update(_checkpoint_note(args))
         _emit(result, args.out)
+        return 0
+    if args.command == "export-mdlm-hardware-package":
+        import numpy as np
+
+        from .checkpoint import checkpoint_module, deterministic_hardware_input, export_hardware_package
+        from .model import MDLMConfig, build_standin, ddit_forward, fold
+
+        cfg = MDLMConfig()
+        module = checkpoint_module(args.checkpoint, cfg) if args.checkpoint else build_standin(cfg, args.weights_seed)
+        folded = fold(module)
+        folded.config = cfg
+        ids = np.asarray([deterministic_hardware_input(64, cfg.vocab_size, cfg.mask_token_id)])
+        source = {"model_id": args.model_id, "revision": args.revision}
+        if args.checkpoint:
+            source["path"] = str(args.checkpoint)
+        else:
+            source["weights"] = _checkpoint_note(args)["weights"]
+        manifest = export_hardware_package(folded, args.out_dir, source=source,
+                                           unfolded_logits=ddit_forward(module, ids))
+        _emit({"package_dir": str(args.out_dir), "constant_fold_validation": manifest["constant_fold_validation"],
+               "golden_tensor_count": manifest["goldens"]["tensor_count"],
+               "weight_tensor_count": manifest["weights"]["tensor_count"], "files": manifest["files"]}, None)
+        return 0
+    if args.command == "validate-mdlm-hardware-package":
+        from .checkpoint import validate_hardware_package
+
+        report = validate_hardware_package(args.package_dir)
+        _emit(report, None)
+        return 0 if report["passed"] else 1
+    if args.command == "validate-hardware-fixed-mlp":
+        from .fixed_mlp import validate_hardware_fixed_mlp
+
+        _emit(validate_hardware_fixed_mlp(args.package_dir, block=args.block,
+                                          activation_granularity=args.activation_granularity,
+                                          down_activation_granularity=args.down_activation_granularity,
+                                          smoothquant_alpha=args.smoothquant_alpha), args.out)
+        return 0
+    if args.command == "sweep-hardware-fixed-mlp":
+        from .fixed_mlp import sweep_hardware_fixed_mlp
+
+        _emit(sweep_hardware_fixed_mlp(args.package_dir, activation_granularity=args.activation_granularity,
+                                       down_activation_granularity=args.down_activation_granularity), args.out)
         return 0
     if args.command == "generate-mdlm-conditioned":
         from .conditioned import evaluate_conditioned_mdlm_ddpm

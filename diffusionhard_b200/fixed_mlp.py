@@ -277,3 +277,142 @@ def hardware_gelu_q10(input_q: Any, device: Any = "cuda") -> Tuple[Any, Any]:
               _lib.stream_handle())
     output_q = out.to(torch.int64).reshape(input_q.shape).to(input_q.device)
     return output_q.float() / 1024.0, output_q
+
+
+def _error_metrics(actual: Any, expected: Any) -> Dict[str, float]:
+    """Max / mean / RMS / relative RMS error and cosine similarity
+    (fixed_mlp.py:500-517)."""
+    import torch
+    import torch.nn.functional as F
+
+    a, e = actual.float().cpu(), expected.float().cpu()
+    d = a - e
+    rms = torch.sqrt(torch.mean(d.square()))
+    cosine = float(F.cosine_similarity(a.reshape(1, -1), e.reshape(1, -1)).item())
+    return {
+        "max_abs_error": float(d.abs().max().item()),
+        "mean_abs_error": float(d.abs().mean().item()),
+        "rms_error": float(rms.item()),
+        "relative_rms_error": float((rms / torch.sqrt(torch.mean(e.square()))).item()),
+        "cosine_similarity": max(-1.0, min(1.0, cosine)),
+    }
+
+
+def _package_tensors(path: Any, names: List[str]) -> Dict[str, Any]:
+    from safetensors import safe_open
+
+    with safe_open(str(path), framework="pt", device="cpu") as handle:
+        return {n: handle.get_tensor(n).float() for n in names}
+
+
+Q13_10_MIN, Q13_10_MAX = -(1 << 23), (1 << 23) - 1
+SWEEP_ALPHAS = (0.75, 0.5, 0.5, 0.75, 0.5, 0.5, 0.75, 0.5, 0.5, 0.5, 0.5, 0.75)
+
+
+def validate_hardware_fixed_mlp(package_dir: Any, *, block: int = 0, activation_granularity: str = "token",
+                                down_activation_granularity: Any = None, smoothquant_alpha: float = 0.75,
+                                device: Any = "cuda") -> Dict[str, object]:
+    """One folded MLP of a hardware package through the RTL integer path
+    (fixed_mlp.validate_hardware_fixed_mlp, fixed_mlp.py:918-1036): the
+    package's norm2 golden -> 16-bit Q5.10 up requant -> Q5.10 GELU lookup ->
+    24-bit Q13.10 down requant -> saturating Q13.10 residual add, compared
+    with the fp32 goldens.  The MACs and requantisation run on the GPU
+    (dh_gemm_i8_requant, dh_gelu_q10); same report as the reference."""
+    import torch
+    from pathlib import Path
+
+    package_dir = Path(package_dir)
+    if not 0 <= block < 12:
+        raise ValueError("block must be between 0 and 11")
+    pre, wpre = "folded.block_%02d" % block, "block_%02d" % block
+    g = _package_tensors(package_dir / "golden_tensors.safetensors",
+                         [pre + s for s in (".norm2_unaffine", ".mlp_up", ".gelu", ".mlp_down", ".after_attention",
+                                            ".output")])
+    w = _package_tensors(package_dir / "folded_fp16_weights.safetensors",
+                         [wpre + s for s in (".mlp_up.weight", ".mlp_up.bias", ".mlp_down.weight", ".mlp_down.bias")])
+    down_gran = activation_granularity if down_activation_granularity is None else down_activation_granularity
+    up, up_q, up_m = hardware_requantized_linear(g[pre + ".norm2_unaffine"][0], w[wpre + ".mlp_up.weight"],
+                                                 w[wpre + ".mlp_up.bias"],
+                                                 activation_granularity=activation_granularity,
+                                                 smoothquant_alpha=smoothquant_alpha, output_width=16, device=device)
+    gelu, gelu_q = hardware_gelu_q10(up_q, device=device)
+    down, down_q, down_m = hardware_requantized_linear(gelu, w[wpre + ".mlp_down.weight"], w[wpre + ".mlp_down.bias"],
+                                                       activation_granularity=down_gran,
+                                                       smoothquant_alpha=smoothquant_alpha, output_width=24,
+                                                       device=device)
+    residual_unclipped = torch.round(g[pre + ".after_attention"][0].double() * 1024.0).to(torch.int64)
+    residual_q = residual_unclipped.clamp(Q13_10_MIN, Q13_10_MAX)
+    block_unclipped = residual_q + down_q
+    block_q = block_unclipped.clamp(Q13_10_MIN, Q13_10_MAX)
+    block_out = block_q.float() / 1024.0
+
+    def sat(t: Any) -> float:
+        return float(((t < Q13_10_MIN) | (t > Q13_10_MAX)).float().mean().item())
+
+    return {
+        "package_dir": str(package_dir),
+        "block": block,
+        "activation_granularity": activation_granularity,
+        "down_activation_granularity": down_gran,
+        "smoothquant_alpha": smoothquant_alpha,
+        "formats": {"mlp_up": "signed-q5.10-16-bit", "gelu": "signed-q5.10-1024-entry-lut",
+                    "mlp_down": "signed-q13.10-24-bit",
+                    "residual_and_block_output": "signed-q13.10-24-bit-saturating"},
+        "integer": {
+            "mlp_up": up_m, "mlp_down": down_m,
+            "mlp_up_q_min": int(up_q.min().item()), "mlp_up_q_max": int(up_q.max().item()),
+            "gelu_q_min": int(gelu_q.min().item()), "gelu_q_max": int(gelu_q.max().item()),
+            "mlp_down_q_min": int(down_q.min().item()), "mlp_down_q_max": int(down_q.max().item()),
+            "residual_q_min": int(residual_q.min().item()), "residual_q_max": int(residual_q.max().item()),
+            "residual_saturation_fraction": sat(residual_unclipped),
+            "block_output_saturation_fraction": sat(block_unclipped),
+        },
+        "accuracy": {
+            "mlp_up": _error_metrics(up, g[pre + ".mlp_up"][0]),
+            "gelu": _error_metrics(gelu, g[pre + ".gelu"][0]),
+            "mlp_down": _error_metrics(down, g[pre + ".mlp_down"][0]),
+            "block_output": _error_metrics(block_out, g[pre + ".output"][0]),
+        },
+        "scope": ("one frozen H0 input with RTL-equivalent integer requantization "
+                  "and GELU; generation quality and vendor timing are not established"),
+    }
+
+
+def sweep_hardware_fixed_mlp(package_dir: Any, *, activation_granularity: str = "token",
+                             down_activation_granularity: Any = None, blocks: int = 12,
+                             device: Any = "cuda") -> Dict[str, object]:
+    """validate_hardware_fixed_mlp over the package's blocks with the
+    reference's per-block alphas and summary (fixed_mlp.py:1039-1110)."""
+    import statistics
+
+    results = [validate_hardware_fixed_mlp(package_dir, block=b, activation_granularity=activation_granularity,
+                                           down_activation_granularity=down_activation_granularity,
+                                           smoothquant_alpha=SWEEP_ALPHAS[b], device=device)
+               for b in range(blocks)]
+    rel = [r["accuracy"]["block_output"]["relative_rms_error"] for r in results]
+    return {
+        "package_dir": str(package_dir),
+        "activation_granularity": activation_granularity,
+        "down_activation_granularity": (activation_granularity if down_activation_granularity is None
+                                        else down_activation_granularity),
+        "blocks": results,
+        "summary": {
+            "minimum_block_output_relative_rms": min(rel),
+            "median_block_output_relative_rms": statistics.median(rel),
+            "maximum_block_output_relative_rms": max(rel),
+            "mean_block_output_relative_rms": statistics.mean(rel),
+            "maximum_up_q5_10_saturation_fraction": max(
+                r["integer"]["mlp_up"]["output_saturation_fraction"] for r in results),
+            "maximum_down_q13_10_saturation_fraction": max(
+                r["integer"]["mlp_down"]["output_saturation_fraction"] for r in results),
+            "maximum_residual_q13_10_saturation_fraction": max(
+                r["integer"]["residual_saturation_fraction"] for r in results),
+            "maximum_block_output_q13_10_saturation_fraction": max(
+                r["integer"]["block_output_saturation_fraction"] for r in results),
+            "maximum_required_unsigned_multiplier_bits": max(
+                r["integer"][layer]["required_unsigned_multiplier_bits"] for r in results
+                for layer in ("mlp_up", "mlp_down")),
+        },
+        "scope": ("all checkpoint blocks on one frozen H0 input; errors are local "
+                  "block comparisons and not composed generation quality"),
+    }

@@ -138,6 +138,9 @@ def build_standin(config: MDLMConfig = MDLMConfig(), seed: int = 0, std: float =
     class Config:
         n_heads = config.heads
         hidden_dim = config.hidden
+        n_blocks = config.blocks
+        vocab_size = config.vocab_size
+        model_length = config.max_positions
         time_conditioning = False
 
     class Model(nn.Module):
@@ -147,6 +150,49 @@ def build_standin(config: MDLMConfig = MDLMConfig(), seed: int = 0, std: float =
             self.config = Config()
 
     return Model().eval()
+
+
+def ddit_forward(model, ids) -> "object":
+    """Unfolded DDiT forward of a module with the HF attribute names (the
+    stand-in above or a loaded checkpoint), fp32 on the CPU: the adaLN
+    conditioning c = silu(sigma_map(0)) is applied as modulate / gate at run
+    time rather than folded.  The block and final-layer structure follows
+    the reference's MLX restatement (mlx_mdlm.py:397-498): per block,
+    x += gate_msa * attn_out(attn(rotary(qkv(norm1(x) * (1 + scale_msa) + shift_msa)))), then
+    x += gate_mlp * mlp(norm2(x) * (1 + scale_mlp) + shift_mlp); logits =
+    linear(norm_final(x) * (1 + scale) + shift).  Returns fp32 logits [B, L, V]."""
+    import torch
+    import torch.nn.functional as F
+
+    with torch.no_grad():
+        bb = model.backbone
+        ids_t = torch.as_tensor(ids, dtype=torch.long)
+        x = bb.vocab_embed(ids_t).float()
+        B, L, d = x.shape
+        heads = int(model.config.n_heads)
+        hd = d // heads
+        c = F.silu(bb.sigma_map(torch.zeros(1)))
+        cos, sin = bb.rotary_emb(x)
+        half = hd // 2
+        cos = cos[0, :, 0, 0, :half][None, :, None, :]
+        sin = sin[0, :, 0, 0, :half][None, :, None, :]
+
+        def rot(t):
+            a, b = t[..., :half], t[..., half:]
+            return torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1)
+
+        for blk in bb.blocks:
+            sa, ca, ga, sm, cm, gm = blk.adaLN_modulation(c)[:, None].chunk(6, dim=2)
+            h = blk.norm1(x) * (1 + ca) + sa
+            qkv = blk.attn_qkv(h).view(B, L, 3, heads, hd)
+            q, k, v = qkv.unbind(dim=2)
+            a = F.scaled_dot_product_attention(rot(q).transpose(1, 2), rot(k).transpose(1, 2), v.transpose(1, 2))
+            x = x + ga * blk.attn_out(a.transpose(1, 2).reshape(B, L, d))
+            h = blk.norm2(x) * (1 + cm) + sm
+            x = x + gm * blk.mlp(h)
+        ol = bb.output_layer
+        shift, scale = ol.adaLN_modulation(c)[:, None].chunk(2, dim=2)
+        return ol.linear(ol.norm_final(x) * (1 + scale) + shift)
 
 
 @dataclass
@@ -221,11 +267,16 @@ def rope_tables(positions: int, head_dim: int = 64):
 
 
 def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict[str, np.ndarray]] = None,
-                 threads: Optional[int] = None) -> np.ndarray:
+                 threads: Optional[int] = None, captured: Optional[Dict[str, object]] = None) -> np.ndarray:
     """Folded fp32 forward (hardware_package.folded_mdlm_forward semantics);
     returns the final hidden state after LayerNorm (unaffine).  When
     `record_amax` is given, the per-input-channel max |activation| of every
-    linear is accumulated into it (keys "b{i}.qkv", ..., "head")."""
+    linear is accumulated into it (keys "b{i}.qkv", ..., "head").  When
+    `captured` is given, it receives the intermediate tensors under the
+    reference's golden names (hardware_package.py:195-289):
+    folded.embedding, folded.block_NN.{norm1_unaffine, qkv, attention,
+    attention_projection, after_attention, norm2_unaffine, mlp_up, gelu,
+    mlp_down, output}, folded.final.norm_unaffine."""
     import torch
     import torch.nn.functional as F
 
@@ -245,27 +296,46 @@ def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict
         a, b = t[..., :h], t[..., h:]
         return torch.cat((a * cos_t - b * sin_t, b * cos_t + a * sin_t), dim=-1)
 
+    def cap(name, t):
+        if captured is not None:
+            captured[name] = t.detach().contiguous().clone()
+
     with torch.no_grad():
         x = torch.from_numpy(folded.embedding)[torch.from_numpy(ids.astype(np.int64))]
+        cap("folded.embedding", x)
         for i, blk in enumerate(folded.blocks):
+            pre = "folded.block_%02d" % i
             h = F.layer_norm(x, [cfg.hidden])
             rec(f"b{i}.qkv", h)
+            cap(pre + ".norm1_unaffine", h)
             qkv = F.linear(h, torch.from_numpy(blk["qkv"].weight), torch.from_numpy(blk["qkv"].bias))
+            cap(pre + ".qkv", qkv)
             qkv = qkv.view(B, L, 3, cfg.heads, cfg.head_dim)
             q, k, v = qkv.unbind(dim=2)
             q, k = rot(q), rot(k)
             a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
             a = a.transpose(1, 2).reshape(B, L, cfg.hidden)
             rec(f"b{i}.out", a)
-            x = x + F.linear(a, torch.from_numpy(blk["out"].weight))
+            cap(pre + ".attention", a)
+            proj = F.linear(a, torch.from_numpy(blk["out"].weight))
+            x = x + proj
+            cap(pre + ".attention_projection", proj)
+            cap(pre + ".after_attention", x)
             h = F.layer_norm(x, [cfg.hidden])
             rec(f"b{i}.up", h)
-            u = F.gelu(F.linear(h, torch.from_numpy(blk["up"].weight), torch.from_numpy(blk["up"].bias)),
-                       approximate="tanh")
+            cap(pre + ".norm2_unaffine", h)
+            up = F.linear(h, torch.from_numpy(blk["up"].weight), torch.from_numpy(blk["up"].bias))
+            cap(pre + ".mlp_up", up)
+            u = F.gelu(up, approximate="tanh")
             rec(f"b{i}.down", u)
-            x = x + F.linear(u, torch.from_numpy(blk["down"].weight), torch.from_numpy(blk["down"].bias))
+            cap(pre + ".gelu", u)
+            dn = F.linear(u, torch.from_numpy(blk["down"].weight), torch.from_numpy(blk["down"].bias))
+            cap(pre + ".mlp_down", dn)
+            x = x + dn
+            cap(pre + ".output", x)
         h = F.layer_norm(x, [cfg.hidden])
         rec("head", h)
+        cap("folded.final.norm_unaffine", h)
         return h.numpy()
 
 
