@@ -7,6 +7,7 @@ device kernels.
   validate-rng-gumbel         cli.py:666-682
   analyze-mdlm-prefix-drift   cli.py:724-739
   generate-mdlm-conditioned   cli.py:769-787
+  run-mdlm-two-turn               cli.py:788-807, 1616-1640 (multiturn.evaluate_two_turn_mdlm_session)
   export-mdlm-hardware-package    cli.py:155-163, 856-880
   validate-mdlm-hardware-package  cli.py:165-169, 882-885
   validate-hardware-fixed-mlp     cli.py:187-200, 905-917
@@ -23,7 +24,9 @@ Differences, all forced by what a run here has:
 - trace-mdlm offers the two candidate-cache samplers the device loop
   implements, and writes a JSON trace rather than the reference's
   workload-trace IR.
-Lengths are multiples of 32 (the kernels' granule).
+Lengths are multiples of 32 (the kernels' granule), so run-mdlm-two-turn's
+answer and follow-up blocks default to 32 tokens where the reference's
+default to 16.
 """
 
 from __future__ import annotations
@@ -110,6 +113,25 @@ def build_parser() -> argparse.ArgumentParser:
     event.add_argument("--seeds", nargs="+", type=int, default=[0, 1, 2])
     event.add_argument("--local-files-only", action="store_true")
     event.add_argument("--weights-seed", type=int, default=0)
+
+    turn = sub.add_parser("run-mdlm-two-turn", help="run an exact block-causal two-turn retained-K/V session")
+    turn.add_argument("--out", type=Path)
+    turn.add_argument("--model-id", default=DEFAULT_MODEL_ID)
+    turn.add_argument("--revision", default=DEFAULT_REVISION)
+    turn.add_argument("--device", default="cuda")
+    turn.add_argument("--dataset-id", default="Salesforce/wikitext")
+    turn.add_argument("--dataset-config", default="wikitext-2-raw-v1")
+    turn.add_argument("--dataset-revision", default="b08601e04326c79dfdd32d625aee71d232d685c3")
+    turn.add_argument("--split", default="test")
+    turn.add_argument("--prefix-tokens", type=int, default=64)
+    turn.add_argument("--first-answer-tokens", type=int, default=32)
+    turn.add_argument("--followup-tokens", type=int, default=32)
+    turn.add_argument("--second-answer-tokens", type=int, default=32)
+    turn.add_argument("--samples", type=int, default=3)
+    turn.add_argument("--steps", type=int, default=64)
+    turn.add_argument("--seed", type=int, default=0)
+    turn.add_argument("--local-files-only", action="store_true")
+    turn.add_argument("--weights-seed", type=int, default=0)
 
     export = sub.add_parser("export-mdlm-hardware-package",
                             help="export 64-token goldens and constant-folded FP16 weights")
@@ -270,6 +292,20 @@ def main(argv: Optional[List[str]] = None) -> int:
                                          seeds=tuple(args.seeds), weights_seed=args.weights_seed,
                                          device=args.device)
         result.update(_checkpoint_note(args))
+        _emit(result, args.out)
+        return 0
+    if args.command == "run-mdlm-two-turn":
+        from .session import evaluate_two_turn_mdlm_session
+
+        result = evaluate_two_turn_mdlm_session(
+            prefix_tokens=args.prefix_tokens, first_answer_tokens=args.first_answer_tokens,
+            followup_tokens=args.followup_tokens, second_answer_tokens=args.second_answer_tokens,
+            samples=args.samples, steps=args.steps, seed=args.seed, weights_seed=args.weights_seed,
+            device=args.device)
+        result.update(_checkpoint_note(args))
+        result["dataset"] = {"id": args.dataset_id, "config": args.dataset_config, "revision": args.dataset_revision,
+                             "split": args.split, "used": False,
+                             "note": "the dataset is not on this host: windows are seeded synthetic ids"}
         _emit(result, args.out)
         return 0
     if args.command == "export-mdlm-hardware-package":

@@ -9,7 +9,11 @@ Restates, in torch-CPU float32 / float64, the reference arithmetic:
     (hardware_package.py:195-289), mlx_mdlm._DDiTBlock (mlx_mdlm.py:397-453);
   * rotate-half rotary (mlx_mdlm.py:316-329) and fp32 SDPA with scale 1/8;
   * prefix-cached suffix forward (prefix_drift._cached_suffix_forward,
-    prefix_drift.py:155-238) over K/V = [prefix ; suffix].
+    prefix_drift.py:155-238) over K/V = [prefix ; suffix];
+  * block-causal attention (mdlm.block_isolation, mdlm.py:61-77, applied as
+    the additive -inf bias of mdlm.py:424-441): a row of a completed block
+    attends to its own and earlier blocks; rows after the last boundary form
+    the active bidirectional block.
 Pinned to the reference in tests/test_model_oracle.py (golden fixtures made by
 tests/golden/make_model_golden.py from the reference's own functions).
 """
@@ -60,12 +64,26 @@ def _rot(t, cos, sin):
     return torch.cat((a * cos - b * sin, b * cos + a * sin), dim=-1)
 
 
+def block_causal_bias(length: int, block_ends):
+    """Additive attention bias [L, L] of mdlm.py:424-441: for consecutive
+    completed blocks [start, end), keys at or after `end` are -inf."""
+    import torch
+
+    bias = torch.zeros((length, length), dtype=torch.float32)
+    start = 0
+    for end in (min(int(e), length) for e in block_ends if int(e) > 0):
+        bias[start:end, end:] = -torch.inf
+        start = end
+    return bias
+
+
 def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
             prefix_kv: Optional[List[Tuple[object, object]]] = None, capture_kv: bool = False,
-            record: Optional[Dict[str, object]] = None):
+            record: Optional[Dict[str, object]] = None, block_ends: Optional[List[int]] = None):
     """W8A8 forward of `ids` [B, L].  Returns the final LayerNorm output [B, L, d].
 
     positions: rotary positions of the rows (default 0..L-1).
+    block_ends: completed block boundaries for block-causal attention.
     prefix_kv: per block (K_rot, V) [B, P, H, 64] prepended to the keys/values.
     capture_kv: store per-block (K_rot, V) of these rows in record["kv"].
     record: optional dict receiving "x{i}" (residual after block i),
@@ -80,6 +98,9 @@ def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
     cos = torch.from_numpy(qm.rope_cos[pos])[None, :, None, :]
     sin = torch.from_numpy(qm.rope_sin[pos])[None, :, None, :]
     kv = []
+    bias = block_causal_bias(L, block_ends) if block_ends else None
+    if bias is not None and prefix_kv is not None:
+        raise ValueError("block_ends apply to a whole-sequence forward")
     with torch.no_grad():
         x = torch.from_numpy(qm.embedding)[torch.from_numpy(ids.astype(np.int64))]
         for i, blk in enumerate(qm.blocks):
@@ -92,7 +113,8 @@ def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
             if prefix_kv is not None:
                 k = torch.cat([prefix_kv[i][0], k], dim=1)
                 v = torch.cat([prefix_kv[i][1], v], dim=1)
-            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               attn_mask=bias)
             a = a.transpose(1, 2).reshape(B * L, cfg.hidden)
             x = x + w8a8_linear(a, blk["out"]).view(B, L, cfg.hidden)
             h = F.layer_norm(x, [cfg.hidden]).reshape(B * L, cfg.hidden)

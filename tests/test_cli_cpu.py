@@ -17,7 +17,7 @@ def _flags(sub):
     return {o for a in action.choices[sub]._actions for o in a.option_strings if o.startswith("--")}
 
 
-# flags of the reference subcommands (cli.py:155-213, 375-409, 552-563, 666-682, 724-739, 769-787)
+# flags of the reference subcommands (cli.py:155-213, 375-409, 552-563, 666-682, 724-739, 769-807)
 REFERENCE_FLAGS = {
     "trace-mdlm": {"--out", "--model-id", "--revision", "--device", "--canvas-tokens", "--steps", "--warmup",
                    "--seed", "--sampler", "--local-files-only"},
@@ -33,6 +33,10 @@ REFERENCE_FLAGS = {
                                   "--seed", "--local-files-only"},
     "generate-mdlm-conditioned": {"--out", "--model-id", "--revision", "--device", "--prefix-tokens",
                                   "--suffix-tokens", "--samples", "--steps", "--seed", "--local-files-only"},
+    "run-mdlm-two-turn": {"--out", "--model-id", "--revision", "--device", "--dataset-id", "--dataset-config",
+                          "--dataset-revision", "--split", "--prefix-tokens", "--first-answer-tokens",
+                          "--followup-tokens", "--second-answer-tokens", "--samples", "--steps", "--seed",
+                          "--local-files-only"},
     "export-mdlm-hardware-package": {"--out-dir", "--model-id", "--revision", "--device", "--local-files-only"},
     "validate-mdlm-hardware-package": {"--package-dir"},
     "validate-hardware-fixed-mlp": {"--package-dir", "--block", "--activation-granularity",
