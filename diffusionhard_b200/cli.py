@@ -12,6 +12,7 @@ device kernels.
   validate-mdlm-hardware-package  cli.py:165-169, 882-885
   validate-hardware-fixed-mlp     cli.py:187-200, 905-917
   sweep-hardware-fixed-mlp        cli.py:202-213
+  sweep-fixed-layernorm / sweep-fixed-rotary / sweep-fixed-attention   cli.py:240-258
   benchmark-mdlm-event        cli.py:397-409 (benchmark-mdlm-apple, apple_mdlm.py:203-390),
                               also accepted under the reference's name
 
@@ -162,6 +163,13 @@ def build_parser() -> argparse.ArgumentParser:
     sfm.add_argument("--activation-granularity", choices=["tensor", "token"], default="token")
     sfm.add_argument("--down-activation-granularity", choices=["tensor", "token"])
     sfm.add_argument("--out", type=Path)
+
+    for name, help_text in (("sweep-fixed-layernorm", "validate Q13.10 to Q5.12 LayerNorm at all H0 boundaries"),
+                            ("sweep-fixed-rotary", "validate Q5.12 rotary Q/K transforms at all H0 blocks"),
+                            ("sweep-fixed-attention", "validate fixed attention, output projection, and residual")):
+        fx = sub.add_parser(name, help=help_text + " (on the GPU)")
+        fx.add_argument("--package-dir", type=Path, required=True)
+        fx.add_argument("--out", type=Path)
 
     cond = sub.add_parser("generate-mdlm-conditioned",
                           help="compare conditioned DDPM generation with retained prefix K/V")
@@ -349,6 +357,14 @@ def main(argv: Optional[List[str]] = None) -> int:
 
         _emit(sweep_hardware_fixed_mlp(args.package_dir, activation_granularity=args.activation_granularity,
                                        down_activation_granularity=args.down_activation_granularity), args.out)
+        return 0
+    if args.command in ("sweep-fixed-layernorm", "sweep-fixed-rotary", "sweep-fixed-attention"):
+        from . import fixed_point
+
+        fn = {"sweep-fixed-layernorm": fixed_point.sweep_fixed_layer_norm,
+              "sweep-fixed-rotary": fixed_point.sweep_fixed_rotary,
+              "sweep-fixed-attention": fixed_point.sweep_fixed_attention}[args.command]
+        _emit(fn(args.package_dir), args.out)
         return 0
     if args.command == "generate-mdlm-conditioned":
         from .conditioned import evaluate_conditioned_mdlm_ddpm

@@ -43,6 +43,9 @@ REFERENCE_FLAGS = {
                                     "--down-activation-granularity", "--smoothquant-alpha", "--out"},
     "sweep-hardware-fixed-mlp": {"--package-dir", "--activation-granularity", "--down-activation-granularity",
                                  "--out"},
+    "sweep-fixed-layernorm": {"--package-dir", "--out"},
+    "sweep-fixed-rotary": {"--package-dir", "--out"},
+    "sweep-fixed-attention": {"--package-dir", "--out"},
     "benchmark-mdlm-apple": {"--out", "--model-id", "--revision", "--device", "--canvas-tokens", "--steps",
                              "--seeds", "--local-files-only"},
 }
