@@ -101,14 +101,17 @@ DH_DEVINL uint32_t pack_bf16x2(float a, float b) {
 struct EpiQKV : EpiBase {
     static constexpr uint32_t kStages = 3;
     static constexpr uint32_t kChunk = 64;
-    // per warp: output staging (4 KB), then its 128 columns' w_scale, bias and
-    // v_scale (512 B each)
-    static constexpr uint32_t kStagingPerWarp = 32 * 128 + 3 * 512;
+    // per warp: the 4 KB source of its q / k TMA stores, then its 128
+    // columns' w_scale, bias and v_scale (512 B each); 1 KB multiples keep
+    // every source 1024-byte aligned for the 128-byte swizzle
+    static constexpr uint32_t kStagingPerWarp = 6144;
     // Rotary rows of each lane quadrant's 32 positions, shared by the two
     // warps that cover that quadrant's rows: [quadrant][cos 4 KB | sin 4 KB],
     // row r's 16-byte piece c at swz128(r, c).
     static constexpr uint32_t kExtraSmem = 4 * 8192;
     struct Params {
+        CUtensorMap q_map;   // Q as [B * 12 * seq_len, 64] bf16, box 32 x 64, 128-byte swizzle
+        CUtensorMap k_map;   // K as [B * 12 * kv_stride, 64] bf16, same box
         const float* a_scale;
         const float* w_scale;
         const float* bias;
@@ -160,7 +163,6 @@ struct EpiQKV : EpiBase {
         const float ab = st.ab;
         const uint32_t which = col0 / 768u;
         const uint32_t h = (col0 % 768u) / 64u;
-        const uint32_t t = ctx.row % p.seq_len;
         float y[64];
         const uint32_t cw = (col0 % 128u) * 4u;  // byte offset of this chunk in the warp's parameters
         const float4* w4 = reinterpret_cast<const float4*>(ctx.stage + 4096 + cw);
@@ -176,7 +178,15 @@ struct EpiQKV : EpiBase {
         const uint32_t b = ctx.row0 / p.seq_len;
         const uint32_t t0 = ctx.row0 % p.seq_len;
         const uint32_t lane = ctx.lane;
+        // The warp's 32 rows lie in one sequence and are all valid or all
+        // past m_eff (both multiples of 32).
+        const bool live = ctx.row0 < ctx.m_eff;
         if (which < 2) {
+            // q / k chunk: staged in shared memory (128-byte swizzle), then one
+            // TMA store, once the previous chunk's store has read the buffer
+            uint8_t* src = ctx.stage;
+            if (lane == 0) tc::tma_store_wait_read<0>();
+            __syncwarp();
             const uint8_t* rope = ctx.extra + ((ctx.row0 / 32u) & 3u) * 8192u;
 #pragma unroll
             for (uint32_t i4 = 0; i4 < 8; ++i4) {
@@ -194,20 +204,20 @@ struct EpiQKV : EpiBase {
             }
 #pragma unroll
             for (uint32_t w = 0; w < 32; w += 4)
-                *reinterpret_cast<uint4*>(ctx.stage + swz128(lane, w / 4)) =
+                *reinterpret_cast<uint4*>(src + swz128(lane, w / 4)) =
                     make_uint4(pack_bf16x2(y[2 * w], y[2 * w + 1]), pack_bf16x2(y[2 * w + 2], y[2 * w + 3]),
                                pack_bf16x2(y[2 * w + 4], y[2 * w + 5]), pack_bf16x2(y[2 * w + 6], y[2 * w + 7]));
-            __syncwarp();
-            const uint32_t len = which == 0 ? p.seq_len : p.kv_stride;
-            const uint32_t pos0 = which == 0 ? t0 : t0 + p.kv_offset;
-            // the warp's 32 rows x 128 B are contiguous: 4 rows per instruction
-            uint4* dst = reinterpret_cast<uint4*>((which == 0 ? p.q : p.k) +
-                                                  ((static_cast<uint64_t>(b) * heads + h) * len + pos0) * 64);
-#pragma unroll
-            for (uint32_t i = 0; i < 8; ++i) {
-                const uint32_t rr = i * 4 + (lane >> 3);
-                if (ctx.row0 + rr < ctx.m_eff)
-                    dst[rr * 8 + (lane & 7u)] = *reinterpret_cast<const uint4*>(ctx.stage + swz128(rr, lane & 7u));
+            if (live) {
+                // rows of (b, h) at position pos0.. in Q [.., seq_len, 64] or K [.., kv_stride, 64]
+                const uint32_t len = which == 0 ? p.seq_len : p.kv_stride;
+                const uint32_t pos0 = which == 0 ? t0 : t0 + p.kv_offset;
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::tma_store_2d(which == 0 ? &p.q_map : &p.k_map, src, 0,
+                                     static_cast<int32_t>((b * heads + h) * len + pos0));
+                    tc::tma_store_commit();
+                }
             }
             __syncwarp();
         } else {
@@ -223,10 +233,12 @@ struct EpiQKV : EpiBase {
                 }
             }
             // V^T: for each channel d the warp's 32 consecutive tokens form
-            // one 64-byte run, so lane = token stores are already coalesced.
-            if (ctx.row_ok) {
-                __half* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride +
-                                     t + p.kv_offset;
+            // one 64-byte run, so lane = token stores are already coalesced
+            // (measured faster than staging the transpose through shared
+            // memory, which the tensor core's operand reads also use).
+            if (live) {
+                __half* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride + t0 + lane +
+                              p.kv_offset;
 #pragma unroll
                 for (uint32_t d = 0; d < 64; ++d)
                     dst[static_cast<uint64_t>(d) * p.kv_stride] = __float2half_rn(y[d]);
@@ -234,6 +246,9 @@ struct EpiQKV : EpiBase {
         }
     }
     static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
+    static DH_DEVINL void finish(uint32_t lane) {
+        if (lane == 0) tc::tma_store_wait_all();
+    }
 };
 
 // x[row, col] += acc * (a_scale * w_scale) + bias  (attention out, MLP down).
@@ -570,7 +585,7 @@ extern "C" uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, cons
         return DH_ERR_NULL_POINTER;
     if (seq_len == 0 || m % seq_len != 0 || kv_offset + seq_len > kv_stride)
         return DH_ERR_INVALID_ARGUMENT;
-    // a warp's 32 rows must lie in one sequence, and V^T pairs are 4-byte stores
+    // a warp's 32 rows must lie in one sequence
     if (seq_len % 32 != 0) return DH_ERR_UNSUPPORTED_SHAPE;
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
          reinterpret_cast<uintptr_t>(w_scale) | reinterpret_cast<uintptr_t>(bias) |
@@ -580,9 +595,24 @@ extern "C" uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, cons
     CUtensorMap ta, tb;
     uint32_t st = make_i8_operand_maps(&ta, &tb, a, 768, w, 768, m, 2304, 768, 256);
     if (st != DH_OK) return st;
-    EpiQKV::Params p{a_scale, w_scale, bias, rope_cos, rope_sin, v_scale, seq_len, pos_offset, kv_stride,
-                     kv_offset, static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k),
-                     static_cast<__half*>(vt)};
+    const uint64_t bh = static_cast<uint64_t>(m / seq_len) * 12;
+    EpiQKV::Params p{};
+    if (!make_tmap_2d(&p.q_map, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bh * seq_len, 64, 128, 32, 64) ||
+        !make_tmap_2d(&p.k_map, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bh * kv_stride, 64, 128, 32, 64))
+        return DH_ERR_CUDA;
+    p.a_scale = a_scale;
+    p.w_scale = w_scale;
+    p.bias = bias;
+    p.rope_cos = rope_cos;
+    p.rope_sin = rope_sin;
+    p.v_scale = v_scale;
+    p.seq_len = seq_len;
+    p.pos_offset = pos_offset;
+    p.kv_stride = kv_stride;
+    p.kv_offset = kv_offset;
+    p.q = static_cast<__nv_bfloat16*>(q);
+    p.k = static_cast<__nv_bfloat16*>(k);
+    p.vt = static_cast<__half*>(vt);
     GemmShape shape{m, 2304, 768, run_rows};
     const uint32_t tiles = ((m + 127) / 128) * 9;
     if (launch_gemm_i8<256, EpiQKV>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=
