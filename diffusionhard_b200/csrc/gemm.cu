@@ -254,10 +254,11 @@ struct EpiQKV : EpiBase {
 // x[row, col] += acc * (a_scale * w_scale) + bias  (attention out, MLP down).
 // The residual read-modify-write goes through the staging buffer with one
 // 128-byte row segment per warp instruction.
-template <uint32_t kStages_, uint32_t kHalfCols_>
+template <uint32_t kStages_, uint32_t kHalfCols_, bool kPrefetchNext_ = false>
 struct EpiResidualT : EpiBase {
     static constexpr uint32_t kStages = kStages_;
     static constexpr uint32_t kHalfCols = kHalfCols_;  // columns per epilogue warp (half the tile)
+    static constexpr bool kPrefetchNext = kPrefetchNext_;
     static constexpr uint32_t kChunk = 32;
     // per warp: dequant staging (4 KB), then its 128 columns' w_scale and bias
     static constexpr uint32_t kStagingPerWarp = 32 * 128 + 2 * 512;
@@ -290,6 +291,17 @@ struct EpiResidualT : EpiBase {
         load_x(p, st, ctx, col_start);
         stage_columns(ctx.stage + 4096, ctx.lane, p.w_scale + col_start, p.bias ? p.bias + col_start : nullptr,
                       nullptr, kHalfCols);
+        // The residual rows of this warp's next tile start towards L2 now,
+        // a whole tile ahead of their loads.  For K = 768 the epilogue, not
+        // the tensor core, sets the pace, so DRAM latency would be exposed;
+        // at K = 3072 the tile is long enough that this only adds traffic.
+        if (kPrefetchNext && ctx.has_next && ctx.next_row0 + ctx.lane < ctx.m_eff) {
+            const char* r = reinterpret_cast<const char*>(p.x + static_cast<uint64_t>(ctx.next_row0 + ctx.lane) * p.n +
+                                                          ctx.next_col);
+#pragma unroll
+            for (uint32_t b = 0; b < kHalfCols * 4; b += 128)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(r + b));
+        }
     }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
@@ -327,7 +339,7 @@ struct EpiResidualT : EpiBase {
 };
 // N = 768 runs as 4 column tiles of 192: 1,024 tiles fill 6.9 waves of 148 SMs
 // (128 x 256 tiles would leave the 6th wave 19% full).
-using EpiResidual = EpiResidualT<3, 96>;      // K = 768
+using EpiResidual = EpiResidualT<3, 96, true>;  // K = 768
 using EpiResidualDeep = EpiResidualT<4, 96>;  // K = 3072: deeper TMA pipeline
 using EpiResidual256 = EpiResidualT<3, 128>;  // other N, multiples of 256
 

@@ -52,6 +52,9 @@ struct EpiCtx {
     uint32_t lane;
     uint8_t* stage;    // kStagingPerWarp bytes private to this warp
     uint8_t* extra;    // kExtraSmem bytes shared by the CTA
+    bool has_next;     // this warp has another tile after this one:
+    uint32_t next_row0;  // its first row
+    uint32_t next_col;   // and first column (the warp's half of that tile)
 };
 
 struct GemmShape {
@@ -225,9 +228,11 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t n0 = (tile % n_tiles) * BN;
             const uint32_t row = m0 + row_in_tile;
             const bool row_ok = row < m_eff;
+            const uint32_t next = tile + Cfg::GROUPS * gridDim.x;
             const EpiCtx ctx{row, row_ok, m0 + quad * 32, m_eff, lane,
                              extra_smem + Epi::kExtraSmem + ew * Epi::kStagingPerWarp,
-                             extra_smem};
+                             extra_smem, next < total, (next / n_tiles) * Cfg::BM + quad * 32,
+                             (next % n_tiles) * BN + half * kHalf};
             typename Epi::TileState st;
             // tile_begin runs before the accumulator is ready: a policy may
             // start loads that do not depend on it (row metadata, residual).
