@@ -104,10 +104,74 @@ struct EpiHead : EpiBase {
         st.key_hi = p.row_key_hi ? p.row_key_hi[row] : p.const_key_hi;
         st.ev = p.row_eval ? p.row_eval[row] : p.const_eval;
     }
+    // The common chunk: Philox noise, dequant scores, all 32 columns inside
+    // the vocabulary and none of them the mask token.  Written for
+    // instruction-level parallelism (the chunk is otherwise one long
+    // dependent chain per warp): the 8 Philox blocks and the 32 scores are
+    // independent, and the running maximum is a tree over (score, column)
+    // pairs in which the left (lower-id) side wins ties, so the result equals
+    // the sequential strict-greater scan.
+    static DH_DEVINL void noisy_chunk(const Params& p, TileState& st, uint32_t col0, const uint32_t* v) {
+        const uint32_t gid0 = col0 + p.vocab_offset;
+        int32_t best_s = INT32_MIN;
+        uint32_t best_j = 0;
+#pragma unroll
+        for (uint32_t hh = 0; hh < 2; ++hh) {
+            uint32_t wd[16];
+#pragma unroll
+            for (uint32_t g = 0; g < 4; ++g) {
+                const Philox4 r = philox4x32_10((gid0 >> 2) + 4 * hh + g, st.pos, st.ev, p.stream_id, p.key_lo,
+                                                st.key_hi);
+                wd[4 * g] = r.x;
+                wd[4 * g + 1] = r.y;
+                wd[4 * g + 2] = r.z;
+                wd[4 * g + 3] = r.w;
+            }
+            int32_t sc[16];
+#pragma unroll
+            for (uint32_t q = 0; q < 4; ++q) {
+                const uint32_t c = col0 + 16 * hh + 4 * q;
+                const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.w_scale + c));
+                const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + c));
+                const float ws[4] = {w4.x, w4.y, w4.z, w4.w};
+                const float bs[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                for (uint32_t e = 0; e < 4; ++e) {
+                    const uint32_t j = 4 * q + e;
+                    // |q10| <= 2^30 and |noise| < 2^15: the sum fits in int32
+                    sc[j] = q10(ref_logit(static_cast<int32_t>(v[16 * hh + j]), st.a_scale, ws[e], bs[e])) +
+                            gumbel_q10(wd[j], st.table);
+                }
+            }
+            uint32_t ix[16];
+#pragma unroll
+            for (uint32_t j = 0; j < 16; ++j) ix[j] = 16 * hh + j;
+#pragma unroll
+            for (uint32_t stride = 1; stride < 16; stride <<= 1) {
+#pragma unroll
+                for (uint32_t j = 0; j < 16; j += 2 * stride) {
+                    const bool right = sc[j + stride] > sc[j];
+                    sc[j] = right ? sc[j + stride] : sc[j];
+                    ix[j] = right ? ix[j + stride] : ix[j];
+                }
+            }
+            if (sc[0] > best_s) {
+                best_s = sc[0];
+                best_j = ix[0];
+            }
+        }
+        const unsigned long long pk = pack_score_id(best_s, gid0 + best_j);
+        st.best = pk > st.best ? pk : st.best;
+    }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
         const uint32_t row = ctx.row;
         if (!ctx.row_ok || col0 >= p.vocab) return;
+        if (p.mode == kDequantNoisy && !p.noise && col0 + 32 <= p.vocab &&
+            p.mask_id - (col0 + p.vocab_offset) >= 32u) {
+            noisy_chunk(p, st, col0, v);
+            return;
+        }
         unsigned long long best = st.best;
         if (p.mode == kDequantGreedy) {
 #pragma unroll
