@@ -83,6 +83,10 @@ DH_DEVINL int32_t q10(float logit) {
 
 struct EpiHead : EpiBase {
     static constexpr uint32_t kChunk = 32;
+    // two groups of 8 epilogue warps: the per-logit work (Philox, Gumbel,
+    // dequant, race) is a chain of dependent integer / FP64 operations that
+    // 2 warps per scheduler cannot keep the pipes busy with
+    static constexpr uint32_t kGroups = 2;
     static constexpr uint32_t kExtraSmem = 32 * 256 * 2;  // merged Gumbel table
     using Params = HeadParams;
     struct TileState {
@@ -116,21 +120,21 @@ struct EpiHead : EpiBase {
         int32_t best_s = INT32_MIN;
         uint32_t best_j = 0;
 #pragma unroll
-        for (uint32_t hh = 0; hh < 2; ++hh) {
-            uint32_t wd[16];
+        for (uint32_t qq = 0; qq < 4; ++qq) {  // 8 columns: two Philox blocks
+            uint32_t wd[8];
 #pragma unroll
-            for (uint32_t g = 0; g < 4; ++g) {
-                const Philox4 r = philox4x32_10((gid0 >> 2) + 4 * hh + g, st.pos, st.ev, p.stream_id, p.key_lo,
+            for (uint32_t g = 0; g < 2; ++g) {
+                const Philox4 r = philox4x32_10((gid0 >> 2) + 2 * qq + g, st.pos, st.ev, p.stream_id, p.key_lo,
                                                 st.key_hi);
                 wd[4 * g] = r.x;
                 wd[4 * g + 1] = r.y;
                 wd[4 * g + 2] = r.z;
                 wd[4 * g + 3] = r.w;
             }
-            int32_t sc[16];
+            int32_t sc[8];
 #pragma unroll
-            for (uint32_t q = 0; q < 4; ++q) {
-                const uint32_t c = col0 + 16 * hh + 4 * q;
+            for (uint32_t q = 0; q < 2; ++q) {
+                const uint32_t c = col0 + 8 * qq + 4 * q;
                 const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.w_scale + c));
                 const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + c));
                 const float ws[4] = {w4.x, w4.y, w4.z, w4.w};
@@ -139,17 +143,17 @@ struct EpiHead : EpiBase {
                 for (uint32_t e = 0; e < 4; ++e) {
                     const uint32_t j = 4 * q + e;
                     // |q10| <= 2^30 and |noise| < 2^15: the sum fits in int32
-                    sc[j] = q10(ref_logit(static_cast<int32_t>(v[16 * hh + j]), st.a_scale, ws[e], bs[e])) +
+                    sc[j] = q10(ref_logit(static_cast<int32_t>(v[8 * qq + j]), st.a_scale, ws[e], bs[e])) +
                             gumbel_q10(wd[j], st.table);
                 }
             }
-            uint32_t ix[16];
+            uint32_t ix[8];
 #pragma unroll
-            for (uint32_t j = 0; j < 16; ++j) ix[j] = 16 * hh + j;
+            for (uint32_t j = 0; j < 8; ++j) ix[j] = 8 * qq + j;
 #pragma unroll
-            for (uint32_t stride = 1; stride < 16; stride <<= 1) {
+            for (uint32_t stride = 1; stride < 8; stride <<= 1) {
 #pragma unroll
-                for (uint32_t j = 0; j < 16; j += 2 * stride) {
+                for (uint32_t j = 0; j < 8; j += 2 * stride) {
                     const bool right = sc[j + stride] > sc[j];
                     sc[j] = right ? sc[j + stride] : sc[j];
                     ix[j] = right ? ix[j + stride] : ix[j];
