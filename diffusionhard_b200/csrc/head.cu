@@ -81,6 +81,50 @@ DH_DEVINL int32_t q10(float logit) {
     return __float2int_rn(scaled);
 }
 
+// Philox4x32-10 of counter (c0, pos, ev, stream) under key (key_lo, key_hi)
+// when only c0 changes between calls: the first round's product of the
+// third counter word, and the words it mixes with, are fixed per row and
+// come in precomputed (r0 = hi(M1 * ev) ^ pos ^ key_lo, r1 = lo(M1 * ev),
+// r2 = stream ^ key_hi).  The rounds are those of dh_philox.cuh.
+struct PhiloxRow {
+    uint32_t r0, r1, r2;
+};
+
+DH_DEVINL PhiloxRow philox_row(uint32_t pos, uint32_t ev, uint32_t stream, uint32_t key_lo, uint32_t key_hi) {
+    const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * ev;
+    return PhiloxRow{static_cast<uint32_t>(p1 >> 32) ^ pos ^ key_lo, static_cast<uint32_t>(p1), stream ^ key_hi};
+}
+
+DH_DEVINL Philox4 philox_row_block(uint32_t c0, const PhiloxRow& pr, uint32_t key_lo, uint32_t key_hi) {
+    const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * c0;
+    uint32_t x0 = pr.r0, x1 = pr.r1;
+    uint32_t x2 = static_cast<uint32_t>(p0 >> 32) ^ pr.r2, x3 = static_cast<uint32_t>(p0);
+#pragma unroll
+    for (int r = 1; r < 10; ++r) {
+        key_lo += 0x9E3779B9u;
+        key_hi += 0xBB67AE85u;
+        const uint64_t q0 = static_cast<uint64_t>(0xD2511F53u) * x0;
+        const uint64_t q1 = static_cast<uint64_t>(0xCD9E8D57u) * x2;
+        const uint32_t n0 = static_cast<uint32_t>(q1 >> 32) ^ x1 ^ key_lo;
+        const uint32_t n2 = static_cast<uint32_t>(q0 >> 32) ^ x3 ^ key_hi;
+        x1 = static_cast<uint32_t>(q1);
+        x3 = static_cast<uint32_t>(q0);
+        x0 = n0;
+        x2 = n2;
+    }
+    return Philox4{x0, x1, x2, x3};
+}
+
+// gumbel_q10 with the mantissa taken from d normalised to bit 31 (one
+// variable shift instead of two shift directions): same table index.
+DH_DEVINL int32_t gumbel_q10_norm(uint32_t word, const int16_t* smem_table) {
+    const uint32_t d = ~word;
+    const uint32_t e = __clz(d);
+    const uint32_t m = ((d << e) >> 23) & 0xFFu;
+    const int32_t v = smem_table[(e << 8) | m];
+    return d == 0u ? DH_GUMBEL_TOP_Q10 : v;
+}
+
 struct EpiHead : EpiBase {
     static constexpr uint32_t kChunk = 32;
     // two groups of 8 epilogue warps: the per-logit work (Philox, Gumbel,
@@ -93,6 +137,7 @@ struct EpiHead : EpiBase {
         unsigned long long best;
         float a_scale;
         uint32_t pos, key_hi, ev;
+        PhiloxRow pr;
         const int16_t* table;
     };
     static DH_DEVINL void init_smem(const Params&, uint8_t* extra) {
@@ -107,6 +152,7 @@ struct EpiHead : EpiBase {
         st.pos = p.row_position ? p.row_position[row] : row;
         st.key_hi = p.row_key_hi ? p.row_key_hi[row] : p.const_key_hi;
         st.ev = p.row_eval ? p.row_eval[row] : p.const_eval;
+        st.pr = philox_row(st.pos, st.ev, p.stream_id, p.key_lo, st.key_hi);
     }
     // The common chunk: Philox noise, dequant scores, all 32 columns inside
     // the vocabulary and none of them the mask token.  Written for
@@ -124,8 +170,7 @@ struct EpiHead : EpiBase {
             uint32_t wd[8];
 #pragma unroll
             for (uint32_t g = 0; g < 2; ++g) {
-                const Philox4 r = philox4x32_10((gid0 >> 2) + 2 * qq + g, st.pos, st.ev, p.stream_id, p.key_lo,
-                                                st.key_hi);
+                const Philox4 r = philox_row_block((gid0 >> 2) + 2 * qq + g, st.pr, p.key_lo, st.key_hi);
                 wd[4 * g] = r.x;
                 wd[4 * g + 1] = r.y;
                 wd[4 * g + 2] = r.z;
@@ -144,7 +189,7 @@ struct EpiHead : EpiBase {
                     const uint32_t j = 4 * q + e;
                     // |q10| <= 2^30 and |noise| < 2^15: the sum fits in int32
                     sc[j] = q10(ref_logit(static_cast<int32_t>(v[8 * qq + j]), st.a_scale, ws[e], bs[e])) +
-                            gumbel_q10(wd[j], st.table);
+                            gumbel_q10_norm(wd[j], st.table);
                 }
             }
             uint32_t ix[8];
