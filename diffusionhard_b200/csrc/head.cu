@@ -73,6 +73,35 @@ DH_DEVINL float ref_logit(int32_t acc, float a_scale, float w_scale, float bias)
     return __double2float_rn(v);
 }
 
+// The same logit with the int and float to double conversions done on the
+// integer and FP64 pipes instead of the conversion unit:
+//   double(acc): the double 2^52 + 2^31 + acc assembled from bits, minus
+//   2^52 + 2^31 (exact for any int32);
+//   double(combined): for a positive normal float the double's bits are the
+//   float's re-biased (exact); other values take the converting path.
+DH_DEVINL float ref_logit_bits(int32_t acc, float a_scale, float w_scale, double bias) {
+    const float combined = __fmul_rn(a_scale, w_scale);
+    const double acc_d = __hiloint2double(0x43300000, static_cast<int32_t>(static_cast<uint32_t>(acc) ^ 0x80000000u)) -
+                         4503601774854144.0;  // 2^52 + 2^31
+    const uint32_t cb = __float_as_uint(combined);
+    double comb_d;
+    if (cb - 0x00800000u < 0x7F000000u)  // positive, normal, finite
+        comb_d = __hiloint2double(static_cast<int32_t>((cb >> 3) + 0x38000000u), static_cast<int32_t>(cb << 29));
+    else
+        comb_d = static_cast<double>(combined);
+    return __double2float_rn(__fma_rn(acc_d, comb_d, bias));
+}
+
+DH_DEVINL int32_t q10(float logit);
+
+// q10 with round-half-even through the 1.5 * 2^23 shifter when |x| < 2^22
+// (the common case), else the converting path.
+DH_DEVINL int32_t q10_shift(float logit) {
+    const float scaled = __fmul_rn(logit, 1024.0f);
+    if (fabsf(scaled) < 4194304.0f) return __float_as_int(__fadd_rn(scaled, 12582912.0f)) - 0x4B400000;
+    return q10(logit);
+}
+
 DH_DEVINL int32_t q10(float logit) {
     const float scaled = __fmul_rn(logit, 1024.0f);
     if (!(scaled == scaled)) return -(1 << 30);
@@ -131,6 +160,10 @@ struct EpiHead : EpiBase {
     // dequant, race) is a chain of dependent integer / FP64 operations that
     // 2 warps per scheduler cannot keep the pipes busy with
     static constexpr uint32_t kGroups = 2;
+    static constexpr uint32_t kStages = 3;
+    // per warp: its 128 columns' bias as double (1 KB) and w_scale (512 B),
+    // converted once per tile instead of once per logit
+    static constexpr uint32_t kStagingPerWarp = 1536;
     static constexpr uint32_t kExtraSmem = 32 * 256 * 2;  // merged Gumbel table
     using Params = HeadParams;
     struct TileState {
@@ -139,12 +172,25 @@ struct EpiHead : EpiBase {
         uint32_t pos, key_hi, ev;
         PhiloxRow pr;
         const int16_t* table;
+        const uint8_t* stage;
     };
     static DH_DEVINL void init_smem(const Params&, uint8_t* extra) {
         load_gumbel_table(reinterpret_cast<int16_t*>(extra));
     }
-    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t) {
+    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
         const uint32_t row = ctx.row;
+        if (p.mode == kDequantNoisy) {
+            double* bd = reinterpret_cast<double*>(ctx.stage);
+            float* wsd = reinterpret_cast<float*>(ctx.stage + 1024);
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+                const uint32_t c = col_start + ctx.lane + 32 * i;
+                bd[ctx.lane + 32 * i] = c < p.vocab ? static_cast<double>(__ldg(p.bias + c)) : 0.0;
+                wsd[ctx.lane + 32 * i] = c < p.vocab ? __ldg(p.w_scale + c) : 0.f;
+            }
+            __syncwarp();
+        }
+        st.stage = ctx.stage;
         st.best = 0ull;
         st.table = reinterpret_cast<const int16_t*>(ctx.extra);
         if (!ctx.row_ok) return;
@@ -177,18 +223,21 @@ struct EpiHead : EpiBase {
                 wd[4 * g + 3] = r.w;
             }
             int32_t sc[8];
+            // this warp's staged column parameters (the chunk lies in its half tile)
+            const uint32_t cl = (col0 % 128u) + 8 * qq;
+            const float4* w4p = reinterpret_cast<const float4*>(st.stage + 1024 + cl * 4);
+            const double2* b2p = reinterpret_cast<const double2*>(st.stage + cl * 8);
 #pragma unroll
             for (uint32_t q = 0; q < 2; ++q) {
-                const uint32_t c = col0 + 8 * qq + 4 * q;
-                const float4 w4 = __ldg(reinterpret_cast<const float4*>(p.w_scale + c));
-                const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + c));
+                const float4 w4 = w4p[q];
+                const double2 b01 = b2p[2 * q], b23 = b2p[2 * q + 1];
                 const float ws[4] = {w4.x, w4.y, w4.z, w4.w};
-                const float bs[4] = {b4.x, b4.y, b4.z, b4.w};
+                const double bs[4] = {b01.x, b01.y, b23.x, b23.y};
 #pragma unroll
                 for (uint32_t e = 0; e < 4; ++e) {
                     const uint32_t j = 4 * q + e;
                     // |q10| <= 2^30 and |noise| < 2^15: the sum fits in int32
-                    sc[j] = q10(ref_logit(static_cast<int32_t>(v[8 * qq + j]), st.a_scale, ws[e], bs[e])) +
+                    sc[j] = q10_shift(ref_logit_bits(static_cast<int32_t>(v[8 * qq + j]), st.a_scale, ws[e], bs[e])) +
                             gumbel_q10_norm(wd[j], st.table);
                 }
             }
