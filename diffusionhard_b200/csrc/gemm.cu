@@ -360,9 +360,15 @@ struct EpiGelu : EpiBase {
     static constexpr uint32_t kStages = 3;
     static constexpr uint32_t kGroups = 2;
     static constexpr uint32_t kChunk = 32;
-    // per warp: a 2 KB store source, then its 128 columns' w_scale, bias,
-    // out_scale (a 2 KB slot); 1 KB multiples keep the source swizzle-aligned
-    static constexpr uint32_t kStagingPerWarp = 2 * 2048;
+    static constexpr uint32_t kMaxCols = 3584;
+    // CTA-wide: w_scale, bias and out_scale of every column, copied in once
+    // when the CTA starts (no per-tile staging wait), then one slot of 32
+    // row scales per epilogue warp that carries the next tile's a_scale
+    static constexpr uint32_t kTableBytes = 3 * kMaxCols * 4;
+    static constexpr uint32_t kExtraSmem = kTableBytes + 16 * 128;
+    // per warp: the 2 KB source of its TMA stores (1 KB multiples keep it
+    // aligned for the swizzle)
+    static constexpr uint32_t kStagingPerWarp = 2048;
     struct Params {
         CUtensorMap out_map;  // out as [m, n] bf16, box 32 x 32, 64-byte swizzle
         const float* a_scale;
@@ -375,20 +381,45 @@ struct EpiGelu : EpiBase {
     struct TileState {
         float ab;
     };
-    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
-        st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
-        stage_columns(ctx.stage + 2048, ctx.lane, p.w_scale + col_start, p.bias + col_start,
-                      p.out_scale ? p.out_scale + col_start : nullptr);
+    static DH_DEVINL void init_smem(const Params& p, uint8_t* extra) {
+        const uint32_t pieces = p.n / 4;  // 16-byte pieces per vector
+        for (uint32_t i = threadIdx.x; i < 3 * pieces; i += blockDim.x) {
+            const uint32_t v = i / pieces, j = i % pieces;
+            const float* src = v == 0 ? p.w_scale : (v == 1 ? p.bias : p.out_scale);
+            if (src) cp_async16(extra + v * (kMaxCols * 4) + j * 16, src + j * 4);
+        }
+        cp_async_wait_all();
+    }
+    static DH_DEVINL float* carry_slot(const EpiCtx& ctx) {
+        const uint32_t ew = static_cast<uint32_t>(ctx.stage - (ctx.extra + kExtraSmem)) / kStagingPerWarp;
+        return reinterpret_cast<float*>(ctx.extra + kTableBytes + ew * 128);
+    }
+    // Row scale of this tile (carried from the previous tile's prefetch), and
+    // an asynchronous copy of the next tile's row scales into the carry slot.
+    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t) {
+        float* carry = carry_slot(ctx);
+        if (ctx.first_tile) {
+            st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
+        } else {
+            cp_async_wait_all();
+            __syncwarp();
+            st.ab = carry[ctx.lane];
+        }
+        __syncwarp();
+        if (ctx.has_next && ctx.next_row0 + ctx.lane < ctx.m_eff)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                             static_cast<uint32_t>(__cvta_generic_to_shared(carry + ctx.lane))),
+                         "l"(p.a_scale + ctx.next_row0 + ctx.lane)
+                         : "memory");
     }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
         const float ab = st.ab;
         const uint32_t lane = ctx.lane;
         uint32_t pk[16];
-        const uint8_t* prm = ctx.stage + 2048 + (col0 % 128u) * 4u;
-        const float4* w4 = reinterpret_cast<const float4*>(prm);
-        const float4* b4 = reinterpret_cast<const float4*>(prm + 512);
-        const float4* o4 = reinterpret_cast<const float4*>(prm + 1024);
+        const float4* w4 = reinterpret_cast<const float4*>(ctx.extra + col0 * 4u);
+        const float4* b4 = reinterpret_cast<const float4*>(ctx.extra + kMaxCols * 4 + col0 * 4u);
+        const float4* o4 = reinterpret_cast<const float4*>(ctx.extra + 2 * kMaxCols * 4 + col0 * 4u);
         // two columns per packed fp32x2 instruction:
         //   x = acc * (a_scale * w_scale) + bias
         //   u = k c x^3 + k x                (k = sqrt(2/pi), c = 0.044715)
@@ -666,7 +697,7 @@ extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const in
                                  void* out, uint32_t m,
                                  uint32_t n, uint32_t k, const uint32_t* run_rows, void* stream) {
     if (!a_scale || !w_scale || !bias || !out) return DH_ERR_NULL_POINTER;
-    if (n % 256 != 0) return DH_ERR_UNSUPPORTED_SHAPE;
+    if (n % 256 != 0 || n > EpiGelu::kMaxCols) return DH_ERR_UNSUPPORTED_SHAPE;
     if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(w_scale) |
          reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(out_scale)) & 15u)
         return DH_ERR_ALIGNMENT;

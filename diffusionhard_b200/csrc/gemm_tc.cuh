@@ -52,6 +52,7 @@ struct EpiCtx {
     uint32_t lane;
     uint8_t* stage;    // kStagingPerWarp bytes private to this warp
     uint8_t* extra;    // kExtraSmem bytes shared by the CTA
+    bool first_tile;   // this is the warp's first tile
     bool has_next;     // this warp has another tile after this one:
     uint32_t next_row0;  // its first row
     uint32_t next_col;   // and first column (the warp's half of that tile)
@@ -231,8 +232,8 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t next = tile + Cfg::GROUPS * gridDim.x;
             const EpiCtx ctx{row, row_ok, m0 + quad * 32, m_eff, lane,
                              extra_smem + Epi::kExtraSmem + ew * Epi::kStagingPerWarp,
-                             extra_smem, next < total, (next / n_tiles) * Cfg::BM + quad * 32,
-                             (next % n_tiles) * BN + half * kHalf};
+                             extra_smem, tile == blockIdx.x + group * gridDim.x, next < total,
+                             (next / n_tiles) * Cfg::BM + quad * 32, (next % n_tiles) * BN + half * kHalf};
             typename Epi::TileState st;
             // tile_begin runs before the accumulator is ready: a policy may
             // start loads that do not depend on it (row metadata, residual).
