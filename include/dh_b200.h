@@ -334,7 +334,9 @@ uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, const int8_t* w
                           uint32_t k, const uint32_t* run_rows, void* stream);
 
 /* out[m, n] = bf16(gelu_tanh(dequant(A . W^T) + bias) * out_scale[n]): MLP-up
- * (K7); out_scale (may be NULL) is the SmoothQuant 1/s of MLP-down. */
+ * (K7); out_scale (may be NULL) is the SmoothQuant 1/s of MLP-down.  n is a
+ * multiple of 256 and at most 3584 (the column parameters stay in shared
+ * memory); DH_ERR_UNSUPPORTED_SHAPE otherwise. */
 uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
                       const float* w_scale, const float* bias, const float* out_scale, void* out,
                       uint32_t m, uint32_t n,
