@@ -15,13 +15,12 @@ cache.
 
 from __future__ import annotations
 
-import math
 from typing import Any, Dict, List, Optional
 
 import numpy as np
 
 from . import _lib
-from .model import MDLMConfig, QuantizedMDLM
+from .model import QuantizedMDLM
 from .sampler import NOISE_EPSILON, MDLMStepMeasurement, hardware_candidate_cache_bytes, reveal_thresholds_q32
 
 
