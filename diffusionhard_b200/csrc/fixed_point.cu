@@ -9,6 +9,8 @@
 //                       activations x 16-bit weights, 64-bit
 //                       multiplier, symmetric rounding shift,
 //                       bias, saturation
+//   K15 packed int8     requantised Q / K / V and               attention_int8.py:20-315
+//       attention       probabilities, Q28 score rescale
 //
 // All arithmetic is integer (int64 where the reference's torch int64
 // tensors are), except the float -> fixed conversions, which round
@@ -274,6 +276,211 @@ __global__ void __launch_bounds__(kAttnThreads) fixed_attention_kernel(FixedAttn
     }
 }
 
+// ------------------------------------------- K15 packed int8 attention
+// The paired-token INT8 attention candidates of attention_int8.py: Q / K
+// (rotated Q5.12) and V (Q5.12) requantised to signed integers of
+// `levels` magnitude, scores rescaled to Q7.10 by a Q28 multiplier, the K13
+// LUT softmax, and probabilities optionally requantised to `p_levels`
+// unsigned levels for an integer P . V.
+//   qk_mode 0  Q / K not requantised
+//           1  calibrated-head: one multiplier per head from a calibration
+//              maximum (attention_int8.py:178-190, 212-240)
+//           2  dynamic-vector: one maximum per token vector
+//              (attention_int8.py:61-90, 191-210)
+//   quant_scores  scores from the requantised vectors; else the fixed18
+//              scores of K13 (the vectors are still requantised, for the
+//              saturation counts the reference reports either way)
+// V is requantised when v_levels != 0, and P . V runs on the requantised
+// probabilities and values when p_levels != 0 (which needs v_levels).
+// Per-head parameters, int64 [H][8]: query / key / value multipliers
+// round(levels * 2^frac / maximum), the calibrated score multiplier, the
+// output multiplier round(v_max * 2^24 / (v_levels * p_levels)), and the
+// query / key / value calibration maxima (saturation counts only).
+enum : uint32_t { kPkQMult, kPkKMult, kPkVMult, kPkScoreMult, kPkOutMult, kPkQMax, kPkKMax, kPkVMax, kPkParams };
+
+struct PackedQuantArgs {
+    const int32_t* q12;    // [T, H, 64] rotated query, Q5.12
+    const int32_t* k12;    // [T, H, 64] rotated key
+    const int32_t* qkv12;  // [T, 3, H, 64]; value at which = 2
+    uint32_t T, H, qk_mode, qk_levels, qk_frac, v_levels;
+    const long long* params;  // [H][kPkParams]
+    int32_t* q8;  // [T, H, 64] requantised query (qk_mode != 0)
+    int32_t* k8;
+    int32_t* v8;  // [T, H, 64] requantised value (v_levels != 0)
+    int32_t* q_max;  // [T, H] dynamic vector maxima (qk_mode 2)
+    int32_t* k_max;
+    long long* head_stats;  // [H][4]: saturated query / key / value inputs, zero probabilities
+};
+
+// One warp per (token, head, q | k | v) vector of 64; lane holds elements
+// lane and lane + 32.  q = clamp(sym_round_shift(x * multiplier, frac),
+// -levels, levels) (attention_int8.py:20-25, 181-190).
+__global__ void __launch_bounds__(256) packed_quant_kernel(PackedQuantArgs a) {
+    const uint32_t wg = blockIdx.x * (blockDim.x / 32) + warp_id();
+    if (wg >= a.T * a.H * 3) return;
+    const uint32_t which = wg % 3, row = wg / 3;  // row = t * H + h
+    const uint32_t h = row % a.H, t = row / a.H;
+    if (which < 2 && a.qk_mode == 0) return;
+    if (which == 2 && a.v_levels == 0) return;
+    const uint32_t lane = lane_id();
+    const int32_t* src = which == 0   ? a.q12 + static_cast<uint64_t>(row) * 64
+                         : which == 1 ? a.k12 + static_cast<uint64_t>(row) * 64
+                                      : a.qkv12 + ((static_cast<uint64_t>(t) * 3 + 2) * a.H + h) * 64;
+    const long long x0 = src[lane], x1 = src[lane + 32];
+    const long long* prm = a.params + static_cast<uint64_t>(h) * kPkParams;
+    long long mult, levels, sat = 0;
+    uint32_t frac;
+    if (which == 2 || a.qk_mode == 1) {
+        mult = prm[which == 0 ? kPkQMult : which == 1 ? kPkKMult : kPkVMult];
+        const long long cal = prm[which == 0 ? kPkQMax : which == 1 ? kPkKMax : kPkVMax];
+        frac = which == 2 ? 24u : a.qk_frac;
+        levels = which == 2 ? a.v_levels : a.qk_levels;
+        sat = ((x0 < 0 ? -x0 : x0) > cal ? 1 : 0) + ((x1 < 0 ? -x1 : x1) > cal ? 1 : 0);
+    } else {
+        // dynamic: this vector's own maximum (at least 1); the multiplier
+        // rounds the correctly rounded double quotient half-to-even like
+        // torch.round
+        long long m = max(x0 < 0 ? -x0 : x0, x1 < 0 ? -x1 : x1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        m = m < 1 ? 1 : m;
+        frac = a.qk_frac;
+        levels = a.qk_levels;
+        mult = static_cast<long long>(rint(static_cast<double>(levels << frac) / static_cast<double>(m)));
+        if (lane == 0) (which == 0 ? a.q_max : a.k_max)[row] = static_cast<int32_t>(m);
+    }
+    int32_t* dst = (which == 0 ? a.q8 : which == 1 ? a.k8 : a.v8) + static_cast<uint64_t>(row) * 64;
+    dst[lane] = static_cast<int32_t>(clampll(sym_round_shift(x0 * mult, frac), -levels, levels));
+    dst[lane + 32] = static_cast<int32_t>(clampll(sym_round_shift(x1 * mult, frac), -levels, levels));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sat += __shfl_xor_sync(0xFFFFFFFFu, sat, o);
+    if (lane == 0 && sat && a.head_stats)
+        atomicAdd(reinterpret_cast<unsigned long long*>(a.head_stats + h * 4 + which),
+                  static_cast<unsigned long long>(sat));
+}
+
+struct PackedAttnArgs {
+    const int32_t* q;      // [T, H, 64]: requantised (quant_scores) or rotated Q5.12
+    const int32_t* k;
+    const int32_t* v8;     // [T, H, 64] requantised value (p_levels != 0)
+    const int32_t* qkv12;  // [T, 3, H, 64] (p_levels == 0)
+    const int32_t* q_max;  // [T, H] (qk_mode 2)
+    const int32_t* k_max;
+    const long long* params;
+    uint32_t T, H, qk_mode, quant_scores, qk_levels, p_levels, sum_correction;
+    uint32_t address_shift, lut_entries;
+    long long cutoff;
+    const int32_t* lut;
+    int32_t* out;       // [T, H * 64] Q5.12
+    int32_t* scores;    // optional [H, T, T] Q7.10
+    int32_t* probs;     // optional [H, T, T] Q0.16
+    int32_t* probs_q;   // optional [H, T, T] requantised probabilities (after the sum correction)
+    long long* head_stats;
+};
+
+// One CTA per (head, query row), like K13.
+__global__ void __launch_bounds__(kAttnThreads) packed_attention_kernel(PackedAttnArgs a) {
+    __shared__ int32_t sc[kMaxTokens];
+    __shared__ int32_t qrow[64];
+    __shared__ long long scratch[32];
+    __shared__ long long part[kAttnThreads];
+    const uint32_t h = blockIdx.x % a.H, t = blockIdx.x / a.H;
+    const uint32_t T = a.T;
+    const long long lo = -(1ll << 17), hi = (1ll << 17) - 1;
+    const long long* prm = a.params + static_cast<uint64_t>(h) * kPkParams;
+    if (threadIdx.x < 64) qrow[threadIdx.x] = a.q[(static_cast<uint64_t>(t) * a.H + h) * 64 + threadIdx.x];
+    __syncthreads();
+    // Q28 score multiplier: per head (calibrated) or per (query, key) pair
+    // from the two vector maxima (dynamic; attention_int8.py:81-86, 215-228)
+    const double qm =
+        a.quant_scores && a.qk_mode == 2 ? static_cast<double>(a.q_max[static_cast<uint64_t>(t) * a.H + h]) : 0.0;
+    const double denom = static_cast<double>(static_cast<long long>(a.qk_levels) * a.qk_levels * (1ll << 17));
+    long long rmax = LLONG_MIN;
+    for (uint32_t s = threadIdx.x; s < T; s += blockDim.x) {
+        const int32_t* kr = a.k + (static_cast<uint64_t>(s) * a.H + h) * 64;
+        long long dot = 0;
+#pragma unroll 8
+        for (uint32_t d = 0; d < 64; ++d) dot += static_cast<long long>(qrow[d]) * kr[d];
+        long long u;
+        if (!a.quant_scores) {
+            u = sym_round_shift(dot, 17);
+        } else {
+            long long m = prm[kPkScoreMult];
+            if (a.qk_mode == 2)
+                m = static_cast<long long>(
+                    rint(qm * static_cast<double>(a.k_max[static_cast<uint64_t>(s) * a.H + h]) * 268435456.0 / denom));
+            u = sym_round_shift(dot * m, 28);
+        }
+        const long long sv = clampll(u, lo, hi);
+        sc[s] = static_cast<int32_t>(sv);
+        rmax = max(rmax, sv);
+    }
+    rmax = block_max_ll(rmax, scratch);
+    long long esum = 0;
+    for (uint32_t s = threadIdx.x; s < T; s += blockDim.x) {
+        long long dl = sc[s] - rmax;
+        dl = dl < -a.cutoff ? -a.cutoff : dl;
+        long long addr = (-dl + (1ll << (a.address_shift - 1))) >> a.address_shift;
+        addr = addr > a.lut_entries - 1 ? a.lut_entries - 1 : addr;
+        if (a.scores) a.scores[(static_cast<uint64_t>(h) * T + t) * T + s] = sc[s];
+        sc[s] = a.lut[addr];
+        esum += sc[s];
+    }
+    esum = block_sum(esum, scratch);
+    const long long recip = ((1ll << 30) + esum / 2) / esum;
+    // Q0.16 probabilities; with p_levels, requantised to
+    // clamp((p * levels + 2^15) >> 16, 0, levels), counting zeros, and the
+    // (first) largest Q0.16 probability tracked for the sum correction
+    long long qsum = 0, zeros = 0, best = -1;
+    for (uint32_t s = threadIdx.x; s < T; s += blockDim.x) {
+        long long p = (static_cast<long long>(sc[s]) * recip + (1ll << 13)) >> 14;
+        p = p > 65535 ? 65535 : p;
+        if (a.probs) a.probs[(static_cast<uint64_t>(h) * T + t) * T + s] = static_cast<int32_t>(p);
+        if (a.p_levels) {
+            const long long key = (p << 12) | (4095 - s);  // larger p, then lower index
+            best = max(best, key);
+            long long pq = (p * a.p_levels + (1ll << 15)) >> 16;
+            pq = clampll(pq, 0, a.p_levels);
+            zeros += pq == 0 ? 1 : 0;
+            qsum += pq;
+            p = pq;
+        }
+        sc[s] = static_cast<int32_t>(p);
+    }
+    if (a.p_levels) {
+        qsum = block_sum(qsum, scratch);
+        zeros = block_sum(zeros, scratch);
+        best = block_max_ll(best, scratch);  // its barrier orders every sc write above
+        if (a.sum_correction && threadIdx.x == 0) sc[4095 - (best & 4095)] += static_cast<int32_t>(a.p_levels - qsum);
+        __syncthreads();
+        if (a.probs_q)
+            for (uint32_t s = threadIdx.x; s < T; s += blockDim.x)
+                a.probs_q[(static_cast<uint64_t>(h) * T + t) * T + s] = sc[s];
+    } else {
+        __syncthreads();
+    }
+    // P . V: thread (d, half) sums keys s = half, half + 2, ...
+    const uint32_t d = threadIdx.x & 63u, half = threadIdx.x >> 6;
+    long long acc = 0;
+    if (a.p_levels) {
+        for (uint32_t s = half; s < T; s += 2)
+            acc += static_cast<long long>(sc[s]) * a.v8[(static_cast<uint64_t>(s) * a.H + h) * 64 + d];
+    } else {
+        for (uint32_t s = half; s < T; s += 2)
+            acc += static_cast<long long>(sc[s]) * a.qkv12[((static_cast<uint64_t>(s) * 3 + 2) * a.H + h) * 64 + d];
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.x < 64) {
+        const long long tot = part[threadIdx.x] + part[threadIdx.x + 64];
+        const long long y = a.p_levels ? sym_round_shift(tot * prm[kPkOutMult], 24) : sym_round_shift(tot, 16);
+        a.out[static_cast<uint64_t>(t) * a.H * 64 + h * 64 + d] = static_cast<int32_t>(clampll(y, lo, hi));
+    }
+    if (threadIdx.x == 0 && a.p_levels && zeros && a.head_stats)
+        atomicAdd(reinterpret_cast<unsigned long long*>(a.head_stats + h * 4 + 3),
+                  static_cast<unsigned long long>(zeros));
+}
+
 constexpr uint32_t kLinTile = 64, kLinK = 32;
 
 struct WideLinearArgs {
@@ -429,6 +636,52 @@ uint32_t dh_fixed_wide_linear(const int32_t* activation, const int16_t* weight, 
                      reinterpret_cast<long long*>(accumulators), reinterpret_cast<long long*>(stats)};
     dim3 grid((n + kLinTile - 1) / kLinTile, (rows + kLinTile - 1) / kLinTile);
     fixed_wide_linear_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+uint32_t dh_packed_int8_attention_q12(const int32_t* query_q12, const int32_t* key_q12, const int32_t* qkv_q12,
+                                      uint32_t tokens, uint32_t heads, uint32_t qk_mode, uint32_t qk_scores,
+                                      uint32_t qk_levels, uint32_t qk_fraction_bits, uint32_t pv_probability_levels,
+                                      uint32_t pv_sum_correction, uint32_t pv_value_levels,
+                                      const int64_t* head_params, uint32_t exponential_step_bits, int64_t cutoff_q10,
+                                      const int32_t* exponential_lut_q16, uint32_t lut_entries, int32_t* workspace,
+                                      int32_t* out_q12, int32_t* scores_q10, int32_t* probabilities_q16,
+                                      int32_t* probabilities_quantized, int32_t* query_maxima,
+                                      int32_t* key_maxima, int64_t* head_stats, void* stream) {
+    if (!query_q12 || !key_q12 || !qkv_q12 || !head_params || !exponential_lut_q16 || !out_q12)
+        return DH_ERR_NULL_POINTER;
+    if (qk_mode > 2 || exponential_step_bits < 1 || exponential_step_bits > 9 || cutoff_q10 <= 0 ||
+        lut_entries == 0 || pv_probability_levels > 65535 || pv_value_levels > 32767)
+        return DH_ERR_INVALID_ARGUMENT;
+    if (qk_mode != 0 && (qk_levels < 1 || qk_levels > 32767 || qk_fraction_bits < 1 || qk_fraction_bits > 30))
+        return DH_ERR_INVALID_ARGUMENT;
+    if ((pv_probability_levels != 0 && pv_value_levels == 0) || (qk_scores && qk_mode == 0))
+        return DH_ERR_INVALID_ARGUMENT;
+    if ((qk_mode != 0 || pv_value_levels != 0) && !workspace) return DH_ERR_NULL_POINTER;
+    if (qk_mode == 2 && (!query_maxima || !key_maxima)) return DH_ERR_NULL_POINTER;
+    if (tokens == 0 || heads == 0) return DH_OK;
+    if (tokens > kMaxTokens) return DH_ERR_UNSUPPORTED_SHAPE;
+    const uint64_t vec = static_cast<uint64_t>(tokens) * heads * 64;
+    int32_t* q8 = workspace;
+    int32_t* k8 = workspace ? workspace + vec : nullptr;
+    int32_t* v8 = workspace ? workspace + 2 * vec : nullptr;
+    const long long* prm = reinterpret_cast<const long long*>(head_params);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (qk_mode != 0 || pv_value_levels != 0) {
+        PackedQuantArgs qa{query_q12, key_q12, qkv_q12, tokens, heads, qk_mode, qk_levels, qk_fraction_bits,
+                           pv_value_levels, prm, q8, k8, v8, query_maxima, key_maxima,
+                           reinterpret_cast<long long*>(head_stats)};
+        const uint32_t warps = tokens * heads * 3;
+        packed_quant_kernel<<<(warps + 7) / 8, 256, 0, st>>>(qa);
+        DH_LAUNCH_CHECK();
+    }
+    PackedAttnArgs aa{qk_scores ? q8 : query_q12, qk_scores ? k8 : key_q12, v8, qkv_q12, query_maxima, key_maxima,
+                      prm, tokens, heads, qk_mode, qk_scores ? 1u : 0u, qk_levels, pv_probability_levels,
+                      pv_sum_correction ? 1u : 0u, 10u - exponential_step_bits, lut_entries,
+                      static_cast<long long>(cutoff_q10), exponential_lut_q16, out_q12, scores_q10,
+                      probabilities_q16, probabilities_quantized, reinterpret_cast<long long*>(head_stats)};
+    packed_attention_kernel<<<tokens * heads, kAttnThreads, 0, st>>>(aa);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }

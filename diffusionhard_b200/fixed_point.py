@@ -9,8 +9,9 @@ Drop-ins for the reference's fixed-point block validation
 * ``fixed_attention_projection_q10`` (:301-364);
 * ``fixed_qkv_projection_q12`` (:367-494);
 * the package sweeps ``sweep_fixed_layer_norm`` (fixed_norm.py:107-183),
-  ``sweep_fixed_rotary`` (fixed_attention.py:116-171) and
-  ``sweep_fixed_attention`` (:658-841).
+  ``sweep_fixed_rotary`` (fixed_attention.py:116-171),
+  ``sweep_qkv_weight_precision`` (:497-655) and ``sweep_fixed_attention``
+  (:658-841).
 
 They take the same arguments, raise the same errors, and return the same
 outputs, tensors and metrics.  The integer stages run in
@@ -528,4 +529,74 @@ def sweep_fixed_attention(package_dir: Any, *, device: Any = "cuda") -> Dict[str
         },
         "scope": ("all twelve complete H0 attention, folded output projection, and "
                   "residual boundaries on one frozen input"),
+    }
+
+
+def sweep_qkv_weight_precision(package_dir: Any, *, weight_bits: Tuple[int, ...] = (8, 16),
+                               smoothquant_alphas: Tuple[Optional[float], ...] = (None,),
+                               device: Any = "cuda") -> Dict[str, object]:
+    """QKV weight widths (and SmoothQuant equalisation of the 8-bit design)
+    at every captured attention boundary of a package: fixed LayerNorm ->
+    fixed QKV projection -> fixed attention, against the package's float
+    goldens (fixed_attention.py:497-655)."""
+    if not weight_bits or any(bits not in (8, 16) for bits in weight_bits):
+        raise ValueError("weight_bits must contain only 8 or 16")
+    if not smoothquant_alphas or any(alpha is not None and not 0.0 <= alpha <= 1.0 for alpha in smoothquant_alphas):
+        raise ValueError("smoothquant_alphas must contain none or values from zero to one")
+    package_dir = Path(package_dir)
+    names = ["folded.embedding"]
+    for b in range(12):
+        names += ["folded.block_%02d.%s" % (b, s) for s in ("qkv", "attention", "output")]
+    g = _package_tensors(package_dir / "golden_tensors.safetensors", names)
+    wn = []
+    for b in range(12):
+        wn += ["block_%02d.qkv.weight" % b, "block_%02d.qkv.bias" % b]
+    tables = _package_tensors(package_dir / "folded_fp16_weights.safetensors", ["rotary.cos", "rotary.sin", *wn])
+    cos, sin = tables["rotary.cos"].float(), tables["rotary.sin"].float()
+    # the fixed LayerNorm of each boundary does not depend on the design
+    normalized = []
+    for b in range(12):
+        residual = g["folded.embedding"][0] if b == 0 else g["folded.block_%02d.output" % (b - 1)][0]
+        normalized.append(fixed_layer_norm_q12(residual, device=device)[1])
+    designs = []
+    for bits in weight_bits:
+        for alpha in (smoothquant_alphas if bits == 8 else (None,)):
+            blocks = []
+            for b in range(12):
+                fixed_qkv, _, qd = fixed_qkv_projection_q12(normalized[b], tables["block_%02d.qkv.weight" % b],
+                                                            tables["block_%02d.qkv.bias" % b], weight_bits=bits,
+                                                            smoothquant_alpha=alpha, device=device)
+                attention, _, ad = fixed_attention_q12(fixed_qkv, cos, sin, device=device)
+                blocks.append({
+                    "block": b,
+                    "qkv_accuracy_vs_h0": _error_metrics(fixed_qkv, g["folded.block_%02d.qkv" % b][0]),
+                    "attention_accuracy_vs_h0": _error_metrics(attention, g["folded.block_%02d.attention" % b][0]),
+                    "qkv_projection": qd["metrics"],
+                    "attention": ad["metrics"],
+                })
+            qe = [x["qkv_accuracy_vs_h0"]["relative_rms_error"] for x in blocks]
+            ae = [x["attention_accuracy_vs_h0"]["relative_rms_error"] for x in blocks]
+            designs.append({
+                "weight_bits": bits,
+                "smoothquant_alpha": alpha,
+                "blocks": blocks,
+                "summary": {
+                    "mean_qkv_relative_rms_vs_h0": statistics.mean(qe),
+                    "maximum_qkv_relative_rms_vs_h0": max(qe),
+                    "mean_attention_relative_rms_vs_h0": statistics.mean(ae),
+                    "maximum_attention_relative_rms_vs_h0": max(ae),
+                    "maximum_qkv_output_saturation_fraction": max(
+                        x["qkv_projection"]["output_saturation_fraction"] for x in blocks),
+                    "maximum_smoothed_activation_saturation_fraction": max(
+                        x["qkv_projection"]["smoothed_activation_saturation_fraction"] for x in blocks),
+                    "minimum_score_argmax_agreement": min(x["attention"]["score_argmax_agreement"] for x in blocks),
+                },
+            })
+    return {
+        "package_dir": str(package_dir),
+        "block_count": 12,
+        "designs": designs,
+        "scope": "all twelve H0 QKV projection and attention boundaries on one frozen input",
+        "limitation": ("boundary fidelity screen only; fresh-canvas final-logit and "
+                       "generation validation remains required before changing RTL"),
     }

@@ -267,7 +267,8 @@ def rope_tables(positions: int, head_dim: int = 64):
 
 
 def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict[str, np.ndarray]] = None,
-                 threads: Optional[int] = None, captured: Optional[Dict[str, object]] = None) -> np.ndarray:
+                 threads: Optional[int] = None, captured: Optional[Dict[str, object]] = None,
+                 attention: Optional[object] = None) -> np.ndarray:
     """Folded fp32 forward (hardware_package.folded_mdlm_forward semantics);
     returns the final hidden state after LayerNorm (unaffine).  When
     `record_amax` is given, the per-input-channel max |activation| of every
@@ -276,7 +277,11 @@ def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict
     reference's golden names (hardware_package.py:195-289):
     folded.embedding, folded.block_NN.{norm1_unaffine, qkv, attention,
     attention_projection, after_attention, norm2_unaffine, mlp_up, gelu,
-    mlp_down, output}, folded.final.norm_unaffine."""
+    mlp_down, output}, folded.final.norm_unaffine.  `attention(block, qkv)`,
+    when given, replaces the float attention of each block: qkv is the fp32
+    [B, L, 3 * hidden] projection and the result the [B, L, hidden]
+    attention output (the error-propagating screens of attention_int8.py:
+    689-936 substitute an integer attention there)."""
     import torch
     import torch.nn.functional as F
 
@@ -310,11 +315,14 @@ def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict
             cap(pre + ".norm1_unaffine", h)
             qkv = F.linear(h, torch.from_numpy(blk["qkv"].weight), torch.from_numpy(blk["qkv"].bias))
             cap(pre + ".qkv", qkv)
-            qkv = qkv.view(B, L, 3, cfg.heads, cfg.head_dim)
-            q, k, v = qkv.unbind(dim=2)
-            q, k = rot(q), rot(k)
-            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
-            a = a.transpose(1, 2).reshape(B, L, cfg.hidden)
+            if attention is not None:
+                a = attention(i, qkv).to(torch.float32).reshape(B, L, cfg.hidden)
+            else:
+                qkv = qkv.view(B, L, 3, cfg.heads, cfg.head_dim)
+                q, k, v = qkv.unbind(dim=2)
+                q, k = rot(q), rot(k)
+                a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
+                a = a.transpose(1, 2).reshape(B, L, cfg.hidden)
             rec(f"b{i}.out", a)
             cap(pre + ".attention", a)
             proj = F.linear(a, torch.from_numpy(blk["out"].weight))

@@ -285,6 +285,42 @@ uint32_t dh_fixed_wide_linear(const int32_t* activation, const int16_t* weight, 
                               int64_t output_min, int64_t output_max, int32_t* out, int64_t* accumulators,
                               int64_t* stats, void* stream);
 
+/* The packed INT8 attention candidates of attention_int8.py (:20-315):
+ * dynamic_qk_fixed_pv_attention_q12 and _evaluate_with_fixed_maxima after the
+ * rotary stage.  Q / K [tokens, heads, 64] (rotated Q5.12) are requantised
+ * per qk_mode -- 0 not at all, 1 one calibrated multiplier per head, 2 one
+ * maximum per token vector with multiplier rint(qk_levels *
+ * 2^qk_fraction_bits / max) (maxima written to query_maxima / key_maxima
+ * [tokens, heads]) -- as clamp(sym_round_shift(x * multiplier,
+ * qk_fraction_bits), +-qk_levels).  With qk_scores (needs qk_mode != 0),
+ * scores = clamp(sym_round_shift(dot * m, 28), +-2^17) with m the per-head
+ * calibrated multiplier or rint(q_max * k_max * 2^28 / (qk_levels^2 *
+ * 2^17)); else the fixed18 scores of dh_fixed_attention_q12.  Then its LUT
+ * softmax.  V is requantised to pv_value_levels (per-head multiplier, 24
+ * fraction bits) when that is non-zero.  With pv_probability_levels != 0
+ * (needs pv_value_levels), p is requantised to clamp((p * levels + 2^15) >>
+ * 16, 0, levels) (the residual levels - sum added at the first largest p
+ * when pv_sum_correction) and out = clamp(sym_round_shift(sum p * v *
+ * output multiplier, 24), +-2^17); else out = clamp(sym_round_shift(sum p *
+ * v_q12, 16), +-2^17).  head_params: int64 [heads][8] = query, key, value
+ * multipliers, calibrated score multiplier, output multiplier, query, key,
+ * value calibration maxima.  workspace: int32 [3 * tokens * heads * 64]
+ * (may be NULL when qk_mode = 0 and pv_value_levels = 0).  Optional outputs
+ * (may be NULL): scores_q10, probabilities_q16, probabilities_quantized
+ * [heads, tokens, tokens]; head_stats int64 [heads][4] (zeroed by the
+ * caller) = query, key and value inputs above their calibration maxima and
+ * requantised probabilities of 0 (before the sum correction).
+ * tokens <= 2048. */
+uint32_t dh_packed_int8_attention_q12(const int32_t* query_q12, const int32_t* key_q12, const int32_t* qkv_q12,
+                                      uint32_t tokens, uint32_t heads, uint32_t qk_mode, uint32_t qk_scores,
+                                      uint32_t qk_levels, uint32_t qk_fraction_bits, uint32_t pv_probability_levels,
+                                      uint32_t pv_sum_correction, uint32_t pv_value_levels,
+                                      const int64_t* head_params, uint32_t exponential_step_bits, int64_t cutoff_q10,
+                                      const int32_t* exponential_lut_q16, uint32_t lut_entries, int32_t* workspace,
+                                      int32_t* out_q12, int32_t* scores_q10, int32_t* probabilities_q16,
+                                      int32_t* probabilities_quantized, int32_t* query_maxima,
+                                      int32_t* key_maxima, int64_t* head_stats, void* stream);
+
 /* ------------------------------------------------------- DDiT forward path */
 /* W8A8 convention (fixed_mlp.quantized_linear, fixed_mlp.py:65-136, with static
  * SmoothQuant scales s per input channel): an activation row a is quantised as
