@@ -13,12 +13,16 @@ device kernels.
   validate-hardware-fixed-mlp     cli.py:187-200, 905-917
   sweep-hardware-fixed-mlp        cli.py:202-213
   sweep-fixed-layernorm / sweep-fixed-rotary / sweep-fixed-attention   cli.py:240-258
+  sweep-qkv-weight-precision      cli.py:260-272, 986-1000
+  screen-packed-int8-attention / -heldout / -logits   cli.py:286-342, 1017-1058
   benchmark-mdlm-event        cli.py:397-409 (benchmark-mdlm-apple, apple_mdlm.py:203-390),
                               also accepted under the reference's name
 
 Differences, all forced by what a run here has:
 - no checkpoint: --model-id / --revision / --local-files-only are recorded
-  but the weights are the seeded random-init stand-in (--weights-seed);
+  but the weights are the seeded random-init stand-in (--weights-seed), or
+  an HF-layout model.safetensors given by --checkpoint where a command
+  takes one;
 - no tokenizer: text is not decoded and --prefix-text is refused, while
   --prefix-tokens takes a seeded synthetic prefix;
 - no dataset: windows are seeded synthetic ids;
@@ -170,6 +174,41 @@ def build_parser() -> argparse.ArgumentParser:
         fx = sub.add_parser(name, help=help_text + " (on the GPU)")
         fx.add_argument("--package-dir", type=Path, required=True)
         fx.add_argument("--out", type=Path)
+
+    qkvp = sub.add_parser("sweep-qkv-weight-precision",
+                          help="compare INT8 and INT16 QKV weights at all H0 boundaries (on the GPU)")
+    qkvp.add_argument("--package-dir", type=Path, required=True)
+    qkvp.add_argument("--weight-bits", type=int, nargs="+", choices=[8, 16], default=[8, 16])
+    qkvp.add_argument("--smoothquant-alphas", type=float, nargs="+", default=[])
+    qkvp.add_argument("--out", type=Path)
+
+    ia = sub.add_parser("screen-packed-int8-attention",
+                        help="screen paired-token INT8 QK and PV on all captured H0 blocks (on the GPU)")
+    ia.add_argument("--package-dir", type=Path, required=True)
+    ia.add_argument("--out", type=Path)
+    for name, help_text in (("screen-packed-int8-attention-heldout",
+                             "apply captured INT8 attention calibration to fresh canvases"),
+                            ("screen-packed-int8-attention-logits",
+                             "propagate packed INT8 attention error through all twelve blocks")):
+        sc = sub.add_parser(name, help=help_text + " (on the GPU)")
+        sc.add_argument("--package-dir", type=Path, required=True)
+        sc.add_argument("--device", choices=["auto", "cuda"], default="auto")
+        sc.add_argument("--seeds", type=int, nargs="+")
+        sc.add_argument("--model-id", default=DEFAULT_MODEL_ID)
+        sc.add_argument("--revision", default=DEFAULT_REVISION)
+        sc.add_argument("--checkpoint", type=Path, help="HF-layout model.safetensors (default: the stand-in)")
+        sc.add_argument("--weights-seed", type=int, default=0)
+        sc.add_argument("--out", type=Path)
+        if name.endswith("-logits"):
+            sc.add_argument("--preserve-qk18", action="store_true")
+            sc.add_argument("--preserve-pv18", action="store_true")
+            sc.add_argument("--qk-bits", type=int, choices=[8, 9], default=8)
+            sc.add_argument("--qk-scale-mode", choices=["calibrated-head", "dynamic-vector"],
+                            default="calibrated-head")
+            sc.add_argument("--qk-multiplier-fraction-bits", type=int, choices=[17, 24], default=24)
+            sc.add_argument("--pv-probability-levels", type=int, choices=[127, 255], default=127)
+            sc.add_argument("--pv-probability-sum-correction", action="store_true")
+            sc.add_argument("--pv-value-bits", type=int, choices=[8, 9], default=8)
 
     cond = sub.add_parser("generate-mdlm-conditioned",
                           help="compare conditioned DDPM generation with retained prefix K/V")
@@ -365,6 +404,39 @@ def main(argv: Optional[List[str]] = None) -> int:
               "sweep-fixed-rotary": fixed_point.sweep_fixed_rotary,
               "sweep-fixed-attention": fixed_point.sweep_fixed_attention}[args.command]
         _emit(fn(args.package_dir), args.out)
+        return 0
+    if args.command == "sweep-qkv-weight-precision":
+        from .fixed_point import sweep_qkv_weight_precision
+
+        _emit(sweep_qkv_weight_precision(args.package_dir, weight_bits=tuple(args.weight_bits),
+                                         smoothquant_alphas=tuple(args.smoothquant_alphas) or (None,)), args.out)
+        return 0
+    if args.command == "screen-packed-int8-attention":
+        from .attention_int8 import screen_packed_int8_attention
+
+        _emit(screen_packed_int8_attention(args.package_dir), args.out)
+        return 0
+    if args.command in ("screen-packed-int8-attention-heldout", "screen-packed-int8-attention-logits"):
+        from . import attention_int8
+        from .checkpoint import checkpoint_module
+        from .model import MDLMConfig, build_standin
+
+        cfg = MDLMConfig()
+        module = checkpoint_module(args.checkpoint, cfg) if args.checkpoint else build_standin(cfg, args.weights_seed)
+        if args.command.endswith("-heldout"):
+            report = attention_int8.screen_packed_int8_attention_heldout(args.package_dir, seeds=args.seeds,
+                                                                        device=args.device, model=module)
+        else:
+            report = attention_int8.screen_packed_int8_attention_logits(
+                args.package_dir, seeds=args.seeds, device=args.device, quantize_qk=not args.preserve_qk18,
+                quantize_pv=not args.preserve_pv18, qk_bits=args.qk_bits, qk_scale_mode=args.qk_scale_mode,
+                qk_multiplier_fraction_bits=args.qk_multiplier_fraction_bits,
+                pv_probability_levels=args.pv_probability_levels,
+                pv_probability_sum_correction=args.pv_probability_sum_correction, pv_value_bits=args.pv_value_bits,
+                model=module)
+        if not args.checkpoint:
+            report.update(_checkpoint_note(args))
+        _emit(report, args.out)
         return 0
     if args.command == "generate-mdlm-conditioned":
         from .conditioned import evaluate_conditioned_mdlm_ddpm

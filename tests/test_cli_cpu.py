@@ -17,7 +17,7 @@ def _flags(sub):
     return {o for a in action.choices[sub]._actions for o in a.option_strings if o.startswith("--")}
 
 
-# flags of the reference subcommands (cli.py:155-213, 375-409, 552-563, 666-682, 724-739, 769-807)
+# flags of the reference subcommands (cli.py:155-213, 260-342, 375-409, 552-563, 666-682, 724-739, 769-807)
 REFERENCE_FLAGS = {
     "trace-mdlm": {"--out", "--model-id", "--revision", "--device", "--canvas-tokens", "--steps", "--warmup",
                    "--seed", "--sampler", "--local-files-only"},
@@ -48,6 +48,14 @@ REFERENCE_FLAGS = {
     "sweep-fixed-attention": {"--package-dir", "--out"},
     "benchmark-mdlm-apple": {"--out", "--model-id", "--revision", "--device", "--canvas-tokens", "--steps",
                              "--seeds", "--local-files-only"},
+    # cli.py:260-272, 286-342
+    "sweep-qkv-weight-precision": {"--package-dir", "--weight-bits", "--smoothquant-alphas", "--out"},
+    "screen-packed-int8-attention": {"--package-dir", "--out"},
+    "screen-packed-int8-attention-heldout": {"--package-dir", "--device", "--seeds", "--out"},
+    "screen-packed-int8-attention-logits": {"--package-dir", "--device", "--seeds", "--preserve-qk18",
+                                            "--preserve-pv18", "--qk-bits", "--qk-scale-mode",
+                                            "--qk-multiplier-fraction-bits", "--pv-probability-levels",
+                                            "--pv-probability-sum-correction", "--pv-value-bits", "--out"},
 }
 
 
@@ -67,6 +75,11 @@ def test_defaults_match_the_reference():
     assert (a.canvas_tokens, a.steps, a.seeds) == (64, 64, [0, 1, 2])
     a = p.parse_args(["trace-mdlm", "--out", "x.json"])
     assert (a.canvas_tokens, a.steps, a.sampler) == (64, 64, "ddpm-cache")
+    a = p.parse_args(["sweep-qkv-weight-precision", "--package-dir", "x"])
+    assert (a.weight_bits, a.smoothquant_alphas) == ([8, 16], [])
+    a = p.parse_args(["screen-packed-int8-attention-logits", "--package-dir", "x"])
+    assert (a.qk_bits, a.qk_scale_mode, a.qk_multiplier_fraction_bits, a.pv_probability_levels, a.pv_value_bits,
+            a.preserve_qk18, a.pv_probability_sum_correction) == (8, "calibrated-head", 24, 127, 8, False, False)
 
 
 def test_validation_argument_errors_precede_device_work():
