@@ -433,7 +433,7 @@ def screen_packed_int8_attention_logits(package_dir: Any, *, seeds: Optional[Seq
     head_w = torch.from_numpy(folded.head.weight)
     head_b = torch.from_numpy(folded.head.bias)
 
-    def candidate_attention(block: int, qkv: Any) -> Any:
+    def candidate_attention(block: int, normalized: Any, qkv: Any) -> Any:
         cand, _, _ = _evaluate_with_fixed_maxima(
             qkv.detach().cpu()[0], cosine, sine, calibrations[block], lut, quantize_qk=quantize_qk,
             quantize_pv=quantize_pv, qk_bits=qk_bits, qk_scale_mode=qk_scale_mode,

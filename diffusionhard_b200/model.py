@@ -277,11 +277,13 @@ def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict
     reference's golden names (hardware_package.py:195-289):
     folded.embedding, folded.block_NN.{norm1_unaffine, qkv, attention,
     attention_projection, after_attention, norm2_unaffine, mlp_up, gelu,
-    mlp_down, output}, folded.final.norm_unaffine.  `attention(block, qkv)`,
-    when given, replaces the float attention of each block: qkv is the fp32
-    [B, L, 3 * hidden] projection and the result the [B, L, hidden]
-    attention output (the error-propagating screens of attention_int8.py:
-    689-936 substitute an integer attention there)."""
+    mlp_down, output}, folded.final.norm_unaffine.  `attention(block,
+    normalized, qkv)`, when given, replaces the float attention of each
+    block: normalized is the unaffine LayerNorm output [B, L, hidden], qkv
+    its fp32 [B, L, 3 * hidden] projection, and the result the [B, L,
+    hidden] attention output (the error-propagating screens of
+    attention_int8.py:689-936 and qkv_int8.py:14-257 substitute an integer
+    attention, or an integer QKV projection and attention, there)."""
     import torch
     import torch.nn.functional as F
 
@@ -316,7 +318,7 @@ def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict
             qkv = F.linear(h, torch.from_numpy(blk["qkv"].weight), torch.from_numpy(blk["qkv"].bias))
             cap(pre + ".qkv", qkv)
             if attention is not None:
-                a = attention(i, qkv).to(torch.float32).reshape(B, L, cfg.hidden)
+                a = attention(i, h, qkv).to(torch.float32).reshape(B, L, cfg.hidden)
             else:
                 qkv = qkv.view(B, L, 3, cfg.heads, cfg.head_dim)
                 q, k, v = qkv.unbind(dim=2)
