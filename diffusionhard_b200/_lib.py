@@ -34,6 +34,17 @@ class DHLibraryError(RuntimeError):
     """The native library is missing or failed to load."""
 
 
+class DHDeviceError(RuntimeError):
+    """A bounded wait inside a kernel gave up (the pipeline barrier it waited
+    on never completed): that kernel abandoned its work, so the outputs of the
+    work enqueued since the last check are undefined.  The CUDA context stays
+    usable."""
+
+    def __init__(self, code: int) -> None:
+        self.code = code
+        super().__init__(f"a bounded device wait expired (device error word {code})")
+
+
 class DHStatusError(RuntimeError):
     """An entry point returned a non-zero status."""
 
@@ -113,6 +124,15 @@ def call(name: str, *args: Any) -> int:
 def raw(name: str, *args: Any) -> int:
     """Call an entry point and return its raw status."""
     return int(getattr(lib(), name)(*args))
+
+
+def check_device_error() -> None:
+    """Read and clear the device error word (synchronous); raise
+    DHDeviceError if a kernel's bounded wait expired since the last check."""
+    word = ctypes.c_uint32(0)
+    call("dh_device_error", ctypes.addressof(word), 1)
+    if word.value:
+        raise DHDeviceError(int(word.value))
 
 
 def ptr(tensor: Any) -> int | None:

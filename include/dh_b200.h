@@ -476,6 +476,15 @@ uint32_t dh_loop_commit(uint32_t sequences, uint32_t positions, uint32_t step, u
  * Synchronous. */
 uint32_t dh_device_error(uint32_t* out, uint32_t clear);
 
+/* Self-check of the bounded waits (failure detection without a GPU fault):
+ * one thread waits on an mbarrier whose single arrival is made only when
+ * `arrive` != 0.  Without it the wait gives up after spin_limit polls
+ * (1 <= spin_limit <= 65536), sets the device error word to 1 (the code of
+ * an expired pipeline wait) and the kernel returns; *completed (device word)
+ * is 1 if the wait completed, else 0.  No counterpart in the reference, whose
+ * HLS kernels report status codes but have no device waits. */
+uint32_t dh_wait_selftest(uint32_t spin_limit, uint32_t arrive, uint32_t* completed, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
