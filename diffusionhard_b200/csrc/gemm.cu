@@ -254,11 +254,14 @@ struct EpiQKV : EpiBase {
 // x[row, col] += acc * (a_scale * w_scale) + bias  (attention out, MLP down).
 // The residual read-modify-write goes through the staging buffer with one
 // 128-byte row segment per warp instruction.
-template <uint32_t kStages_, uint32_t kHalfCols_, bool kPrefetchNext_ = false>
+template <uint32_t kStages_, uint32_t kHalfCols_, bool kPrefetchNext_ = false, uint32_t kAhead_ = 1>
 struct EpiResidualT : EpiBase {
     static constexpr uint32_t kStages = kStages_;
     static constexpr uint32_t kHalfCols = kHalfCols_;  // columns per epilogue warp (half the tile)
     static constexpr bool kPrefetchNext = kPrefetchNext_;
+    // x chunks in flight ahead of the one being summed (1 or 2)
+    static constexpr uint32_t kAhead = kAhead_;
+    static_assert(kAhead == 1 || kAhead == 2, "one or two chunks ahead");
     static constexpr uint32_t kChunk = 32;
     // per warp: dequant staging (4 KB), then its 128 columns' w_scale and bias
     static constexpr uint32_t kStagingPerWarp = 32 * 128 + 2 * 512;
@@ -269,26 +272,34 @@ struct EpiResidualT : EpiBase {
         float* x;
         uint32_t n;
     };
-    // x of the next chunk is loaded one chunk ahead (the first chunk before
-    // the accumulator is ready): lane -> (row i*4 + lane/8, 4 columns).
+    // x is loaded kAhead chunks ahead (the first kAhead chunks before the
+    // accumulator is ready), chunk k into slot k % kAhead: lane -> (row
+    // i*4 + lane/8, 4 columns).
     struct TileState {
-        float4 xv[8];
+        float4 xv[kAhead][8];
         uint32_t col_end;
         float ab;
     };
-    static DH_DEVINL void load_x(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0) {
+    static DH_DEVINL void load_into(const Params& p, float4 (&dst)[8], const EpiCtx& ctx, uint32_t col0) {
         const uint32_t cq = (ctx.lane & 7u) * 4;
 #pragma unroll
         for (uint32_t i = 0; i < 8; ++i) {
             const uint32_t rr = i * 4 + (ctx.lane >> 3);
             if (ctx.row0 + rr < ctx.m_eff)
-                st.xv[i] = *reinterpret_cast<const float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq);
+                dst[i] = *reinterpret_cast<const float4*>(p.x + static_cast<uint64_t>(ctx.row0 + rr) * p.n + col0 + cq);
         }
+    }
+    static DH_DEVINL void load_x(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0, uint32_t slot) {
+        if (kAhead == 2 && slot)
+            load_into(p, st.xv[kAhead - 1], ctx, col0);
+        else
+            load_into(p, st.xv[0], ctx, col0);
     }
     static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
         st.col_end = col_start + kHalfCols;
         st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
-        load_x(p, st, ctx, col_start);
+        load_x(p, st, ctx, col_start, 0);
+        if (kAhead == 2 && kHalfCols > 32) load_x(p, st, ctx, col_start + 32, 1);
         stage_columns(ctx.stage + 4096, ctx.lane, p.w_scale + col_start, p.bias ? p.bias + col_start : nullptr,
                       nullptr, kHalfCols);
         // The residual rows of this warp's next tile start towards L2 now,
@@ -319,15 +330,18 @@ struct EpiResidualT : EpiBase {
         }
         __syncwarp();
         const uint32_t cq = (lane & 7u) * 4;
+        const uint32_t slot = kAhead == 2 ? ((col0 % kHalfCols) / 32u) & 1u : 0u;
         float4 out[8];
 #pragma unroll
         for (uint32_t i = 0; i < 8; ++i) {
             const uint32_t rr = i * 4 + (lane >> 3);
             const float4 y = *reinterpret_cast<const float4*>(ctx.stage + swz128(rr, lane & 7u));
-            out[i] = make_float4(st.xv[i].x + y.x, st.xv[i].y + y.y, st.xv[i].z + y.z, st.xv[i].w + y.w);
+            const float4 xv = slot ? st.xv[kAhead - 1][i] : st.xv[0][i];
+            out[i] = make_float4(xv.x + y.x, xv.y + y.y, xv.z + y.z, xv.w + y.w);
         }
         __syncwarp();
-        if (col0 + 32 < st.col_end) load_x(p, st, ctx, col0 + 32);  // next chunk, in flight during the stores
+        // the chunk kAhead ahead, in flight during the stores
+        if (col0 + 32 * kAhead < st.col_end) load_x(p, st, ctx, col0 + 32 * kAhead, slot);
 #pragma unroll
         for (uint32_t i = 0; i < 8; ++i) {
             const uint32_t rr = i * 4 + (lane >> 3);
@@ -339,7 +353,9 @@ struct EpiResidualT : EpiBase {
 };
 // N = 768 runs as 4 column tiles of 192: 1,024 tiles fill 6.9 waves of 148 SMs
 // (128 x 256 tiles would leave the 6th wave 19% full).
-using EpiResidual = EpiResidualT<3, 96, true>;  // K = 768
+// K = 768: x two chunks ahead (53.4 -> 49.5 us at 32,768 rows); at K = 3072
+// the mainloop is long enough that one chunk ahead is as fast.
+using EpiResidual = EpiResidualT<3, 96, true, 2>;  // K = 768
 using EpiResidualDeep = EpiResidualT<4, 96>;  // K = 3072: deeper TMA pipeline
 using EpiResidual256 = EpiResidualT<3, 128>;  // other N, multiples of 256
 
