@@ -170,3 +170,22 @@ def test_c_abi_argument_checks(cuda):
     assert call(mode=2, qm=None) == 100
     assert call(tokens=2049) == 103
     assert call(tokens=0) == 0
+
+
+@pytest.mark.parametrize("tokens", [64, 2048])
+def test_unquantized_candidate_equals_fixed18_baseline(cuda, tokens):
+    """With neither phase requantised the K15 candidate is the fixed18
+    attention itself, so it must equal K13's output bit for bit -- checked up
+    to the 2,048-token limit, where the oracle would be slow."""
+    torch = cuda
+    from diffusionhard_b200.attention_int8 import _evaluate_with_fixed_maxima, _exponential_table
+    from diffusionhard_b200.model import rope_tables
+
+    g = torch.Generator().manual_seed(tokens + 1)
+    qkv = torch.randn((tokens, 2304), generator=g) * 2.0
+    cos, sin = (torch.from_numpy(t).half().float() for t in rope_tables(tokens, 64))
+    cal = [{"query_q12": 4096, "key_q12": 4096, "value_q12": 4096}] * 12
+    cand, base, heads = _evaluate_with_fixed_maxima(qkv, cos, sin, cal, _exponential_table(), quantize_qk=False,
+                                                    quantize_pv=False)
+    assert torch.equal(cand, base)
+    assert all(h["score_argmax_agreement_vs_fixed18"] == 1.0 for h in heads)
