@@ -61,7 +61,8 @@ def run_ddpm_candidate_cache_sampler(model: MDLMEngine, input_ids: Any, *, mask_
     ids_dev = input_ids.to(model.device, non_blocking=True)
     out, _ = model.generate(ids_dev, steps=steps, seed=seed, sampling_epsilon=sampling_epsilon, graph=graph)
     ids = out.to(torch.int64).to(src_device)
-    _lib.check_device_error()  # the generation's kernels all completed their waits
+    with torch.cuda.device(model.device):
+        _lib.check_device_error()  # the generation's kernels all completed their waits
     return ids, model.measurements(steps, sampling_epsilon), model.metadata(steps)
 
 
@@ -118,7 +119,8 @@ def run_event_driven_candidate_sampler(model: MDLMEngine, input_ids: Any, *, mas
     src_device = input_ids.device
     out = model.generate_event_driven(input_ids.to(model.device), sched, seed=seed, graph=graph)
     ids = out.to(torch.int64).to(src_device)
-    _lib.check_device_error()
+    with torch.cuda.device(model.device):
+        _lib.check_device_error()
     return ids, sched.metadata(model.generation_ms())
 
 

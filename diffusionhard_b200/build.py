@@ -82,10 +82,13 @@ def build(verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
 
 
 def build_oracle(reference_root: str | None = None) -> None:
-    """Build the CPU checkers in oracle/ (test infrastructure)."""
+    """Build the CPU checkers in oracle/ (test infrastructure).  The reference
+    C++ checkers are compiled from the reference tree given as an argument or
+    by $DH_REFERENCE_ROOT, else from its checkout at /root/reference when that
+    exists; without a tree only the plain-C oracle is built."""
     oracle_dir = PKG.parent / "oracle"
     subprocess.run(["make", "-s", "-C", str(oracle_dir)], check=True)
-    ref = Path(reference_root or "/root/reference")
+    ref = Path(reference_root or os.environ.get("DH_REFERENCE_ROOT") or "/root/reference")
     if (ref / "hls").is_dir():
         subprocess.run(["make", "-s", "-C", str(oracle_dir), "ref", f"REF={ref}"], check=True)
 

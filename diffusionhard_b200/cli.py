@@ -15,7 +15,6 @@ device kernels.
   sweep-fixed-layernorm / sweep-fixed-rotary / sweep-fixed-attention   cli.py:240-258
   sweep-qkv-weight-precision      cli.py:260-272, 986-1000
   screen-packed-int8-attention / -heldout / -logits   cli.py:286-342, 1017-1058
-  screen-qkv-int8-logits          cli.py:274-284, 1003-1015
   benchmark-mdlm-event        cli.py:397-409 (benchmark-mdlm-apple, apple_mdlm.py:203-390),
                               also accepted under the reference's name
 
@@ -182,18 +181,6 @@ def build_parser() -> argparse.ArgumentParser:
     qkvp.add_argument("--weight-bits", type=int, nargs="+", choices=[8, 16], default=[8, 16])
     qkvp.add_argument("--smoothquant-alphas", type=float, nargs="+", default=[])
     qkvp.add_argument("--out", type=Path)
-
-    qi = sub.add_parser("screen-qkv-int8-logits",
-                        help="propagate calibrated SmoothQuant INT8 QKV through all blocks (on the GPU)")
-    qi.add_argument("--package-dir", type=Path, required=True)
-    qi.add_argument("--seeds", type=int, nargs="+")
-    qi.add_argument("--device", choices=["auto", "cuda"], default="auto")
-    qi.add_argument("--smoothquant-alpha", type=float, default=0.25)
-    qi.add_argument("--model-id", default=DEFAULT_MODEL_ID)
-    qi.add_argument("--revision", default=DEFAULT_REVISION)
-    qi.add_argument("--checkpoint", type=Path, help="HF-layout model.safetensors (default: the stand-in)")
-    qi.add_argument("--weights-seed", type=int, default=0)
-    qi.add_argument("--out", type=Path)
 
     ia = sub.add_parser("screen-packed-int8-attention",
                         help="screen paired-token INT8 QK and PV on all captured H0 blocks (on the GPU)")
@@ -429,20 +416,14 @@ def main(argv: Optional[List[str]] = None) -> int:
 
         _emit(screen_packed_int8_attention(args.package_dir), args.out)
         return 0
-    if args.command in ("screen-packed-int8-attention-heldout", "screen-packed-int8-attention-logits",
-                        "screen-qkv-int8-logits"):
+    if args.command in ("screen-packed-int8-attention-heldout", "screen-packed-int8-attention-logits"):
         from . import attention_int8
         from .checkpoint import checkpoint_module
         from .model import MDLMConfig, build_standin
 
         cfg = MDLMConfig()
         module = checkpoint_module(args.checkpoint, cfg) if args.checkpoint else build_standin(cfg, args.weights_seed)
-        if args.command == "screen-qkv-int8-logits":
-            from .qkv_int8 import screen_qkv_int8_logits
-
-            report = screen_qkv_int8_logits(args.package_dir, seeds=args.seeds, device=args.device,
-                                            smoothquant_alpha=args.smoothquant_alpha, model=module)
-        elif args.command.endswith("-heldout"):
+        if args.command.endswith("-heldout"):
             report = attention_int8.screen_packed_int8_attention_heldout(args.package_dir, seeds=args.seeds,
                                                                         device=args.device, model=module)
         else:

@@ -470,13 +470,8 @@ extern "C" uint32_t dh_attention(const void* q, const void* k, const void* vt, v
         !make_tmap_2d(&tv, vt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bh * kDh, kv_stride,
                       static_cast<uint64_t>(kv_stride) * 2, 64, 64))
         return DH_ERR_CUDA;
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kSmemBytes) != cudaSuccess)
-            return DH_ERR_CUDA;
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    if (smem_optin_once(attention_kernel, kSmemBytes, configured) != cudaSuccess) return DH_ERR_CUDA;
     AttnArgs a{sequences, q_len, kv_len, kv_stride, static_cast<__nv_bfloat16*>(out), run_flag};
     int sms = kNumSMs, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) {

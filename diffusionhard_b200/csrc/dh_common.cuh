@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/dh_b200.h"
 
 #define DH_DEVINL __device__ __forceinline__
@@ -28,6 +30,23 @@ constexpr int kNumSMs = 148;
 // exceeds it records DH_DEVERR_TIMEOUT in the kernel's status word and gives up
 // instead of hanging the GPU.
 constexpr uint32_t kSpinLimit = 1u << 26;
+
+// Host: opt `kernel` into `bytes` of dynamic shared memory on the current
+// device, once per device.  The attribute is per device, so a process that
+// launches on several GPUs sets it on each; `done` holds one bit per device
+// ordinal (the kernel's own static flag word).  Two threads that race set the
+// same value twice, which is harmless.
+template <class Kernel>
+inline cudaError_t smem_optin_once(Kernel kernel, uint32_t bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
 
 DH_DEVINL uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

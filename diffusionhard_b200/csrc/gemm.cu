@@ -24,7 +24,7 @@ struct EpiStoreI32 : EpiBase {
         uint32_t n;
     };
     struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
+    static DH_DEVINL bool tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) { return true; }
     static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
         if (!ctx.row_ok) return;
@@ -70,9 +70,6 @@ DH_DEVINL void stage_columns(uint8_t* dst, uint32_t lane, const float* a, const 
 }
 
 DH_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Barrier of the two epilogue warps that cover lane quadrant q (ids 1-4).
-DH_DEVINL void pair_sync(uint32_t q) { asm volatile("bar.sync %0, 64;" ::"r"(q + 1u) : "memory"); }
 
 // y = acc * (a_scale[row] * w_scale[col]) + bias[col]   (fp32)
 DH_DEVINL float dequant(uint32_t acc, float ab, float w, float b) {
@@ -135,16 +132,17 @@ struct EpiQKV : EpiBase {
     // cos rows, the other the sin rows -- instead of per-lane row loads in
     // every chunk.  Both halves of a 256-column tile are q, k or v alike, so
     // the pair agrees on the branch and on the named barriers.
-    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
+    static DH_DEVINL bool tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
         st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
         // the warp's 128 columns of w_scale / bias (/ v_scale, indexed from 0 at the v block)
         stage_columns(ctx.stage + 4096, ctx.lane, p.w_scale + col_start, p.bias + col_start,
                       col_start >= 1536u && p.v_scale ? p.v_scale + (col_start - 1536u) : nullptr);
-        if (col_start >= 1536u) return;
+        if (col_start >= 1536u) return true;
         const uint32_t quad = (ctx.row0 / 32u) & 3u;
         const uint32_t half = static_cast<uint32_t>(ctx.stage - ctx.extra - kExtraSmem) / kStagingPerWarp / 4u;
         uint8_t* buf = ctx.extra + quad * 8192u + half * 4096u;
-        pair_sync(quad);  // the pair finished reading the previous tile's rows
+        // the pair finished reading the previous tile's rows
+        if (!tc::mbar_arrive_wait(ctx.pair_bar, tc::kErrTimeoutPair)) return false;
         if (ctx.row0 < ctx.m_eff) {
             const float* table = (half == 0 ? p.rope_cos : p.rope_sin) +
                                  static_cast<uint64_t>(ctx.row0 % p.seq_len + p.pos_offset) * 32;
@@ -155,7 +153,7 @@ struct EpiQKV : EpiBase {
             }
         }
         cp_async_wait_all();
-        pair_sync(quad);  // both tables landed
+        return tc::mbar_arrive_wait(ctx.pair_bar, tc::kErrTimeoutPair);  // both tables landed
     }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
@@ -295,7 +293,7 @@ struct EpiResidualT : EpiBase {
         else
             load_into(p, st.xv[0], ctx, col0);
     }
-    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
+    static DH_DEVINL bool tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
         st.col_end = col_start + kHalfCols;
         st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
         load_x(p, st, ctx, col_start, 0);
@@ -313,6 +311,7 @@ struct EpiResidualT : EpiBase {
             for (uint32_t b = 0; b < kHalfCols * 4; b += 128)
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(r + b));
         }
+        return true;
     }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
@@ -412,7 +411,7 @@ struct EpiGelu : EpiBase {
     }
     // Row scale of this tile (carried from the previous tile's prefetch), and
     // an asynchronous copy of the next tile's row scales into the carry slot.
-    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t) {
+    static DH_DEVINL bool tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t) {
         float* carry = carry_slot(ctx);
         if (ctx.first_tile) {
             st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
@@ -427,6 +426,7 @@ struct EpiGelu : EpiBase {
                              static_cast<uint32_t>(__cvta_generic_to_shared(carry + ctx.lane))),
                          "l"(p.a_scale + ctx.next_row0 + ctx.lane)
                          : "memory");
+        return true;
     }
     static DH_DEVINL void chunk(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
@@ -527,7 +527,7 @@ struct EpiRequantQ : EpiBase {
         long long* stats;  // [min acc, max acc, saturated count, max multiplier]
     };
     struct TileState {};
-    static DH_DEVINL void tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) {}
+    static DH_DEVINL bool tile_begin(const Params&, TileState&, const EpiCtx&, uint32_t) { return true; }
     static DH_DEVINL void chunk(const Params& p, TileState&, const EpiCtx& ctx, uint32_t col0,
                                 const uint32_t* v) {
         long long acc_min = LLONG_MAX, acc_max = LLONG_MIN, sat = 0, mult_max = 0;

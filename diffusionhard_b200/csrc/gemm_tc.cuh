@@ -56,6 +56,11 @@ struct EpiCtx {
     bool has_next;     // this warp has another tile after this one:
     uint32_t next_row0;  // its first row
     uint32_t next_col;   // and first column (the warp's half of that tile)
+    // Bounded rendezvous of the two warps that cover this warp's lane
+    // quadrant in its group (an mbarrier of count 64, for
+    // tc::mbar_arrive_wait).  A policy that needs the pair in step uses it
+    // instead of a named barrier, so a partner that gave up cannot hang it.
+    uint64_t* pair_bar;
 };
 
 struct GemmShape {
@@ -81,6 +86,11 @@ struct GemmCfg {
     // rounded to 1 KB so the epilogue region that follows can hold swizzled
     // TMA store sources
     static constexpr uint32_t BAR_BYTES = ((8 * (2 * STAGES + 5) + 16) + 1023) / 1024 * 1024;
+    // the epilogue pair barriers (2 groups x 4 lane quadrants) sit in the
+    // upper half of the barrier region
+    static constexpr uint32_t PAIR_BAR_OFFSET = 512;
+    static_assert(8 * (2 * STAGES + 5) + 16 <= PAIR_BAR_OFFSET && PAIR_BAR_OFFSET + 64 <= BAR_BYTES,
+                  "barrier region layout");
     static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
     template <class Epi>
     static constexpr uint32_t smem_bytes() {
@@ -106,6 +116,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint64_t* acce_bar = accf_bar + 2;             // [2]
     uint64_t* drain_bar = acce_bar + 2;            // [1]
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+    uint64_t* pair_bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(full_bar) + Cfg::PAIR_BAR_OFFSET);
     uint8_t* extra_smem = smem + Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::BAR_BYTES;
 
     const uint32_t warp = warp_id();
@@ -120,6 +131,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             tc::mbar_init(&acce_bar[b], 8 * 32);  // one group of 8 warps drains a buffer
         }
         tc::mbar_init(drain_bar, 1);
+        for (uint32_t q = 0; q < 8; ++q) tc::mbar_init(&pair_bars[q], 64);
         tc::fence_barrier_init();
         tc::prefetch_tmap(&tmap_a);
         tc::prefetch_tmap(&tmap_b);
@@ -233,11 +245,13 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const EpiCtx ctx{row, row_ok, m0 + quad * 32, m_eff, lane,
                              extra_smem + Epi::kExtraSmem + ew * Epi::kStagingPerWarp,
                              extra_smem, tile == blockIdx.x + group * gridDim.x, next < total,
-                             (next / n_tiles) * Cfg::BM + quad * 32, (next % n_tiles) * BN + half * kHalf};
+                             (next / n_tiles) * Cfg::BM + quad * 32, (next % n_tiles) * BN + half * kHalf,
+                             &pair_bars[group * 4 + quad]};
             typename Epi::TileState st;
             // tile_begin runs before the accumulator is ready: a policy may
             // start loads that do not depend on it (row metadata, residual).
-            Epi::tile_begin(ep, st, ctx, n0 + half * kHalf);
+            // It returns false when one of its own bounded waits gave up.
+            if (!Epi::tile_begin(ep, st, ctx, n0 + half * kHalf)) break;
             if (!tc::mbar_wait(&accf_bar[acc], acc_phase, tc::kErrTimeoutAccFull)) break;
             tc::tc_fence_after();
 #pragma unroll 1
@@ -280,13 +294,9 @@ inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
                                   uint32_t tiles_hint, cudaStream_t stream) {
     using Cfg = GemmCfg<BN, Epi::kStages, Epi::kGroups>;
     auto kernel = gemm_i8_tc_kernel<BN, Epi>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg::template smem_bytes<Epi>());
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    cudaError_t e = smem_optin_once(kernel, Cfg::template smem_bytes<Epi>(), configured);
+    if (e != cudaSuccess) return e;
     int sms = kNumSMs;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) {

@@ -177,7 +177,7 @@ struct EpiHead : EpiBase {
     static DH_DEVINL void init_smem(const Params&, uint8_t* extra) {
         load_gumbel_table(reinterpret_cast<int16_t*>(extra));
     }
-    static DH_DEVINL void tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
+    static DH_DEVINL bool tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
         const uint32_t row = ctx.row;
         if (p.mode == kDequantNoisy) {
             double* bd = reinterpret_cast<double*>(ctx.stage);
@@ -193,12 +193,13 @@ struct EpiHead : EpiBase {
         st.stage = ctx.stage;
         st.best = 0ull;
         st.table = reinterpret_cast<const int16_t*>(ctx.extra);
-        if (!ctx.row_ok) return;
+        if (!ctx.row_ok) return true;
         st.a_scale = p.a_scale ? p.a_scale[row] : 0.f;
         st.pos = p.row_position ? p.row_position[row] : row;
         st.key_hi = p.row_key_hi ? p.row_key_hi[row] : p.const_key_hi;
         st.ev = p.row_eval ? p.row_eval[row] : p.const_eval;
         st.pr = philox_row(st.pos, st.ev, p.stream_id, p.key_lo, st.key_hi);
+        return true;
     }
     // The common chunk: Philox noise, dequant scores, all 32 columns inside
     // the vocabulary and none of them the mask token.  Written for

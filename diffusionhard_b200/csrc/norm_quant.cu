@@ -6,6 +6,10 @@
 //                          symmetric int8 + row scale      (fixed_mlp.py:11-35, 82-90)
 //   K3' quant_rows_bf16    same quantiser for bf16 activations (attention
 //                          output, GELU output)
+// The quantiser divides as the reference does: a = x / s, scale = amax / 127,
+// q = round_half_even(a / scale) clamped to +-127, every quotient the
+// IEEE-rounded fp32 division (__fdiv_rn), so the same fp32 input row gives
+// the same bytes and row scale as fixed_mlp._quantize_symmetric.
 // One warp per row; rows are read once (float4 / 16-byte vector loads) and
 // kept in registers between the statistics and the quantisation pass.
 #include <cuda_bf16.h>
@@ -29,11 +33,16 @@ constexpr uint32_t kWideRowWarps = 1;
 // conversion on the (quarter-rate) XU pipe; the result equals rintf / cvt.rni.
 DH_DEVINL uint32_t rint_bits(float v) { return __float_as_uint(__fadd_rn(v, 12582912.0f)); }
 
-// int8 of clamp(v * inv_scale, +-127), rounded half to even (the clamp after
-// rounding of the reference is the same thing, 127 being an integer).
-DH_DEVINL uint32_t q8_bits(float v, float inv_scale) {
-    return rint_bits(fminf(fmaxf(v * inv_scale, -127.0f), 127.0f));
+// int8 of round_half_even(a / scale) clamped to +-127
+// (fixed_mlp._quantize_symmetric, fixed_mlp.py:24-35: torch.round(x /
+// scale).clamp(-127, 127); clamping the quotient first gives the same byte,
+// 127 being an integer).
+DH_DEVINL uint32_t q8_div_bits(float a, float scale) {
+    return rint_bits(fminf(fmaxf(__fdiv_rn(a, scale), -127.0f), 127.0f));
 }
+
+// Row scale of the reference: amax / 127 (fp32 division), 1 for an all-zero row.
+DH_DEVINL float row_scale(float amax) { return amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f; }
 
 // four int8 (low bytes of a, b, c, d) into one word, a lowest
 DH_DEVINL uint32_t pack4_i8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -59,7 +68,7 @@ embed_gather_kernel(const int32_t* __restrict__ tokens, const float* __restrict_
 // LayerNorm + SmoothQuant + int8.  Optional row gather: output row i reads
 // input row rows_index[i] (used to project only selected rows).
 __global__ void __launch_bounds__(kRowWarps * 32)
-ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ inv_smooth,
+ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ smooth,
                 int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
                 const uint32_t* __restrict__ rows_index, const uint32_t* __restrict__ rows_count,
                 const uint32_t* __restrict__ run_flag) {
@@ -85,36 +94,37 @@ ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ inv_smoot
     }
     const float var = warp_sum_f32(sq) * (1.0f / kD);
     const float rstd = rsqrtf(var + 1e-5f);
-    const float4* is = reinterpret_cast<const float4*>(inv_smooth);
+    const float4* sm = reinterpret_cast<const float4*>(smooth);
     float amax = 0.f;
 #pragma unroll
     for (uint32_t j = 0; j < kD / 128; ++j) {
-        const float4 s = __ldg(is + lane_id() + 32 * j);
-        v[j].x = (v[j].x - mean) * rstd * s.x;
-        v[j].y = (v[j].y - mean) * rstd * s.y;
-        v[j].z = (v[j].z - mean) * rstd * s.z;
-        v[j].w = (v[j].w - mean) * rstd * s.w;
+        const float4 s = __ldg(sm + lane_id() + 32 * j);
+        v[j].x = __fdiv_rn((v[j].x - mean) * rstd, s.x);
+        v[j].y = __fdiv_rn((v[j].y - mean) * rstd, s.y);
+        v[j].z = __fdiv_rn((v[j].z - mean) * rstd, s.z);
+        v[j].w = __fdiv_rn((v[j].w - mean) * rstd, s.w);
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
     }
     amax = warp_max_f32(amax);
-    const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
-    const float inv = 1.0f / sc;
+    const float sc = row_scale(amax);
     uint32_t* dst = reinterpret_cast<uint32_t*>(out + static_cast<uint64_t>(i) * kD);
 #pragma unroll
     for (uint32_t j = 0; j < kD / 128; ++j)
-        dst[lane_id() + 32 * j] = pack4_i8(q8_bits(v[j].x, inv), q8_bits(v[j].y, inv), q8_bits(v[j].z, inv),
-                                           q8_bits(v[j].w, inv));
+        dst[lane_id() + 32 * j] = pack4_i8(q8_div_bits(v[j].x, sc), q8_div_bits(v[j].y, sc),
+                                           q8_div_bits(v[j].z, sc), q8_div_bits(v[j].w, sc));
     if (lane_id() == 0) scale[i] = sc;
 }
 
 // bf16 rows of C = 768 or 3072 columns -> per-token int8 + row scale.  The
 // SmoothQuant division is already applied by the producer (the attention
 // output inherits it from V, the GELU output from the MLP-up epilogue), or
-// here when inv_smooth is given.  The row amax is taken in packed bf16x2
-// (exact), the quantisation in fp32.
-template <uint32_t C>
+// here when `smooth` is given: then a = fp32(x) / s is kept in fp32 registers
+// (never rounded back to bf16) for the amax and the quantisation, as the
+// reference divides fp32 activations.  Without it the row amax is taken in
+// packed bf16x2 (exact) and the quantisation in fp32.
+template <uint32_t C, bool kSmooth>
 __global__ void __launch_bounds__(kRowWarps * 32)
-quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __restrict__ inv_smooth,
+quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __restrict__ smooth,
                        int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
                        const uint32_t* __restrict__ run_flag) {
     if (run_flag && *run_flag == 0u) return;
@@ -125,20 +135,35 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
     uint4 raw[kVec];
 #pragma unroll
     for (uint32_t j = 0; j < kVec; ++j) raw[j] = __ldcs(src + lane_id() + 32 * j);
-    if (inv_smooth) {
-        const float4* is = reinterpret_cast<const float4*>(inv_smooth);
+    uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * C);
+    if (kSmooth) {
+        const float4* sm = reinterpret_cast<const float4*>(smooth);
+        float a[kVec][8];
+        float amax = 0.f;
 #pragma unroll
         for (uint32_t j = 0; j < kVec; ++j) {
             const uint32_t c4 = (lane_id() + 32 * j) * 2;
-            const float4 s0 = __ldg(is + c4), s1 = __ldg(is + c4 + 1);
-            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw[j]);
-            const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            const float4 s0 = __ldg(sm + c4), s1 = __ldg(sm + c4 + 1);
+            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
 #pragma unroll
             for (uint32_t e = 0; e < 4; ++e) {
                 const float2 f = __bfloat1622float2(h[e]);
-                h[e] = __floats2bfloat162_rn(f.x * sc[2 * e], f.y * sc[2 * e + 1]);
+                a[j][2 * e] = __fdiv_rn(f.x, sv[2 * e]);
+                a[j][2 * e + 1] = __fdiv_rn(f.y, sv[2 * e + 1]);
+                amax = fmaxf(amax, fmaxf(fabsf(a[j][2 * e]), fabsf(a[j][2 * e + 1])));
             }
         }
+        const float sc = row_scale(warp_max_f32(amax));
+#pragma unroll
+        for (uint32_t j = 0; j < kVec; ++j)
+            dst[lane_id() + 32 * j] =
+                make_uint2(pack4_i8(q8_div_bits(a[j][0], sc), q8_div_bits(a[j][1], sc), q8_div_bits(a[j][2], sc),
+                                    q8_div_bits(a[j][3], sc)),
+                           pack4_i8(q8_div_bits(a[j][4], sc), q8_div_bits(a[j][5], sc), q8_div_bits(a[j][6], sc),
+                                    q8_div_bits(a[j][7], sc)));
+        if (lane_id() == 0) scale[r] = sc;
+        return;
     }
     __nv_bfloat162 m2 = __float2bfloat162_rn(0.f);
 #pragma unroll
@@ -147,11 +172,7 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
 #pragma unroll
         for (uint32_t e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
     }
-    float amax = fmaxf(__low2float(m2), __high2float(m2));
-    amax = warp_max_f32(amax);
-    const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
-    const float inv = 1.0f / sc;
-    uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * C);
+    const float sc = row_scale(warp_max_f32(fmaxf(__low2float(m2), __high2float(m2))));
 #pragma unroll
     for (uint32_t j = 0; j < kVec; ++j) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
@@ -159,7 +180,8 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
 #pragma unroll
         for (uint32_t e = 0; e < 4; e += 2) {
             const float2 f0 = __bfloat1622float2(h[e]), f1 = __bfloat1622float2(h[e + 1]);
-            packed[e >> 1] = pack4_i8(q8_bits(f0.x, inv), q8_bits(f0.y, inv), q8_bits(f1.x, inv), q8_bits(f1.y, inv));
+            packed[e >> 1] = pack4_i8(q8_div_bits(f0.x, sc), q8_div_bits(f0.y, sc), q8_div_bits(f1.x, sc),
+                                      q8_div_bits(f1.y, sc));
         }
         dst[lane_id() + 32 * j] = make_uint2(packed[0], packed[1]);
     }
@@ -187,9 +209,7 @@ quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __rest
 #pragma unroll
         for (uint32_t e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
     }
-    float amax = warp_max_f32(fmaxf(__low2float(m2), __high2float(m2)));
-    const float sc = amax > 0.f ? amax / 127.0f : 1.0f;
-    const float inv = 1.0f / sc;
+    const float sc = row_scale(warp_max_f32(fmaxf(__low2float(m2), __high2float(m2))));
     uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * cols);
 #pragma unroll 4
     for (uint32_t j = lane_id(); j < nvec; j += 32) {
@@ -199,7 +219,8 @@ quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __rest
 #pragma unroll
         for (uint32_t e = 0; e < 4; e += 2) {
             const float2 f0 = __bfloat1622float2(h[e]), f1 = __bfloat1622float2(h[e + 1]);
-            packed[e >> 1] = pack4_i8(q8_bits(f0.x, inv), q8_bits(f0.y, inv), q8_bits(f1.x, inv), q8_bits(f1.y, inv));
+            packed[e >> 1] = pack4_i8(q8_div_bits(f0.x, sc), q8_div_bits(f0.y, sc), q8_div_bits(f1.x, sc),
+                                      q8_div_bits(f1.y, sc));
         }
         dst[j] = make_uint2(packed[0], packed[1]);
     }
@@ -226,36 +247,40 @@ uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x
     return DH_OK;
 }
 
-uint32_t dh_ln_smooth_quant(const float* x, const float* inv_smooth, int8_t* out, float* scale,
+uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, int8_t* out, float* scale,
                             uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
                             const uint32_t* run_flag, void* stream) {
-    if (!x || !inv_smooth || !out || !scale) return DH_ERR_NULL_POINTER;
+    if (!x || !smooth || !out || !scale) return DH_ERR_NULL_POINTER;
     if (rows == 0) return DH_OK;
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(inv_smooth) |
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(smooth) |
          reinterpret_cast<uintptr_t>(out)) & 15u)
         return DH_ERR_ALIGNMENT;
     ln_quant_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
-                      static_cast<cudaStream_t>(stream)>>>(x, inv_smooth, out, scale, rows,
+                      static_cast<cudaStream_t>(stream)>>>(x, smooth, out, scale, rows,
                                                            rows_index, rows_count, run_flag);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }
 
-uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out, float* scale,
+uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, int8_t* out, float* scale,
                             uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream) {
     if (!in || !out || !scale) return DH_ERR_NULL_POINTER;
     if (rows == 0) return DH_OK;
-    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out) |
+         reinterpret_cast<uintptr_t>(smooth)) & 15u)
         return DH_ERR_ALIGNMENT;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const uint32_t grid = (rows + kRowWarps - 1) / kRowWarps;
     const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in);
-    if (cols == 768)
-        quant_rows_bf16_kernel<768><<<grid, kRowWarps * 32, 0, st>>>(src, inv_smooth, out, scale,
-                                                                     rows, run_flag);
-    else if (cols == 3072 && inv_smooth)
-        quant_rows_bf16_kernel<3072><<<grid, kRowWarps * 32, 0, st>>>(src, inv_smooth, out, scale,
-                                                                      rows, run_flag);
+    if (cols == 768 && smooth)
+        quant_rows_bf16_kernel<768, true><<<grid, kRowWarps * 32, 0, st>>>(src, smooth, out, scale, rows,
+                                                                           run_flag);
+    else if (cols == 768)
+        quant_rows_bf16_kernel<768, false><<<grid, kRowWarps * 32, 0, st>>>(src, nullptr, out, scale, rows,
+                                                                            run_flag);
+    else if (cols == 3072 && smooth)
+        quant_rows_bf16_kernel<3072, true><<<grid, kRowWarps * 32, 0, st>>>(src, smooth, out, scale, rows,
+                                                                            run_flag);
     else if (cols == 3072)
         quant_rows_bf16_wide_kernel<<<(rows + kWideRowWarps - 1) / kWideRowWarps, kWideRowWarps * 32, 0, st>>>(
             src, out, scale, rows, cols, run_flag);

@@ -10,6 +10,8 @@
 //
 // All of these are HBM- or latency-bound integer kernels: coalesced loads,
 // grids sized by rows x vocab chunks, no tensor cores.
+#include <cuda.h>
+
 #include "dh_common.cuh"
 #include "dh_philox.cuh"
 
@@ -384,24 +386,57 @@ static __device__ __align__(256) uint64_t g_noalloc_argmax_scratch[kNoAllocScrat
 
 constexpr int kMaxDevices = 64;
 
+// Unique id of the context current on this thread, 0 when there is none or
+// the driver does not provide the query.  The driver functions are reached
+// through cudaGetDriverEntryPoint, so the library binds no libcuda symbol.
+unsigned long long current_context_id() {
+    typedef CUresult (*GetCurrentFn)(CUcontext*);
+    typedef CUresult (*GetIdFn)(CUcontext, unsigned long long*);
+    static GetCurrentFn get_current = nullptr;
+    static GetIdFn get_id = nullptr;
+    if (!get_current || !get_id) {
+        void* a = nullptr;
+        void* b = nullptr;
+        cudaDriverEntryPointQueryResult qa, qb;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa) != cudaSuccess ||
+            qa != cudaDriverEntryPointSuccess ||
+            cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb) != cudaSuccess ||
+            qb != cudaDriverEntryPointSuccess)
+            return 0;
+        get_current = reinterpret_cast<GetCurrentFn>(a);
+        get_id = reinterpret_cast<GetIdFn>(b);
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+    if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
 // Device address of the scratch array for the current device (set-up on the
-// first call per device; nullptr and *status set on failure).
+// first call per device; nullptr and *status set on failure).  The address
+// is cached with the id of the context it was resolved in: after a device
+// reset the module is loaded again in a new context, and the first call
+// there resolves the address afresh.
 uint64_t* noalloc_scratch(uint32_t* status) {
     static std::mutex mu;
     static uint64_t* addr[kMaxDevices] = {};
+    static unsigned long long ctx_id[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         *status = DH_ERR_CUDA;
         return nullptr;
     }
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    const unsigned long long id = current_context_id();
+    if (!addr[dev] || id == 0 || id != ctx_id[dev]) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_argmax_scratch) != cudaSuccess || !p) {
             *status = DH_ERR_CUDA;
             return nullptr;
         }
         addr[dev] = static_cast<uint64_t*>(p);
+        ctx_id[dev] = current_context_id();  // the lookup made the context current
     }
     return addr[dev];
 }

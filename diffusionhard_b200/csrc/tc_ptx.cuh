@@ -22,6 +22,7 @@ constexpr uint32_t kErrTimeoutFull = 1;
 constexpr uint32_t kErrTimeoutEmpty = 2;
 constexpr uint32_t kErrTimeoutAccFull = 3;
 constexpr uint32_t kErrTimeoutAccEmpty = 4;
+constexpr uint32_t kErrTimeoutPair = 5;  // epilogue warp-pair rendezvous
 
 DH_DEVINL void report_error(uint32_t code) { atomicCAS(&g_device_error, 0u, code); }
 
@@ -61,6 +62,29 @@ DH_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 DH_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
     for (uint32_t i = 0; i < kSpinLimit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
+    report_error(code);
+    return false;
+}
+
+// Bounded rendezvous: arrive on `bar` and wait for the phase this arrival
+// belongs to (identified by the arrival's state token, so the caller keeps no
+// parity).  Every participant of the barrier's count must call it.  Returns
+// false (and records `code`) when the spin limit expires, e.g. because a
+// participant gave up earlier and will never arrive.
+DH_DEVINL bool mbar_arrive_wait(uint64_t* bar, uint32_t code) {
+    uint64_t token;
+    asm volatile("mbarrier.arrive.shared::cta.b64 %0, [%1];" : "=l"(token) : "r"(smem_u32(bar)) : "memory");
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "l"(token)
+            : "memory");
+        if (ok) return true;
+    }
     report_error(code);
     return false;
 }

@@ -15,6 +15,7 @@ cache.
 
 from __future__ import annotations
 
+import functools
 from typing import Any, Dict, List, Optional
 
 import numpy as np
@@ -29,8 +30,23 @@ class _DevLinear:
         self.w = torch.from_numpy(np.ascontiguousarray(ql.weight_q)).to(device)
         self.w_scale = torch.from_numpy(ql.w_scale.astype(np.float32)).to(device)
         self.bias = torch.from_numpy(ql.bias.astype(np.float32)).to(device)
+        self.smooth = torch.from_numpy(ql.smooth.astype(np.float32)).to(device)
         self.inv_smooth = torch.from_numpy(ql.inv_smooth.astype(np.float32)).to(device)
         self.out_features, self.in_features = ql.weight_q.shape
+
+
+def _on_device(method):
+    """Run an engine method with the engine's GPU as the current device.
+    Every launch goes to the current device's current stream and reads the
+    current device's error word, so an engine on cuda:1 must not launch
+    while cuda:0 is current."""
+
+    @functools.wraps(method)
+    def wrapper(self, *args, **kwargs):
+        with self.torch.cuda.device(self.device):
+            return method(self, *args, **kwargs)
+
+    return wrapper
 
 
 class MDLMEngine:
@@ -65,6 +81,10 @@ class MDLMEngine:
         self.pos_offset, self.kv_len, self.kv_offset = pos_offset, kv_len, kv_offset
         self.M = batch * seq_len
         self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("the engine runs on a CUDA device")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         d = self.device
         self.embedding = torch.from_numpy(qm.embedding).to(d)
         self.rope_cos = torch.from_numpy(np.ascontiguousarray(qm.rope_cos)).to(d)
@@ -145,6 +165,7 @@ class MDLMEngine:
     def _p(self, t):
         return _lib.ptr(t)
 
+    @_on_device
     def forward(self, tokens: Any = None, run_rows: Any = None, hook: Any = None) -> None:
         """Forward over self.tokens (or `tokens`, int32 [M] on the device);
         leaves the residual stream in self.x.  run_rows: device word, the
@@ -165,7 +186,7 @@ class MDLMEngine:
         call = _lib.call
         k, vt = self.kv_buffers[i]
         qkv, out, up, down = blk["qkv"], blk["out"], blk["up"], blk["down"]
-        call("dh_ln_smooth_quant", p(self.x), p(qkv.inv_smooth), p(self.act_q), p(self.act_scale), M,
+        call("dh_ln_smooth_quant", p(self.x), p(qkv.smooth), p(self.act_q), p(self.act_scale), M,
              None, None, rr, s)
         call("dh_gemm_qkv_rope", p(self.act_q), p(self.act_scale), p(qkv.w), p(qkv.w_scale), p(qkv.bias),
              p(self.rope_cos), p(self.rope_sin), p(out.inv_smooth), M, L, self.pos_offset, self.kv_stride, self.kv_offset,
@@ -176,7 +197,7 @@ class MDLMEngine:
              768, rr, s)
         call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(out.w), p(out.w_scale), p(out.bias),
              p(self.x), M, 768, 768, rr, s)
-        call("dh_ln_smooth_quant", p(self.x), p(up.inv_smooth), p(self.act_q), p(self.act_scale), M,
+        call("dh_ln_smooth_quant", p(self.x), p(up.smooth), p(self.act_q), p(self.act_scale), M,
              None, None, rr, s)
         call("dh_gemm_gelu", p(self.act_q), p(self.act_scale), p(up.w), p(up.w_scale), p(up.bias),
              p(down.inv_smooth), p(self.mlp), M, 3072, 768, rr, s)
@@ -185,15 +206,17 @@ class MDLMEngine:
         call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(down.w), p(down.w_scale),
              p(down.bias), p(self.x), M, 768, 3072, rr, s)
 
+    @_on_device
     def final_hidden_q(self, rows_index: Any = None, rows_count: Any = None):
         """Final LayerNorm + head SmoothQuant + int8 of (selected) rows."""
         s = _lib.stream_handle()
-        _lib.call("dh_ln_smooth_quant", self._p(self.x), self._p(self.head.inv_smooth),
+        _lib.call("dh_ln_smooth_quant", self._p(self.x), self._p(self.head.smooth),
                   self._p(self.head_q), self._p(self.head_scale), self.M,
                   self._p(rows_index) if rows_index is not None else None,
                   self._p(rows_count) if rows_count is not None else None, None, s)
         return self.head_q, self.head_scale
 
+    @_on_device
     def logits(self) -> Any:
         """fp32 logits [B, L, V] of the last forward: a debug / drift-analysis
         path (the samplers never materialise logits).  int32 accumulators of
@@ -211,6 +234,7 @@ class MDLMEngine:
         out = (acc.double() * combined + h.bias.double()[None, :]).float()
         return out.view(self.B, self.L, V)
 
+    @_on_device
     def selected_logits(self, input_ids: Any, selected: Any) -> Any:
         """fp32 logits [n, V] of the selected positions of a single-sequence
         canvas (apple_mdlm._AppleSelectedLogits, apple_mdlm.py:159-200): the
@@ -236,6 +260,7 @@ class MDLMEngine:
         combined = (hs[:n, None] * h.w_scale[None, :]).double()
         return (acc.double() * combined + h.bias.double()[None, :]).float()
 
+    @_on_device
     def head_argmax(self, rows: int, mode: int, rows_count: Any = None, row_position: Any = None,
                     row_key_hi: Any = None, row_eval: Any = None, key_lo: int = 0,
                     out_ids: Any = None, out_scores: Any = None, const_eval: int = 0) -> None:
@@ -250,6 +275,7 @@ class MDLMEngine:
 
     # ------------------------------------------------------------- loop
 
+    @_on_device
     def enqueue_transition(self, k: int, steps: int, seed: int, threshold_q32: int) -> None:
         """Transition k of `steps` (k == steps: the final greedy pass)."""
         s = _lib.stream_handle()
@@ -283,6 +309,7 @@ class MDLMEngine:
         for k in range(steps + 1):
             self.enqueue_transition(k, steps, seed, thresholds[k] if k < steps else 0)
 
+    @_on_device
     def init_loop(self, input_ids: Any, steps: int) -> None:
         """Load ids [B, L] (device) and reset the loop state."""
         torch = self.torch
@@ -300,6 +327,7 @@ class MDLMEngine:
         per_transition = 1 + self.launches_per_forward + 1 + 1 + 2 + 1
         return 1 + (steps + 1) * per_transition
 
+    @_on_device
     def generate(self, input_ids: Any, *, steps: int, seed: int = 0, sampling_epsilon: float = 1e-5,
                  graph: bool = False) -> tuple[Any, dict]:
         """Candidate-cache generation of B sequences (device input_ids int
@@ -330,6 +358,7 @@ class MDLMEngine:
 
     # ------------------------------------------------- event-driven loop
 
+    @_on_device
     def _load_schedule(self, sched: Any) -> Any:
         """Copy a host EventSchedule into the selected-row buffers: rows,
         canvas positions, Philox key_hi and per-transition counts."""
@@ -375,6 +404,7 @@ class MDLMEngine:
             _lib.call("dh_loop_commit", B, L, min(k, steps - 1), steps, final, p(self.packed), p(rows), p(cnt),
                       p(self.tokens), p(self.active), p(self.need_eval), p(self.counters), s)
 
+    @_on_device
     def generate_event_driven(self, input_ids: Any, sched: Any, *, seed: int = 0,
                               graph: bool = False) -> Any:
         """Event-driven generation (apple_mdlm.py:62-156, batched): only the

@@ -282,8 +282,7 @@ def fp32_forward(folded: FoldedMDLM, ids: np.ndarray, record_amax: Optional[Dict
     block: normalized is the unaffine LayerNorm output [B, L, hidden], qkv
     its fp32 [B, L, 3 * hidden] projection, and the result the [B, L,
     hidden] attention output (the error-propagating screens of
-    attention_int8.py:689-936 and qkv_int8.py:14-257 substitute an integer
-    attention, or an integer QKV projection and attention, there)."""
+    attention_int8.py:689-936 substitute an integer attention there)."""
     import torch
     import torch.nn.functional as F
 

@@ -120,8 +120,9 @@ uint32_t dh_noisy_argmax_f32(const float* logits, uint64_t row_stride, uint32_t 
  * exceed 65,536 (e.g. 5,041 rows of the 50,258-token vocabulary), else
  * DH_ERR_SCRATCH_LIMIT.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress), so make that first call before any
- * stream capture.  Calls share the array: calls that overlap on one GPU race
- * and must be serialised by the caller.  Allocates nothing. */
+ * stream capture; after a device reset the first call in the new context
+ * looks it up again.  Calls share the array: calls that overlap on one GPU
+ * race and must be serialised by the caller.  Allocates nothing. */
 uint32_t dh_noisy_argmax_f32_noalloc(const float* logits, uint64_t row_stride, uint32_t rows,
                                      uint32_t vocabulary_size, uint32_t mask_token_id,
                                      const uint32_t* row_position, const uint32_t* row_key_hi,
@@ -334,18 +335,23 @@ uint32_t dh_packed_int8_attention_q12(const int32_t* query_q12, const int32_t* k
 uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x, uint32_t rows,
                          uint32_t vocabulary_size, const uint32_t* run_flag, void* stream);
 
-/* LayerNorm (no affine, eps 1e-5) -> SmoothQuant -> per-token int8 (K3).
- * The adaLN affine is folded into the following linear
- * (model_specialization.py:10-29).  Optional gather: output row i reads input
- * row rows_index[i] for i < *rows_count. */
-uint32_t dh_ln_smooth_quant(const float* x, const float* inv_smooth, int8_t* out, float* scale,
+/* LayerNorm (no affine, eps 1e-5) -> SmoothQuant division by smooth[768]
+ * -> per-token int8 (K3): a = LN(x) / s, scale = amax(|a|) / 127 (1 for a
+ * zero row), q = round_half_even(a / scale) clamped to +-127, each quotient
+ * an IEEE fp32 division as in fixed_mlp._quantize_symmetric
+ * (fixed_mlp.py:11-35) and quantized_linear (:82-90).  The adaLN affine is
+ * folded into the following linear (model_specialization.py:10-29).
+ * Optional gather: output row i reads input row rows_index[i] for
+ * i < *rows_count. */
+uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, int8_t* out, float* scale,
                             uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
                             const uint32_t* run_flag, void* stream);
 
-/* bf16 rows (cols = 768 or 3072) -> per-token int8 (K3').  inv_smooth may be
- * NULL when the producer already applied the SmoothQuant 1/s (see v_scale /
- * out_scale below). */
-uint32_t dh_quant_rows_bf16(const void* in, const float* inv_smooth, int8_t* out, float* scale,
+/* bf16 rows (cols = 768 or 3072) -> per-token int8 (K3'), the quantiser of
+ * dh_ln_smooth_quant on fp32(in) / smooth.  smooth may be NULL when the
+ * producer already applied the SmoothQuant scale (see v_scale / out_scale
+ * below). */
+uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, int8_t* out, float* scale,
                             uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream);
 
 /* QKV projection (K4): [m, 768] x [2304, 768]^T, dequant, rotate-half rotary

@@ -31,15 +31,26 @@ import numpy as np
 USE_INT_MM = False
 
 
+def quantize_rows(a, smooth=None):
+    """Per-token symmetric int8 of fp32 rows a [R, C], after division by the
+    SmoothQuant scale when given: fixed_mlp._quantize_symmetric(a / s, 8,
+    "token") (fixed_mlp.py:11-35; quantized_linear divides by s first,
+    :82-96).  Returns (int8 [R, C], fp32 row scales [R])."""
+    import torch
+
+    if smooth is not None:
+        a = a / torch.as_tensor(smooth, dtype=torch.float32)[None, :]
+    maximum = a.abs().amax(dim=1)
+    scale = torch.where(maximum > 0, maximum / 127.0, torch.ones_like(maximum))
+    q = torch.round(a / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    return q, scale
+
+
 def w8a8_linear(a, ql, return_parts: bool = False):
     """Reference quantized_linear arithmetic with a static smoothing scale."""
     import torch
 
-    s = torch.from_numpy(ql.smooth)
-    a = a / s[None, :]
-    maximum = a.abs().amax(dim=1)
-    scale = torch.where(maximum > 0, maximum / 127.0, torch.ones_like(maximum))
-    q = torch.round(a / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    q, scale = quantize_rows(a, ql.smooth)
     w_scale = torch.from_numpy(ql.w_scale)
     if USE_INT_MM:
         wq = getattr(ql, "_wq_t", None)
@@ -124,11 +135,7 @@ def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
                 record[f"x{i}"] = x.clone()
         h = F.layer_norm(x, [cfg.hidden])
         if record is not None:
-            hs = h.reshape(B * L, cfg.hidden) / torch.from_numpy(qm.head.smooth)[None, :]
-            maximum = hs.abs().amax(dim=1)
-            scale = torch.where(maximum > 0, maximum / 127.0, torch.ones_like(maximum))
-            record["head_q"] = torch.round(hs / scale[:, None]).clamp(-127, 127).to(torch.int8)
-            record["head_scale"] = scale
+            record["head_q"], record["head_scale"] = quantize_rows(h.reshape(B * L, cfg.hidden), qm.head.smooth)
             if capture_kv:
                 record["kv"] = kv
         return h

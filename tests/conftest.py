@@ -10,7 +10,21 @@ GOLDEN = ROOT / "tests" / "golden"
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
-REFERENCE_ROOT = Path(os.environ.get("DH_REFERENCE_ROOT", "/root/reference"))
+
+def _reference_root() -> Path:
+    """The reference tree for the CPU pins: $DH_REFERENCE_ROOT, else the tree
+    the oracle build compiled (oracle/_ref/REFERENCE_ROOT); a path that does
+    not exist when neither is set, so the pins that need the tree skip."""
+    env = os.environ.get("DH_REFERENCE_ROOT")
+    if env:
+        return Path(env)
+    recorded = ROOT / "oracle" / "_ref" / "REFERENCE_ROOT"
+    if recorded.is_file():
+        return Path(recorded.read_text().strip())
+    return ROOT / "oracle" / "_ref" / "no-reference-tree"
+
+
+REFERENCE_ROOT = _reference_root()
 
 
 def pytest_configure(config):

@@ -1,6 +1,6 @@
 #!/usr/bin/env python3
 """Golden outputs of the reference's packed INT8 attention screens
-(src/diffusion_accel/attention_int8.py, qkv_int8.py and
+(src/diffusion_accel/attention_int8.py and
 fixed_attention.sweep_qkv_weight_precision, imported in place):
 
   * dynamic_qk_fixed_pv_attention_q12 on the seeded qkv canvases of
@@ -14,18 +14,17 @@ fixed_attention.sweep_qkv_weight_precision, imported in place):
     the full-size DDiT stand-in of diffusionhard_b200.model.build_standin
     (seed STANDIN_SEED) in place of the Hugging Face checkpoint, which the
     reference loads from its local cache (its loader is replaced for this
-    run), on the HELDOUT_SEEDS canvases;
-  * qkv_int8.screen_qkv_int8_logits (SmoothQuant alpha 0.25 and 0.5) on that
-    package and stand-in.
+    run), on the HELDOUT_SEEDS canvases.
 Integer outputs are stored as SHA-256 digests of their int64 arrays, metrics
 as JSON.  Writes tests/golden/attention_int8_golden.json.
 
-    python tests/golden/make_attention_int8_golden.py [--reference /root/reference]
+    python tests/golden/make_attention_int8_golden.py --reference <reference root>
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import math
 import sys
@@ -51,7 +50,6 @@ LOGIT_OPTIONS = {
                           "pv_probability_sum_correction": True},
 }
 HELDOUT_SEEDS = [101, 202]
-QKV_ALPHAS = [0.25, 0.5]
 STANDIN_SEED = 5
 
 
@@ -69,7 +67,9 @@ def calibration_of(fa, qkv, cos, sin):
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DH_REFERENCE_ROOT"),
+                    required="DH_REFERENCE_ROOT" not in os.environ,
+                    help="reference tree (default: $DH_REFERENCE_ROOT)")
     args = ap.parse_args()
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(HERE))
@@ -80,7 +80,6 @@ def main() -> None:
     from diffusion_accel import attention_int8 as ai  # reference, in place
     from diffusion_accel import fixed_attention as fa
     from diffusion_accel import mdlm
-    from diffusion_accel import qkv_int8 as qi
     from diffusionhard_b200.model import MDLMConfig, build_standin
 
     _, qkvs, cos, sin, _, _, _ = fixed_point_cases(torch)
@@ -109,8 +108,6 @@ def main() -> None:
         out["heldout"] = ai.screen_packed_int8_attention_heldout(pkg, seeds=HELDOUT_SEEDS, device="cpu")
         out["logits"] = {k: ai.screen_packed_int8_attention_logits(pkg, seeds=HELDOUT_SEEDS, device="cpu", **kw)
                          for k, kw in LOGIT_OPTIONS.items()}
-        out["qkv_int8_logits"] = {str(a): qi.screen_qkv_int8_logits(pkg, seeds=HELDOUT_SEEDS, device="cpu",
-                                                                    smoothquant_alpha=a) for a in QKV_ALPHAS}
     (HERE / "attention_int8_golden.json").write_text(json.dumps(out, sort_keys=True) + "\n")
     print({k: (len(v) if isinstance(v, (dict, list)) else v) for k, v in out.items()})
 

@@ -9,12 +9,13 @@ blocker first.  For seeded packed qkv [S, 3, H, D] (qkv_case below) and each
 boundary list in CASES, it records flash_attn_varlen_qkvpacked_func's output
 under block_isolation.  Writes tests/golden/block_golden.npz.
 
-    python tests/golden/make_block_golden.py [--reference /root/reference]
+    python tests/golden/make_block_golden.py --reference <reference root>
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.abc
 import sys
 from pathlib import Path
@@ -39,7 +40,9 @@ class _Block(importlib.abc.MetaPathFinder):
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DH_REFERENCE_ROOT"),
+                    required="DH_REFERENCE_ROOT" not in os.environ,
+                    help="reference tree (default: $DH_REFERENCE_ROOT)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
     sys.meta_path.insert(0, _Block())

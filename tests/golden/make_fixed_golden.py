@@ -14,12 +14,13 @@ reference's own Python (src/diffusion_accel/fixed_mlp.py, imported in place):
 Inputs are regenerated from the seeds by tests/test_fixed_mlp_*.py (fixed_case
 below); only outputs are stored.  Writes tests/golden/fixed_golden.npz (+ .json).
 
-    python tests/golden/make_fixed_golden.py [--reference /root/reference]
+    python tests/golden/make_fixed_golden.py --reference <reference root>
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import sys
 from pathlib import Path
@@ -43,7 +44,9 @@ def fixed_case(torch):
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DH_REFERENCE_ROOT"),
+                    required="DH_REFERENCE_ROOT" not in os.environ,
+                    help="reference tree (default: $DH_REFERENCE_ROOT)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
     import torch

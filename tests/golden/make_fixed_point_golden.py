@@ -17,12 +17,13 @@ place) on seeded inputs (fixed_point_cases below):
 Integer outputs are stored as SHA-256 digests of their int64 arrays, metrics
 as JSON.  Writes tests/golden/fixed_point_golden.json.
 
-    python tests/golden/make_fixed_point_golden.py [--reference /root/reference]
+    python tests/golden/make_fixed_point_golden.py --reference <reference root>
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 import sys
@@ -104,7 +105,9 @@ def strip(report):
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DH_REFERENCE_ROOT"),
+                    required="DH_REFERENCE_ROOT" not in os.environ,
+                    help="reference tree (default: $DH_REFERENCE_ROOT)")
     args = ap.parse_args()
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(Path(args.reference) / "src"))

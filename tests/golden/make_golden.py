@@ -1,18 +1,19 @@
 #!/usr/bin/env python3
 """Generate the committed golden fixtures from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference) and
+Run in a container that has the reference tree (--reference or DH_REFERENCE_ROOT) and
 ``make -C oracle ref`` built: the fixtures come from the reference's own code --
 its HLS C++ compiled from source (oracle/_ref/libdh_ref.so) and its Python
 package (src/diffusion_accel, imported in place).  The GPU box does not have
 the reference; tests there compare against these files.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference root>
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import sys
 from pathlib import Path
@@ -179,7 +180,9 @@ def make_reveal(lib) -> dict:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("DH_REFERENCE_ROOT"),
+                    required="DH_REFERENCE_ROOT" not in os.environ,
+                    help="reference tree (default: $DH_REFERENCE_ROOT)")
     args = parser.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
     import diffusion_accel.rng  # noqa: F401  (reference package, imported in place)

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Golden fixtures for the model path, produced by the reference's own Python.
 
-Runs, in place from the reference tree (default /root/reference/src):
+Runs, in place from the reference tree (its src/ directory):
   * hardware_package.folded_mdlm_forward on the seeded stand-in DDiT built by
     diffusionhard_b200.model.build_standin (HF attribute names; 2 blocks,
     vocabulary 1000) -> fp32 logits;
@@ -11,12 +11,13 @@ Runs, in place from the reference tree (default /root/reference/src):
   * prefix_drift.tensor_drift_metrics on a seeded pair.
 Writes tests/golden/model_golden.npz (+ .json for the scalar metrics).
 
-    python tests/golden/make_model_golden.py [--reference /root/reference]
+    python tests/golden/make_model_golden.py --reference <reference root>
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import sys
 from pathlib import Path
@@ -32,7 +33,9 @@ SMALL = dict(vocab_size=1000, mask_token_id=999, blocks=2)
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DH_REFERENCE_ROOT"),
+                    required="DH_REFERENCE_ROOT" not in os.environ,
+                    help="reference tree (default: $DH_REFERENCE_ROOT)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))
     import torch

@@ -20,12 +20,13 @@ that diffusionhard_b200.checkpoint.export_hardware_package writes for the
 same stand-in, plus the reference's validate_hardware_fixed_mlp reports on
 the package's two blocks (FIXED_MLP_CASES).  Writes tests/golden/package/ and tests/golden/package_golden.json.
 
-    python tests/golden/make_package_golden.py [--reference /root/reference]
+    python tests/golden/make_package_golden.py --reference <reference root>
 """
 
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import shutil
 import sys
@@ -68,7 +69,9 @@ def package_standin():
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DH_REFERENCE_ROOT"),
+                    required="DH_REFERENCE_ROOT" not in os.environ,
+                    help="reference tree (default: $DH_REFERENCE_ROOT)")
     args = ap.parse_args()
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(Path(args.reference) / "src"))

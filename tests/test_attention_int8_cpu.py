@@ -84,12 +84,6 @@ def test_argument_errors():
         ai.screen_packed_int8_attention_logits("unused", seeds=[])
     with pytest.raises(ValueError, match="at least one attention matrix phase"):
         ai.screen_packed_int8_attention_logits("unused", quantize_qk=False, quantize_pv=False)
-    from diffusionhard_b200.qkv_int8 import screen_qkv_int8_logits
-
-    with pytest.raises(ValueError, match="smoothquant_alpha"):
-        screen_qkv_int8_logits("unused", smoothquant_alpha=1.5)
-    with pytest.raises(ValueError, match="logit-screen seed"):
-        screen_qkv_int8_logits("unused", seeds=[])
     with pytest.raises(ValueError, match="weight_bits"):
         sweep_qkv_weight_precision("unused", weight_bits=(4,))
     with pytest.raises(ValueError, match="smoothquant_alphas"):

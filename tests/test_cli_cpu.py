@@ -51,7 +51,6 @@ REFERENCE_FLAGS = {
     # cli.py:260-272, 286-342
     "sweep-qkv-weight-precision": {"--package-dir", "--weight-bits", "--smoothquant-alphas", "--out"},
     "screen-packed-int8-attention": {"--package-dir", "--out"},
-    "screen-qkv-int8-logits": {"--package-dir", "--seeds", "--device", "--smoothquant-alpha", "--out"},
     "screen-packed-int8-attention-heldout": {"--package-dir", "--device", "--seeds", "--out"},
     "screen-packed-int8-attention-logits": {"--package-dir", "--device", "--seeds", "--preserve-qk18",
                                             "--preserve-pv18", "--qk-bits", "--qk-scale-mode",

@@ -1,0 +1,79 @@
+"""The per-token int8 quantiser of the W8A8 linears (K3 / K3') against the
+reference's fixed_mlp._quantize_symmetric (fixed_mlp.py:11-35), whose
+outputs on seeded rows are the golden fixture tests/golden/quant_golden.npz
+(made by tests/golden/make_quant_golden.py).
+
+Bars: dh_quant_rows_bf16 is bit-exact -- the same int8 bytes and the same
+fp32 row scales -- because it divides exactly as the reference does.
+dh_ln_smooth_quant adds the LayerNorm, whose fp32 mean and variance the GPU
+sums in another order than the CPU: its int8 bytes may differ by one step
+where the normalised value lies within rounding of a half-integer quotient
+(at most 0.2% of the bytes here), and its row scales by a few ulps.
+"""
+
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, load_npz_cases
+from diffusionhard_b200 import _lib
+from oracle import model_oracle
+
+sys.path.insert(0, str(GOLDEN))
+from make_quant_golden import quant_cases  # noqa: E402
+
+
+def _cases():
+    import torch
+
+    gold = load_npz_cases("quant_golden.npz")
+    return {name: (x, s, ln, gold[name]) for name, (x, s, ln) in quant_cases(torch).items()}
+
+
+def test_oracle_quantiser_matches_reference_golden():
+    import torch
+    import torch.nn.functional as F
+
+    for name, (x, s, ln, g) in _cases().items():
+        a = F.layer_norm(x, [x.shape[1]]) if ln else x
+        q, scale = model_oracle.quantize_rows(a, None if s is None else s.numpy())
+        assert np.array_equal(q.numpy(), g["q"]), name
+        assert np.array_equal(scale.numpy(), g["scale"]), name
+    del torch
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["bf16_768", "bf16_768_smooth", "bf16_3072", "bf16_3072_smooth", "edge_768"])
+def test_quant_rows_bit_exact(cuda, name):
+    torch = cuda
+    x, s, _, g = _cases()[name]
+    rows, cols = x.shape
+    xin = x.to(torch.bfloat16).cuda()
+    sd = None if s is None else s.cuda()
+    q = torch.empty((rows, cols), dtype=torch.int8, device="cuda")
+    sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+    _lib.call("dh_quant_rows_bf16", _lib.ptr(xin), _lib.ptr(sd), _lib.ptr(q), _lib.ptr(sc), rows, cols, None, None)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), g["q"]), name
+    assert np.array_equal(sc.cpu().numpy(), g["scale"]), name
+    oq, osc = model_oracle.quantize_rows(x, None if s is None else s.numpy())
+    assert np.array_equal(q.cpu().numpy(), oq.numpy()) and np.array_equal(sc.cpu().numpy(), osc.numpy())
+
+
+@pytest.mark.gpu
+def test_ln_smooth_quant_matches_reference(cuda):
+    torch = cuda
+    x, s, _, g = _cases()["ln_768"]
+    rows = x.shape[0]
+    xd, sd = x.cuda(), s.cuda()
+    q = torch.empty((rows, 768), dtype=torch.int8, device="cuda")
+    sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+    _lib.call("dh_ln_smooth_quant", _lib.ptr(xd), _lib.ptr(sd), _lib.ptr(q), _lib.ptr(sc), rows, None, None, None,
+              None)
+    torch.cuda.synchronize()
+    gq = q.cpu().numpy().astype(np.int32)
+    diff = np.abs(gq - g["q"].astype(np.int32))
+    assert diff.max() <= 1
+    assert (diff == 0).mean() >= 0.998
+    assert np.allclose(sc.cpu().numpy(), g["scale"], rtol=4e-6, atol=0)

@@ -5,15 +5,17 @@ framework that owns every device allocation, or a serving path that must not
 call cudaMalloc (which can synchronise the whole device) once it is running.
 For them the Gumbel-max kernel keeps its scratch in an array inside the
 library.  This test calls it through the C ABI and checks it against the
-workspace entry point dh_noisy_argmax_f32, bit for bit (argmax ids and scores
-are exact), on two calls in a row: the second call runs on the scratch the
-first one left behind.
+workspace entry point dh_noisy_argmax_f32 and against the CPU oracle, bit for
+bit (argmax ids and scores are exact), on two calls in a row: the second call
+runs on the scratch the first one left behind.  It also runs the largest row
+count the scratch accepts.
 """
 
 import numpy as np
 import pytest
 
 from diffusionhard_b200 import _lib
+from oracle import pyoracle
 
 pytestmark = pytest.mark.gpu
 
@@ -48,6 +50,32 @@ def test_noalloc_matches_workspace_entry_on_two_calls(cuda):
         assert np.array_equal(got[0], ref[0]), call
         assert np.array_equal(got[1], ref[1]), call
         assert (got[0] >= 0).all() and not (got[0] == mask).any()
+        oids, oscores = pyoracle.noisy_argmax_f32(logits.cpu().numpy(), mask, row_position=pos.cpu().numpy(),
+                                                  row_key_hi=key.cpu().numpy(), row_eval=ev.cpu().numpy(),
+                                                  key_lo=17)
+        assert np.array_equal(got[0], oids), call
+        assert np.array_equal(got[1], oscores), call
+
+
+def test_noalloc_accepts_the_largest_row_count(cuda):
+    # 5,041 rows x 13 chunks of the 50,258-token vocabulary = 65,533 of the
+    # 65,536 scratch slots; the oracle checks a sample of the rows
+    torch = cuda
+    rows, vocab = 5041, 50258
+    g = torch.Generator(device="cuda").manual_seed(3)
+    logits = 3 * torch.randn((rows, vocab), device="cuda", generator=g)
+    pos = torch.arange(rows, dtype=torch.int32, device="cuda") % 1024
+    key = torch.arange(rows, dtype=torch.int32, device="cuda") // 1024
+    ev = torch.full((rows,), 5, dtype=torch.int32, device="cuda")
+    got = _call(torch, True, logits, rows, vocab, vocab - 1, pos, key, ev, 4)
+    ref = _call(torch, False, logits, rows, vocab, vocab - 1, pos, key, ev, 4)
+    assert np.array_equal(got[0], ref[0]) and np.array_equal(got[1], ref[1])
+    sample = np.r_[0:16, rows - 16:rows]
+    oids, oscores = pyoracle.noisy_argmax_f32(logits[sample].cpu().numpy(), vocab - 1,
+                                              row_position=pos[sample].cpu().numpy(),
+                                              row_key_hi=key[sample].cpu().numpy(),
+                                              row_eval=ev[sample].cpu().numpy(), key_lo=4)
+    assert np.array_equal(got[0][sample], oids) and np.array_equal(got[1][sample], oscores)
 
 
 def test_noalloc_rejects_rows_beyond_the_scratch(cuda):
