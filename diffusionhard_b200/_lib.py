@@ -27,7 +27,26 @@ STATUS_NAMES = {
     104: "DH_ERR_CUDA",
     105: "DH_ERR_INVALID_ARGUMENT",
     106: "DH_ERR_SCRATCH_LIMIT",
+    107: "DH_ERR_NCCL",
 }
+
+
+class LinearWeights(ctypes.Structure):
+    """dh_linear_weights of include/dh_b200.h (device pointers)."""
+
+    _fields_ = [("weight", ctypes.c_void_p), ("w_scale", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+                ("smooth", ctypes.c_void_p), ("inv_smooth", ctypes.c_void_p)]
+
+
+class MDLMWeights(ctypes.Structure):
+    """dh_mdlm_weights of include/dh_b200.h; block_linears points to a host
+    array of 4 LinearWeights per block (qkv, out, up, down)."""
+
+    _fields_ = [("blocks", ctypes.c_uint32), ("vocabulary_size", ctypes.c_uint32),
+                ("mask_token_id", ctypes.c_uint32), ("max_positions", ctypes.c_uint32),
+                ("embedding", ctypes.c_void_p), ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
+                ("block_linears", ctypes.POINTER(LinearWeights)), ("head", LinearWeights),
+                ("head_rows", ctypes.c_uint32), ("head_vocab_offset", ctypes.c_uint32)]
 
 
 class DHLibraryError(RuntimeError):

@@ -70,3 +70,28 @@ def decode_packed(packed: Any) -> Tuple[Any, Any]:
     high = (packed >> 32) & 0xFFFFFFFF  # score + 2^31 (sign bit flipped)
     scores = high - (1 << 31)
     return ids, scores
+
+
+def nccl_comm_handle(group: Any, device: Any) -> Any:
+    """The ncclComm_t (as an int) behind a process group's NCCL backend on
+    `device`, for dh_vocab_shard_reduce; None when the group has no NCCL
+    backend (gloo, or a torch without the accessor).  A communicator that
+    torch creates lazily is created by one collective, which every rank of
+    the group takes at the same point."""
+    import torch
+    import torch.distributed as dist
+
+    try:
+        backend = group._get_backend(torch.device(device))
+    except Exception:
+        return None
+    get = getattr(backend, "_comm_ptr", None)
+    if get is None:
+        return None
+    ptr = int(get())
+    if ptr == 0:
+        t = torch.zeros(1, device=device)
+        dist.all_reduce(t, group=group)
+        torch.cuda.synchronize(device)
+        ptr = int(get())
+    return ptr or None

@@ -1,9 +1,13 @@
 """MDLM engine: device-resident W8A8 DDiT + fused head + candidate-cache loop.
 
-Host orchestration over the C ABI (include/dh_b200.h).  Per forward and
-block: LN+SmoothQuant+int8 -> QKV GEMM (+rotary) -> attention -> requant ->
+Host side of the C ABI (include/dh_b200.h).  Per forward and block:
+LN+SmoothQuant+int8 -> QKV GEMM (+rotary) -> attention -> requant ->
 attention-out GEMM (+residual) -> LN+quant -> MLP-up GEMM (+GELU) -> requant ->
-MLP-down GEMM (+residual).  Every launch of a transition is enqueued on one
+MLP-down GEMM (+residual).  `generate` hands the whole generation to the
+library's composite entry point dh_sample_loop (one C call enqueues every
+launch); the per-kernel orchestration here serves the loop variants the
+composite does not cover (prefix K/V offsets, Python hooks, a non-NCCL head
+reduction) and the per-transition tests.  Every launch is enqueued on one
 stream with no host synchronisation; a whole generation can be captured in
 one CUDA graph (`generate(..., graph=True)`).
 
@@ -15,6 +19,7 @@ cache.
 
 from __future__ import annotations
 
+import ctypes
 import functools
 from typing import Any, Dict, List, Optional
 
@@ -116,6 +121,7 @@ class MDLMEngine:
         W = (seq_len + 63) // 64
         u32 = torch.int32
         self.tokens = torch.empty(M, dtype=torch.int32, device=d)
+        self.ids_in = torch.empty(M, dtype=torch.int32, device=d)  # input canvas of the composite loop
         self.active = torch.empty(batch * W, dtype=torch.int64, device=d)
         self.need_eval = torch.empty(batch, dtype=u32, device=d)
         self.eval_id = torch.empty(batch, dtype=u32, device=d)
@@ -126,6 +132,9 @@ class MDLMEngine:
         self.sel_key = torch.empty(M, dtype=u32, device=d)
         self.sel_eval = torch.empty(M, dtype=u32, device=d)
         self.counters: Optional[Any] = None
+        self._counters: Dict[int, Any] = {}  # per step count: captured graphs keep their buffer
+        self._native: Optional[tuple] = None   # (dh_mdlm_weights, its block array)
+        self._loop_ws: Optional[Any] = None    # workspace of dh_sample_loop
         self.seq_offset = 0  # global index of local sequence 0 (Philox key_hi)
         self.head_vocab_offset = 0  # global id of the first head row held here (vocab-sharded head)
         self.head_group = None      # process group reducing the sharded head, or None
@@ -147,6 +156,7 @@ class MDLMEngine:
         h.bias = h.bias[v0:v1].contiguous()
         h.out_features = v1 - v0
         self.head_vocab_offset = v0
+        self._native = None
         self.head_group = group
         self.head_reduce = reduce
 
@@ -309,12 +319,22 @@ class MDLMEngine:
         for k in range(steps + 1):
             self.enqueue_transition(k, steps, seed, thresholds[k] if k < steps else 0)
 
+    def _use_counters(self, steps: int) -> Any:
+        """The per-transition counters of a `steps`-transition generation.
+        One buffer per step count, kept for the engine's life: a captured
+        graph holds the address it was captured with."""
+        c = self._counters.get(steps)
+        if c is None:
+            c = self.torch.zeros(3 * steps, dtype=self.torch.int32, device=self.device)
+            self._counters[steps] = c
+        self.counters = c
+        return c
+
     @_on_device
     def init_loop(self, input_ids: Any, steps: int) -> None:
         """Load ids [B, L] (device) and reset the loop state."""
         torch = self.torch
-        if self.counters is None or self.counters.numel() != 3 * steps:
-            self.counters = torch.zeros(3 * steps, dtype=torch.int32, device=self.device)
+        self._use_counters(steps)
         ids = input_ids.to(device=self.device, dtype=torch.int32).contiguous().view(-1)
         if ids.numel() != self.M:
             raise ValueError("input_ids must be [batch, seq_len]")
@@ -323,36 +343,102 @@ class MDLMEngine:
                   _lib.ptr(self.tokens), _lib.ptr(self.active), _lib.ptr(self.need_eval),
                   _lib.ptr(self.eval_id), _lib.ptr(self.counters), _lib.stream_handle())
 
+    # ------------------------------------------- composite (C-ABI) loop
+
+    def native_weights(self) -> Any:
+        """dh_mdlm_weights over this engine's device tensors (built once; the
+        engine keeps the structs and the tensors alive)."""
+        if self._native is None:
+            p = _lib.ptr
+
+            def lin(d: _DevLinear) -> Any:
+                return _lib.LinearWeights(p(d.w), p(d.w_scale), p(d.bias), p(d.smooth), p(d.inv_smooth))
+
+            names = ("qkv", "out", "up", "down")
+            arr = (_lib.LinearWeights * (4 * len(self.blocks)))(*[lin(b[n]) for b in self.blocks for n in names])
+            w = _lib.MDLMWeights(len(self.blocks), self.cfg.vocab_size, self.cfg.mask_token_id,
+                                 int(self.rope_cos.shape[0]), p(self.embedding), p(self.rope_cos), p(self.rope_sin),
+                                 ctypes.cast(arr, ctypes.POINTER(_lib.LinearWeights)), lin(self.head),
+                                 self.head.out_features, self.head_vocab_offset)
+            self._native = (w, arr)
+        return self._native[0]
+
+    def _nccl_comm(self) -> Any:
+        if self.head_group is None:
+            return None
+        from .distributed import nccl_comm_handle
+
+        return nccl_comm_handle(self.head_group, self.device)
+
+    def native_loop_ok(self) -> bool:
+        """Whether dh_sample_loop covers this engine's configuration: whole
+        canvases (no prefix K/V offsets), no Python hooks, and a head that is
+        whole or merged over NCCL."""
+        if self.pre_forward is not None or self.head_reduce is not None:
+            return False
+        if self.pos_offset or self.kv_offset or self.kv_len != self.L or self.kv_stride != self.L:
+            return False
+        return self.head_group is None or self._nccl_comm() is not None
+
+    def _enqueue_native(self, steps: int, seed: int, thresholds: List[int]) -> None:
+        torch = self.torch
+        if self._loop_ws is None:
+            size = _lib.lib().dh_sample_loop_workspace_size(self.B, self.L)
+            self._loop_ws = torch.empty(size, dtype=torch.uint8, device=self.device)
+        thr = (ctypes.c_uint64 * steps)(*thresholds[:steps])
+        w = self.native_weights()
+        _lib.call("dh_sample_loop", ctypes.addressof(w), _lib.ptr(self.ids_in), _lib.ptr(self.tokens), self.B,
+                  self.L, steps, ctypes.addressof(thr), seed, self.seq_offset, _lib.ptr(self.counters),
+                  self._nccl_comm(), _lib.ptr(self._loop_ws), self._loop_ws.numel(), _lib.stream_handle())
+
     def launches_per_generation(self, steps: int) -> int:
         per_transition = 1 + self.launches_per_forward + 1 + 1 + 2 + 1
         return 1 + (steps + 1) * per_transition
 
     @_on_device
     def generate(self, input_ids: Any, *, steps: int, seed: int = 0, sampling_epsilon: float = 1e-5,
-                 graph: bool = False) -> tuple[Any, dict]:
-        """Candidate-cache generation of B sequences (device input_ids int
-        [B, L]).  Returns (device int32 ids [B, L], metadata)."""
+                 graph: bool = False, native: Optional[bool] = None) -> tuple[Any, dict]:
+        """Candidate-cache generation of B sequences (input_ids int [B, L],
+        any device).  native: run the loop through the composite entry point
+        dh_sample_loop (default when native_loop_ok()), else through the
+        per-kernel entry points from Python.  Both launch the same kernels
+        with the same arguments.  Returns (device int32 ids [B, L],
+        metadata)."""
         torch = self.torch
         thresholds = reveal_thresholds_q32(steps, sampling_epsilon)
-        self.init_loop(input_ids, steps)
+        native = self.native_loop_ok() if native is None else native
+        if native:
+            if input_ids.numel() != self.M:
+                raise ValueError("input_ids must be [batch, seq_len]")
+            self.ids_in.copy_(input_ids.reshape(-1))
+            self._use_counters(steps)
+
+            def enqueue() -> None:
+                self._enqueue_native(steps, seed, thresholds)
+        else:
+            self.init_loop(input_ids, steps)
+
+            def enqueue() -> None:
+                self._enqueue_generation(steps, seed, thresholds)
         if graph:
-            key = (steps, seed, sampling_epsilon, self.seq_offset)
+            key = (native, steps, seed, sampling_epsilon, self.seq_offset)
             g = self._graphs.get(key)
             if g is None:
                 # warm-up outside capture (function attributes, tensor maps)
-                self._enqueue_generation(steps, seed, thresholds)
-                self.init_loop(input_ids, steps)
+                enqueue()
+                if not native:
+                    self.init_loop(input_ids, steps)
                 torch.cuda.synchronize()
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
-                    self._enqueue_generation(steps, seed, thresholds)
+                    enqueue()
                 self._graphs[key] = g
             self._events[0].record()
             g.replay()
             self._events[1].record()
         else:
             self._events[0].record()
-            self._enqueue_generation(steps, seed, thresholds)
+            enqueue()
             self._events[1].record()
         return self.tokens.view(self.B, self.L), {}
 

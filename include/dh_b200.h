@@ -45,6 +45,7 @@ extern "C" {
 #define DH_ERR_CUDA 104u
 #define DH_ERR_INVALID_ARGUMENT 105u
 #define DH_ERR_SCRATCH_LIMIT 106u
+#define DH_ERR_NCCL 107u
 
 /* RNG family -- same values as RngKernelStatus (philox_rng.hpp:29-33). */
 #define DH_RNG_INVALID_POSITION_COUNT 1u
@@ -473,6 +474,84 @@ uint32_t dh_loop_commit(uint32_t sequences, uint32_t positions, uint32_t step, u
                         uint32_t final_pass, const uint64_t* packed, const uint32_t* sel_rows,
                         const uint32_t* sel_count, int32_t* tokens, uint64_t* active,
                         uint32_t* need_eval, int32_t* counters, void* stream);
+
+/* ------------------------------------------ composite entry points (C ABI) */
+/*
+ * The whole forward and the whole generation enqueued by the library on one
+ * stream, for hosts that do not orchestrate the per-kernel entry points
+ * above themselves.  Weights are device pointers gathered in the structs
+ * below (the host array `block_linears` holds 4 linears per block: qkv, out,
+ * up, down).  Workspaces are caller-owned device buffers, 256-byte aligned,
+ * of the size the matching *_workspace_size query returns; nothing is
+ * allocated.  Arguments are checked before anything is enqueued.
+ */
+typedef struct dh_linear_weights {
+    const int8_t* weight;     /* [out_features, in_features] int8, per-output-channel quantised */
+    const float* w_scale;     /* [out_features] */
+    const float* bias;        /* [out_features] fp32; required for qkv and up, may be NULL for out and down */
+    const float* smooth;      /* [in_features] SmoothQuant divisor s of this linear's input */
+    const float* inv_smooth;  /* [in_features] 1 / s (folded into the producer of out's / down's input) */
+} dh_linear_weights;
+
+typedef struct dh_mdlm_weights {
+    uint32_t blocks;                          /* DDiT blocks (d = 768, 12 x 64 heads, MLP 3072) */
+    uint32_t vocabulary_size;                 /* embedding rows = global vocabulary, mask id included */
+    uint32_t mask_token_id;
+    uint32_t max_positions;                   /* rows of rope_cos / rope_sin */
+    const float* embedding;                   /* [vocabulary_size, 768] fp32 */
+    const float* rope_cos;                    /* [max_positions, 32] fp32 */
+    const float* rope_sin;
+    const dh_linear_weights* block_linears;   /* HOST array [blocks * 4] */
+    dh_linear_weights head;                   /* head rows [head_vocab_offset, + head_rows) of [V, 768] */
+    uint32_t head_rows;                       /* the whole vocabulary, or this rank's shard */
+    uint32_t head_vocab_offset;               /* global id of head row 0, a multiple of 4 */
+} dh_mdlm_weights;
+
+/* The folded W8A8 DDiT forward (hardware_package.folded_mdlm_forward,
+ * hardware_package.py:195-289; per block the kernels dh_ln_smooth_quant,
+ * dh_gemm_qkv_rope, dh_attention, dh_quant_rows_bf16, dh_gemm_residual,
+ * dh_ln_smooth_quant, dh_gemm_gelu, dh_quant_rows_bf16, dh_gemm_residual)
+ * of `sequences` x `positions` token ids (device int32, positions a multiple
+ * of 32, full bidirectional attention, rotary positions 0..positions-1).
+ * x (device fp32 [sequences * positions, 768]) receives the residual stream
+ * after the last block, before the final LayerNorm.  run_rows (device word,
+ * may be NULL): the forward does nothing when it holds 0. */
+size_t dh_ddit_forward_workspace_size(uint32_t sequences, uint32_t positions);
+uint32_t dh_ddit_forward(const dh_mdlm_weights* weights, const int32_t* tokens, uint32_t sequences,
+                         uint32_t positions, float* x, void* workspace, size_t workspace_bytes,
+                         const uint32_t* run_rows, void* stream);
+
+/* The candidate-cache generation of mdlm._run_ddpm_candidate_cache_sampler
+ * (mdlm.py:1104-1218) over the model: input_ids (device int32 [sequences *
+ * positions], masked positions = mask_token_id) -> tokens (device int32, same
+ * shape; the loop's canvas), `steps` transitions and the final greedy pass,
+ * with the reveal threshold of transition k thresholds_q32[k] (HOST array,
+ * min(2^32, floor(p_k 2^32)) for the schedule's reveal probability p_k,
+ * mdlm.py:1116-1117, 1151-1153) and the noise / reveal words keyed by
+ * (seed, seq_offset + b) as in dh_loop_select and dh_head_argmax_i8.
+ * counters (device int32 [3 * steps]): per transition the active count, the
+ * changed count and 1 if the model ran (the reference's metadata).
+ * nccl_comm: NULL, or the ncclComm_t of the ranks that hold the vocabulary
+ * shards of the head (weights->head_rows / head_vocab_offset); after every
+ * head launch the packed per-row results are merged by
+ * dh_vocab_shard_reduce over it, so every rank commits the unsharded argmax.
+ * The whole generation is enqueued without host synchronisation (it can be
+ * captured in a CUDA graph).  Status: DH_CAND_INVALID_THRESHOLD for a
+ * threshold above 2^32, else DH_ERR_*. */
+size_t dh_sample_loop_workspace_size(uint32_t sequences, uint32_t positions);
+uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids, int32_t* tokens,
+                        uint32_t sequences, uint32_t positions, uint32_t steps, const uint64_t* thresholds_q32,
+                        uint32_t seed, uint32_t seq_offset, int32_t* counters, void* nccl_comm,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge of the vocab-sharded head: packed (device uint64 [count], as written
+ * by dh_head_argmax_i8: (score ^ 2^31) << 32 | ~id) is MAX-all-reduced in
+ * place over nccl_comm (an ncclComm_t; the NCCL library that created it must
+ * be loaded in the process, its ncclAllReduce is used) on `stream`.  The
+ * unsigned order of the packed words is the order of (score, lower id), the
+ * tie rule of ordered_noisy_argmax_reducer.sv:106-133.  DH_ERR_NCCL when
+ * NCCL is not loaded or the call fails. */
+uint32_t dh_vocab_shard_reduce(void* nccl_comm, uint64_t* packed, uint64_t count, void* stream);
 
 /* ------------------------------------------------------------- diagnostics */
 

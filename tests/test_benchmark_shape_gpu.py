@@ -67,7 +67,7 @@ def _ids(B, L, vocab, seed, masked=0.5):
     return ids
 
 
-def _forward_vs_oracle(torch, qm, B, L, seed):
+def _forward_vs_oracle(torch, qm, B, L, seed, min_agree):
     eng = MDLMEngine(qm, B, L)
     ids = _ids(B, L, qm.config.vocab_size, seed)
     eng.tokens.copy_(ids.view(-1).to(torch.int32))
@@ -87,21 +87,23 @@ def _forward_vs_oracle(torch, qm, B, L, seed):
     print(f"\n{qm.config.blocks} blocks, {B} x {L}: residual rel. error per block "
           f"{', '.join('%.1e' % e for e in errs)}; int8 head inputs identical {agree:.4f}")
     assert max(errs) < 1e-2
-    assert agree > 0.95
+    assert agree > min_agree
     assert np.abs(gq.astype(np.int32) - oq.astype(np.int32)).max() <= 1
     assert np.allclose(hs.cpu().numpy(), rec["head_scale"].numpy(), rtol=1e-2)
     return eng, ids, h, rec
 
 
 def test_two_block_forward_at_16x1024(cuda):
-    _forward_vs_oracle(cuda, build_quantized(TWO_BLOCKS, seed=0), 16, 1024, seed=21)
+    _forward_vs_oracle(cuda, build_quantized(TWO_BLOCKS, seed=0), 16, 1024, seed=21, min_agree=0.95)
 
 
 def test_full_forward_and_head_at_4x1024(cuda, full_model):
     torch = cuda
     qm = full_model
     B, L = 4, 1024
-    eng, ids, h, rec = _forward_vs_oracle(torch, qm, B, L, seed=22)
+    # 12 blocks of tolerance-level differences: fewer identical int8 head
+    # inputs than after 2 blocks, each still within one step
+    eng, ids, h, rec = _forward_vs_oracle(torch, qm, B, L, seed=22, min_agree=0.9)
     M, V, mask = B * L, FULL.vocab_size, FULL.mask_token_id
     pos = torch.arange(M, dtype=torch.int32, device="cuda") % L
     key = torch.arange(M, dtype=torch.int32, device="cuda") // L
@@ -144,4 +146,4 @@ def test_free_running_generation_matches_oracle(cuda, full_model):
           f"({int((got != ref['tokens']).sum())} of {B * L} differ); GPU changed per step "
           f"{meta['transition_changed_tokens'][:4]}..., oracle {ref['changed'][:4]}...")
     assert meta["transition_changed_tokens"][0] == ref["changed"][0]
-    assert agree >= 0.99
+    assert agree >= 0.998

@@ -1,0 +1,129 @@
+"""The composite entry points dh_ddit_forward, dh_sample_loop and
+dh_vocab_shard_reduce, called through the C ABI with no Python orchestration
+of the kernels.
+
+GPU: the forward equals the per-kernel forward bit for bit, and a whole
+generation equals the one the per-kernel entry points produce when driven
+from Python (engine.generate(native=False)) -- tokens and the per-transition
+counters.  CPU: argument checks return their status before any GPU work.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from diffusionhard_b200 import _lib
+from diffusionhard_b200.model import MDLMConfig, build_quantized
+from diffusionhard_b200.sampler import reveal_thresholds_q32
+
+SMALL = MDLMConfig(vocab_size=1000, mask_token_id=999, blocks=2)
+
+
+def test_composite_argument_checks_need_no_gpu():
+    assert _lib.raw("dh_ddit_forward", None, 1, 1, 64, 1, 1, 1 << 20, None, None) == 100
+    assert _lib.raw("dh_vocab_shard_reduce", None, 1, 1, None) == 100
+    w = _lib.MDLMWeights()
+    w.blocks = 0
+    w.vocabulary_size = 1000
+    w.mask_token_id = 999
+    w.max_positions = 1024
+    assert _lib.raw("dh_ddit_forward", ctypes.addressof(w), 1, 1, 64, 1, 1, 1 << 20, None, None) == 105
+    w.blocks = 2
+    assert _lib.raw("dh_ddit_forward", ctypes.addressof(w), 1, 1, 48, 1, 1, 1 << 20, None, None) == 103
+    assert _lib.raw("dh_ddit_forward", ctypes.addressof(w), 1, 1, 64, 1, 1, 1 << 20, None, None) == 100
+    thr = (ctypes.c_uint64 * 2)(1 << 31, (1 << 32) + 1)
+    assert _lib.raw("dh_sample_loop", ctypes.addressof(w), 1, 1, 1, 64, 2, ctypes.addressof(thr), 0, 0, 1,
+                    None, 1, 1 << 20, None) == 100
+    assert _lib.lib().dh_sample_loop_workspace_size(4, 1024) > _lib.lib().dh_ddit_forward_workspace_size(4, 1024)
+
+
+def test_weight_struct_layout():
+    # four uint32, three pointers, the block array pointer, the head's five
+    # pointers, two uint32 (natural alignment, LP64)
+    assert ctypes.sizeof(_lib.LinearWeights) == 40
+    assert _lib.MDLMWeights.head.offset == 16 + 4 * 8
+    assert ctypes.sizeof(_lib.MDLMWeights) == 16 + 32 + 40 + 8
+
+
+@pytest.mark.gpu
+def test_ddit_forward_equals_per_kernel_forward(cuda):
+    torch = cuda
+    from diffusionhard_b200.engine import MDLMEngine
+
+    qm = build_quantized(SMALL, seed=0)
+    B, L = 3, 256
+    eng = MDLMEngine(qm, B, L)
+    ids = torch.randint(0, 1000, (B * L,), generator=torch.Generator().manual_seed(4)).to(torch.int32).cuda()
+    eng.tokens.copy_(ids)
+    eng.forward()
+    ref = eng.x.clone()
+    x = torch.empty_like(ref)
+    ws = torch.empty(_lib.lib().dh_ddit_forward_workspace_size(B, L), dtype=torch.uint8, device="cuda")
+    w = eng.native_weights()
+    _lib.call("dh_ddit_forward", ctypes.addressof(w), _lib.ptr(ids), B, L, _lib.ptr(x), _lib.ptr(ws), ws.numel(),
+              None, _lib.stream_handle())
+    torch.cuda.synchronize()
+    assert torch.equal(x, ref)
+    assert _lib.raw("dh_ddit_forward", ctypes.addressof(w), _lib.ptr(ids), B, L, _lib.ptr(x), _lib.ptr(ws),
+                    ws.numel() - 1, None, None) == 102
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,steps", [(2, 256, 12), (3, 96, 8)])
+def test_sample_loop_equals_per_kernel_loop(cuda, B, L, steps):
+    torch = cuda
+    from diffusionhard_b200.engine import MDLMEngine
+
+    qm = build_quantized(SMALL, seed=0)
+    eng = MDLMEngine(qm, B, L)
+    eng.seq_offset = 5
+    ids = torch.full((B, L), SMALL.mask_token_id, dtype=torch.int64)
+    ids[:, ::7] = 3  # a few clean positions
+    ref, _ = eng.generate(ids.cuda(), steps=steps, seed=11, native=False)
+    ref = ref.clone()
+    ref_counters = eng.counters.clone()
+    # the composite entry point through ctypes, on fresh buffers
+    w = eng.native_weights()
+    ids_in = ids.reshape(-1).to(torch.int32).cuda()
+    tokens = torch.empty(B * L, dtype=torch.int32, device="cuda")
+    counters = torch.empty(3 * steps, dtype=torch.int32, device="cuda")
+    ws = torch.empty(_lib.lib().dh_sample_loop_workspace_size(B, L), dtype=torch.uint8, device="cuda")
+    thr = (ctypes.c_uint64 * steps)(*reveal_thresholds_q32(steps))
+    _lib.call("dh_sample_loop", ctypes.addressof(w), _lib.ptr(ids_in), _lib.ptr(tokens), B, L, steps,
+              ctypes.addressof(thr), 11, 5, _lib.ptr(counters), None, _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+    torch.cuda.synchronize()
+    assert torch.equal(tokens.view(B, L), ref)
+    assert torch.equal(counters, ref_counters)
+    assert not (tokens == SMALL.mask_token_id).any()
+    # and engine.generate's default route (the composite) gives the same
+    out, _ = eng.generate(ids.cuda(), steps=steps, seed=11, graph=True)
+    assert torch.equal(out, ref)
+    err = np.zeros(1, np.uint32)
+    _lib.call("dh_device_error", err.ctypes.data, 1)
+    assert err[0] == 0
+
+
+@pytest.mark.gpu
+def test_vocab_shard_reduce_on_one_rank(cuda, tmp_path):
+    """One-rank NCCL communicator: the all-reduce leaves the packed words as
+    they are.  (The multi-rank merge is tests/test_vocab_shard_gpu.py.)"""
+    torch = cuda
+    import torch.distributed as dist
+
+    from diffusionhard_b200.distributed import nccl_comm_handle
+
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised")
+    dist.init_process_group("nccl", init_method=f"file://{tmp_path}/pg", rank=0, world_size=1,
+                            device_id=torch.device("cuda", 0))
+    try:
+        comm = nccl_comm_handle(dist.group.WORLD, torch.device("cuda", 0))
+        assert comm
+        packed = torch.randint(0, 1 << 62, (257,), dtype=torch.int64, device="cuda")
+        before = packed.clone()
+        _lib.call("dh_vocab_shard_reduce", comm, _lib.ptr(packed), packed.numel(), _lib.stream_handle())
+        torch.cuda.synchronize()
+        assert torch.equal(packed, before)
+    finally:
+        dist.destroy_process_group()
