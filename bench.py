@@ -16,6 +16,12 @@ Prints one JSON line (rank 0).  `value` is device-timed (CUDA events, max
 over ranks) with inputs resident on the GPU; `e2e` is the same metric
 through the public drop-in API (run_ddpm_candidate_cache_sampler) from
 pinned host ids, with the host<->device copies inside the timed region.
+The line also carries, each measured after the headline on the same ranks:
+the whole-generation roofline (`step_roofline`), the measured int8 peak the
+int8 fractions use (`int8_peak`), the speed-mode throughput sweep of 512 x
+1024 canvases and 32 steps split over the N ranks (`strong_sweep`), and the
+single-sequence latency with the head vocab-sharded over the N ranks and the
+cost of its per-transition all-reduce (`vocab_shard`).
 """
 
 from __future__ import annotations
@@ -146,6 +152,166 @@ def time_kernel(fn, iters: int = 20) -> float:
     return s.elapsed_time(e) / iters
 
 
+def measure_int8_peak() -> dict:
+    """Dense int8 tensor throughput of this GPU, measured the way the bf16
+    peak is: a library int8 GEMM (torch._int_mm -> cuBLASLt, int32
+    accumulation) of 8192^3, best of 10 timed launches after warm-up
+    (2 * 8192^3 ops per launch)."""
+    import torch
+
+    n = 8192
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g).t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del a, b
+    torch.cuda.empty_cache()
+    return {"tops": round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1),
+            "how": "torch._int_mm (cuBLASLt) int8 x int8 -> int32, 8192^3, best of 10 launches, CUDA events"}
+
+
+# Algorithmic work of one forward, per row (SURVEY-style units of the MDLM
+# specification, model_spec.py:29-84): backbone int8 ops, attention FLOP per
+# key, and the bytes the memory-bound row kernels must move.
+BACKBONE_OPS_PER_ROW = 2 * 12 * (768 * 2304 + 768 * 768 + 2 * 768 * 3072)  # 169,869,312
+ATTN_FLOP_PER_ROW_PER_KEY = 36864
+HEAD_OPS_PER_ROW = 2 * 768 * 50258  # 77,196,288
+STREAM_BYTES_PER_ROW = (12 * (2 * (768 * 4 + 768 + 4) + (768 * 2 + 768 + 4) + (3072 * 2 + 3072 + 4))
+                        + (768 * 4 * 2 + 4))
+
+
+def step_roofline(ms_per_generation: float, rows: int, kv_len: int, evaluations: int, head_rows: int,
+                  int8_tops: float, bf16_tflops: float, hbm_gbs: float) -> dict:
+    """Whole-generation roofline: the time the algorithmic work would take at
+    the peaks, each kind of work at its own peak and summed
+    (int8 ops / int8 peak + bf16 FLOP / bf16 peak + stream bytes / HBM), over
+    the measured time."""
+    int8_ops = evaluations * rows * BACKBONE_OPS_PER_ROW + head_rows * HEAD_OPS_PER_ROW
+    bf16_flop = evaluations * rows * ATTN_FLOP_PER_ROW_PER_KEY * kv_len
+    stream = evaluations * rows * STREAM_BYTES_PER_ROW
+    t = {"int8": int8_ops / (int8_tops * 1e12), "bf16": bf16_flop / (bf16_tflops * 1e12),
+         "hbm": stream / (hbm_gbs * 1e9)}
+    ideal_ms = sum(t.values()) * 1e3
+    return {"ideal_ms": round(ideal_ms, 2), "measured_ms": round(ms_per_generation, 2),
+            "frac": round(ideal_ms / ms_per_generation, 4),
+            "ideal_ms_by_kind": {k: round(v * 1e3, 2) for k, v in t.items()},
+            "work": {"int8_ops": int8_ops, "bf16_flop": bf16_flop, "stream_bytes": stream,
+                     "evaluations": evaluations, "rows_per_evaluation": rows, "head_rows": head_rows},
+            "peaks": {"int8_tops": int8_tops, "bf16_tflops": bf16_tflops, "hbm_gbs": hbm_gbs}}
+
+
+def strong_sweep(qm, world: int, rank: int, global_batch: int = 512, steps: int = 32, warmup: int = 3,
+                 iters: int = 2) -> dict:
+    """The throughput sweep of the speed mode: global_batch x 1024 all-masked
+    canvases split over the ranks (strong scaling), `steps` transitions +
+    the final pass; device time, max over ranks."""
+    import torch
+
+    from diffusionhard_b200.distributed import shard_batch
+    from diffusionhard_b200.engine import MDLMEngine
+
+    offset, B = shard_batch(global_batch, world, rank)
+    eng = MDLMEngine(qm, B, 1024)
+    eng.seq_offset = offset
+    ids = torch.full((B, 1024), qm.config.mask_token_id, dtype=torch.int64, device="cuda")
+    for _ in range(warmup):
+        eng.generate(ids, steps=steps, seed=0, graph=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        eng.generate(ids, steps=steps, seed=0, graph=True)
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e), world) / iters
+    meta = eng.metadata(steps)
+    eng._graphs.clear()
+    del eng
+    torch.cuda.empty_cache()
+    return {"value": round(global_batch * 1024 / (ms * 1e-3), 1), "unit": "tok/s", "scaling": "strong",
+            "n_gpus": world, "global_batch": global_batch, "sequences_per_gpu": B, "seq_len": 1024,
+            "steps": steps, "ms_per_generation": round(ms, 3), "warmup": warmup, "timed": iters,
+            "model_evaluations": meta["model_evaluations"]}
+
+
+def vocab_shard_latency(qm, world: int, rank: int, steps: int = 64, warmup: int = 3, iters: int = 3) -> dict:
+    """Single-sequence latency with the head split over the ranks and merged
+    by dh_vocab_shard_reduce (NCCL all-reduce of the packed per-row words)
+    after every head launch; beside it, the time of that all-reduce alone
+    (back-to-back calls on the 1024 packed words of a transition)."""
+    import torch
+
+    from diffusionhard_b200 import _lib
+    from diffusionhard_b200.distributed import vocab_shards
+    from diffusionhard_b200.engine import MDLMEngine
+
+    L = 1024
+    eng = MDLMEngine(qm, 1, L)
+    if world > 1:
+        import torch.distributed as dist
+
+        v0, v1 = vocab_shards(qm.config.vocab_size, world)[rank]
+        eng.shard_head(v0, v1, group=dist.group.WORLD)
+    ids = torch.full((1, L), qm.config.mask_token_id, dtype=torch.int64, device="cuda")
+    for _ in range(warmup):
+        eng.generate(ids, steps=steps, seed=0, graph=False)
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        eng.generate(ids, steps=steps, seed=0, graph=False)
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e), world) / iters
+    tokens = eng.tokens.clone()
+    agree = True
+    reduce_us = None
+    if world > 1:
+        import torch.distributed as dist
+
+        gathered = [torch.empty_like(tokens) for _ in range(world)]
+        dist.all_gather(gathered, tokens)
+        agree = all(torch.equal(g, tokens) for g in gathered)
+        comm = eng._nccl_comm()
+        packed = torch.zeros(L, dtype=torch.int64, device="cuda")
+        for _ in range(10):
+            _lib.call("dh_vocab_shard_reduce", comm, _lib.ptr(packed), L, _lib.stream_handle())
+        torch.cuda.synchronize()
+        barrier(world)
+        n = 200
+        s.record()
+        for _ in range(n):
+            _lib.call("dh_vocab_shard_reduce", comm, _lib.ptr(packed), L, _lib.stream_handle())
+        e.record()
+        torch.cuda.synchronize()
+        reduce_us = max_over_ranks(s.elapsed_time(e), world) / n * 1e3
+    meta = eng.metadata(steps)
+    del eng
+    torch.cuda.empty_cache()
+    out = {"value": round(L / (ms * 1e-3), 1), "unit": "tok/s", "ms_per_generation": round(ms, 3),
+           "n_gpus": world, "head_split": world, "seq_len": L, "steps": steps,
+           "model_evaluations": meta["model_evaluations"], "ranks_agree_on_tokens": agree,
+           "loop": "dh_sample_loop, eager launches (no graph)"}
+    if reduce_us is not None:
+        transitions = steps + 1
+        out["allreduce_us_per_transition"] = round(reduce_us, 2)
+        out["allreduce_ms_per_generation"] = round(reduce_us * transitions / 1e3, 3)
+        out["allreduce_share"] = round(reduce_us * transitions / 1e3 / ms, 4)
+    return out
+
+
 def kernel_breakdown(eng) -> dict:
     """Per-kernel average launch time of one forward's kernels (ms)."""
     from diffusionhard_b200 import _lib
@@ -179,9 +345,9 @@ def kernel_breakdown(eng) -> dict:
     return {name: time_kernel(fn) for name, fn in fns.items()}
 
 
-def roofline_for(name: str, ms: float, eng, peaks: dict, peaks_kind: str) -> dict:
+def roofline_for(name: str, ms: float, eng, peaks: dict, peaks_kind: str, int8: dict) -> dict:
     M, L, B = eng.M, eng.L, eng.B
-    int8_peak = 2.0 * peaks["bf16_tflops"]
+    int8_peak = int8["tops"]
     gemm = {"gemm_qkv_rope": (768, 2304), "gemm_out_residual": (768, 768), "gemm_up_gelu": (768, 3072),
             "gemm_down_residual": (3072, 768)}
     if name in gemm:
@@ -189,7 +355,7 @@ def roofline_for(name: str, ms: float, eng, peaks: dict, peaks_kind: str) -> dic
         ach = 2.0 * M * N * K / (ms * 1e-3) / 1e12
         return {"kernel": name, "bound": "tensor", "achieved": round(ach, 1),
                 "peak": round(int8_peak, 1), "unit": "TOP/s", "frac": round(ach / int8_peak, 4),
-                "peak_source": f"int8 dense = 2 x {peaks_kind} bf16 burst ({peaks['bf16_tflops']} TFLOP/s)",
+                "peak_source": "measured int8: " + int8["how"],
                 "work_per_launch": f"2*{M}*{N}*{K} int8 ops"}
     if name == "attention":
         flops = 4.0 * B * 12 * L * eng.kv_len * 64
@@ -205,7 +371,7 @@ def roofline_for(name: str, ms: float, eng, peaks: dict, peaks_kind: str) -> dic
             "work_per_launch": f"{bytes_per} bytes"}
 
 
-def head_microbench(qm, peaks: dict, peaks_kind: str) -> dict:
+def head_microbench(qm, peaks: dict, peaks_kind: str, int8: dict) -> dict:
     """Fused head + sampler on the head-microbench shape: 32768 masked rows
     (B=64 x L=1024, 50% masked) x 50258 vocab x 768, Philox-Gumbel argmax."""
     import numpy as np
@@ -234,7 +400,7 @@ def head_microbench(qm, peaks: dict, peaks_kind: str) -> dict:
     ms = time_kernel(run, iters=10)
     ops = 2.0 * rows * V * 768
     ach = ops / (ms * 1e-3) / 1e12
-    int8_peak = 2.0 * peaks["bf16_tflops"]
+    int8_peak = int8["tops"]
     del np
     return {"rows": rows, "vocab": V, "ms": round(ms, 4), "achieved_top_s": round(ach, 1),
             "int8_peak_top_s": round(int8_peak, 1), "tensor_frac": round(ach / int8_peak, 4),
@@ -570,17 +736,23 @@ def main() -> None:
     e2e_value = tokens / (e2e_ms * 1e-3)
 
     # ------------------------------------------------ kernel breakdown / roofline
+    int8 = measure_int8_peak()
     bd = kernel_breakdown(eng)
     per_gen = {k: v * (1 if k == "embed_gather" else (len(eng.blocks) * (2 if k == "ln_smooth_quant" else 1)))
                for k, v in bd.items()}
     dominant = max(per_gen, key=per_gen.get)
-    roof = roofline_for(dominant, bd[dominant], eng, peaks, peaks_kind)
+    roof = roofline_for(dominant, bd[dominant], eng, peaks, peaks_kind, int8)
     traffic_file = ROOT / "profiles" / "traffic.json"
     traffic = None
     if traffic_file.exists():
         traffic = json.loads(traffic_file.read_text()).get(dominant)
     roof["traffic"] = traffic
-    head = head_microbench(qm, peaks, peaks_kind) if rank == 0 else None
+    head = head_microbench(qm, peaks, peaks_kind, int8) if rank == 0 else None
+    step_roof = step_roofline(ms / args.steps, B * L, eng.kv_len, meta["model_evaluations"], B * L,
+                              int8["tops"], peaks["bf16_tflops"], peaks["hbm_gbs"])
+    eng._graphs.clear()
+    sweep = strong_sweep(qm, world, rank)
+    shard = vocab_shard_latency(qm, world, rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -607,12 +779,16 @@ def main() -> None:
             "e2e": {"value": round(e2e_value, 1), "unit": "tok/s", "h2d_bytes_per_step": B * L * 8,
                     "d2h_bytes_per_step": B * L * 8 + 3 * S * 4, "wall_ms_per_step": round(wall_e2e / args.steps, 3)},
             "roofline": roof,
+            "step_roofline": step_roof,
+            "int8_peak": int8,
             "cpu_baseline": cpu,
             "gpu_launches": eng.launches_per_generation(S) * args.steps,
             "clocks": clock_info,
             "kernel_ms": {k: round(v, 4) for k, v in bd.items()},
             "kernel_ms_per_generation_est": {k: round(v * (S + 1), 2) for k, v in per_gen.items()},
             "head_microbench": head,
+            "strong_sweep": sweep,
+            "vocab_shard": shard,
             "generation": {"model_evaluations": meta["model_evaluations"],
                            "sampling_transitions": meta["sampling_transitions"], "masks_left": masks_left,
                            "e2e_matches_device": bool(torch.equal(ids_out.cuda().to(torch.int32), eng.tokens.view(B, L)))},

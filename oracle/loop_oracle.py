@@ -50,12 +50,14 @@ def thresholds_q32(steps: int, sampling_epsilon: float = 1e-5) -> List[int]:
 
 
 def generate(qm, ids: np.ndarray, *, steps: int, seed: int, seq_offset: int = 0,
-             sampling_epsilon: float = 1e-5,
+             sampling_epsilon: float = 1e-5, ln_fp64: bool = False,
              on_transition: Optional[Callable[[int, np.ndarray], None]] = None) -> Dict[str, object]:
     """Candidate-cache generation of ids [B, L] (int, mask = model mask id).
     Returns {"tokens": [B, L] int32, "evaluations": per-sequence counts,
     "changed": per-transition changed counts}.  on_transition(k, tokens) is
-    called after each transition's commit."""
+    called after each transition's commit.  ln_fp64: the forward's
+    LayerNorms in float64 (model_oracle.forward), a second CPU evaluation of
+    the same arithmetic."""
     mask = qm.config.mask_token_id
     tokens = np.array(ids, dtype=np.int32, copy=True)
     B, L = tokens.shape
@@ -75,7 +77,7 @@ def generate(qm, ids: np.ndarray, *, steps: int, seed: int, seq_offset: int = 0,
                 continue
             if final or need[b]:
                 rec: Dict[str, object] = {}
-                model_oracle.forward(qm, tokens[b:b + 1], record=rec)
+                model_oracle.forward(qm, tokens[b:b + 1], record=rec, ln_fp64=ln_fp64)
                 hidden[b] = (rec["head_q"].numpy(), rec["head_scale"].numpy())
                 evaluations[b] += 1
                 if not final:

@@ -90,8 +90,13 @@ def block_causal_bias(length: int, block_ends):
 
 def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
             prefix_kv: Optional[List[Tuple[object, object]]] = None, capture_kv: bool = False,
-            record: Optional[Dict[str, object]] = None, block_ends: Optional[List[int]] = None):
+            record: Optional[Dict[str, object]] = None, block_ends: Optional[List[int]] = None,
+            ln_fp64: bool = False):
     """W8A8 forward of `ids` [B, L].  Returns the final LayerNorm output [B, L, d].
+
+    ln_fp64: compute every LayerNorm in float64 and round its output to
+        float32 -- the same arithmetic with other rounding, which measures how
+        far two CPU evaluations of the reference agree.
 
     positions: rotary positions of the rows (default 0..L-1).
     block_ends: completed block boundaries for block-causal attention.
@@ -106,6 +111,10 @@ def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
     cfg = qm.config
     B, L = ids.shape
     pos = np.arange(L) if positions is None else positions
+
+    def layer_norm(t, shape):
+        return F.layer_norm(t.double(), shape).float() if ln_fp64 else F.layer_norm(t, shape)
+
     cos = torch.from_numpy(qm.rope_cos[pos])[None, :, None, :]
     sin = torch.from_numpy(qm.rope_sin[pos])[None, :, None, :]
     kv = []
@@ -115,7 +124,7 @@ def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
     with torch.no_grad():
         x = torch.from_numpy(qm.embedding)[torch.from_numpy(ids.astype(np.int64))]
         for i, blk in enumerate(qm.blocks):
-            h = F.layer_norm(x, [cfg.hidden]).reshape(B * L, cfg.hidden)
+            h = layer_norm(x, [cfg.hidden]).reshape(B * L, cfg.hidden)
             qkv = w8a8_linear(h, blk["qkv"]).view(B, L, 3, cfg.heads, cfg.head_dim)
             q, k, v = qkv.unbind(dim=2)
             q, k = _rot(q, cos, sin), _rot(k, cos, sin)
@@ -128,12 +137,12 @@ def forward(qm, ids: np.ndarray, *, positions: Optional[np.ndarray] = None,
                                                attn_mask=bias)
             a = a.transpose(1, 2).reshape(B * L, cfg.hidden)
             x = x + w8a8_linear(a, blk["out"]).view(B, L, cfg.hidden)
-            h = F.layer_norm(x, [cfg.hidden]).reshape(B * L, cfg.hidden)
+            h = layer_norm(x, [cfg.hidden]).reshape(B * L, cfg.hidden)
             u = F.gelu(w8a8_linear(h, blk["up"]), approximate="tanh")
             x = x + w8a8_linear(u, blk["down"]).view(B, L, cfg.hidden)
             if record is not None:
                 record[f"x{i}"] = x.clone()
-        h = F.layer_norm(x, [cfg.hidden])
+        h = layer_norm(x, [cfg.hidden])
         if record is not None:
             record["head_q"], record["head_scale"] = quantize_rows(h.reshape(B * L, cfg.hidden), qm.head.smooth)
             if capture_kv:

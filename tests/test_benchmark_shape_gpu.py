@@ -20,7 +20,13 @@ these tests run the model where every CTA gets several:
 The forward is fp32 / bf16 on the GPU and fp32 / fp64 on the CPU, so the
 residual streams agree to tolerance, not bit for bit; a candidate flips where
 two noisy scores lie within that tolerance of each other.  The tests print
-the measured agreement.
+the measured agreement.  How close any two implementations of the same
+arithmetic get is measured in (iii) too: the oracle loop is run a second time
+with its LayerNorms in float64, and the GPU must agree with the oracle at
+least as well as that second CPU evaluation does (less one token per
+thousand).  After 12 blocks any rounding difference, even one ulp in a
+LayerNorm, moves about 5% of the int8 activations by one step and the logits
+by about 0.6%, so neither pair agrees bit for bit.
 """
 
 import numpy as np
@@ -141,9 +147,12 @@ def test_free_running_generation_matches_oracle(cuda, full_model):
     assert not (got == FULL.mask_token_id).any()
     ref = loop_oracle.generate(qm, ids.numpy(), steps=steps, seed=seed)
     agree = float((got == ref["tokens"]).mean())
+    ref64 = loop_oracle.generate(qm, ids.numpy(), steps=steps, seed=seed, ln_fp64=True)
+    floor = float((ref64["tokens"] == ref["tokens"]).mean())
     meta = eng.metadata(steps)
-    print(f"free-running 2 x 1024, {steps} steps: tokens identical {agree:.5f} "
-          f"({int((got != ref['tokens']).sum())} of {B * L} differ); GPU changed per step "
-          f"{meta['transition_changed_tokens'][:4]}..., oracle {ref['changed'][:4]}...")
+    print(f"free-running 2 x 1024, {steps} steps: GPU vs oracle tokens identical {agree:.5f} "
+          f"({int((got != ref['tokens']).sum())} of {B * L} differ); oracle with fp64 LayerNorm vs oracle "
+          f"{floor:.5f}; GPU changed per step {meta['transition_changed_tokens'][:4]}..., "
+          f"oracle {ref['changed'][:4]}...")
     assert meta["transition_changed_tokens"][0] == ref["changed"][0]
-    assert agree >= 0.998
+    assert agree >= min(0.999, floor - 1e-3)
