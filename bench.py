@@ -324,20 +324,20 @@ def kernel_breakdown(eng) -> dict:
     fns = {
         "embed_gather": lambda: c("dh_embed_gather", p(eng.tokens), p(eng.embedding), p(eng.x), M,
                                   eng.cfg.vocab_size, None, s),
-        "ln_smooth_quant": lambda: c("dh_ln_smooth_quant", p(eng.x), p(qkv.smooth), p(eng.act_q),
+        "ln_smooth_quant": lambda: c("dh_ln_smooth_quant", p(eng.x), p(qkv.smooth), p(qkv.inv_smooth), p(eng.act_q),
                                      p(eng.act_scale), M, None, None, None, s),
         "gemm_qkv_rope": lambda: c("dh_gemm_qkv_rope", p(eng.act_q), p(eng.act_scale), p(qkv.w),
                                    p(qkv.w_scale), p(qkv.bias), p(eng.rope_cos), p(eng.rope_sin), p(out.inv_smooth), M, L, 0,
                                    eng.kv_stride, 0, p(eng.q), p(k), p(vt), None, s),
         "attention": lambda: c("dh_attention", p(eng.q), p(k), p(vt), p(eng.attn), eng.B, L, eng.kv_len,
                                eng.kv_stride, None, s),
-        "quant_rows_768": lambda: c("dh_quant_rows_bf16", p(eng.attn), None, p(eng.act_q),
+        "quant_rows_768": lambda: c("dh_quant_rows_bf16", p(eng.attn), None, None, p(eng.act_q),
                                     p(eng.act_scale), M, 768, None, s),
         "gemm_out_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(out.w),
                                        p(out.w_scale), p(out.bias), p(eng.x), M, 768, 768, None, s),
         "gemm_up_gelu": lambda: c("dh_gemm_gelu", p(eng.act_q), p(eng.act_scale), p(up.w), p(up.w_scale),
                                   p(up.bias), p(down.inv_smooth), p(eng.mlp), M, 3072, 768, None, s),
-        "quant_rows_3072": lambda: c("dh_quant_rows_bf16", p(eng.mlp), None, p(eng.act_q),
+        "quant_rows_3072": lambda: c("dh_quant_rows_bf16", p(eng.mlp), None, None, p(eng.act_q),
                                      p(eng.act_scale), M, 3072, None, s),
         "gemm_down_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(down.w),
                                         p(down.w_scale), p(down.bias), p(eng.x), M, 768, 3072, None, s),

@@ -138,17 +138,17 @@ uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32
         const dh_linear_weights& out = w->block_linears[4 * i + 1];
         const dh_linear_weights& up = w->block_linears[4 * i + 2];
         const dh_linear_weights& down = w->block_linears[4 * i + 3];
-        DH_TRY(dh_ln_smooth_quant(x, qkv.smooth, act_q, act_scale, M, nullptr, nullptr, run_rows, s));
+        DH_TRY(dh_ln_smooth_quant(x, qkv.smooth, qkv.inv_smooth, act_q, act_scale, M, nullptr, nullptr, run_rows, s));
         DH_TRY(dh_gemm_qkv_rope(act_q, act_scale, qkv.weight, qkv.w_scale, qkv.bias, w->rope_cos, w->rope_sin,
                                 out.inv_smooth, M, L, 0, L, 0, q, k, vt, run_rows, s));
         DH_TRY(dh_attention(q, k, vt, attn, B, L, L, L, run_rows, s));
-        DH_TRY(dh_quant_rows_bf16(attn, nullptr, act_q, act_scale, M, kHidden, run_rows, s));
+        DH_TRY(dh_quant_rows_bf16(attn, nullptr, nullptr, act_q, act_scale, M, kHidden, run_rows, s));
         DH_TRY(dh_gemm_residual(act_q, act_scale, out.weight, out.w_scale, out.bias, x, M, kHidden, kHidden,
                                 run_rows, s));
-        DH_TRY(dh_ln_smooth_quant(x, up.smooth, act_q, act_scale, M, nullptr, nullptr, run_rows, s));
+        DH_TRY(dh_ln_smooth_quant(x, up.smooth, up.inv_smooth, act_q, act_scale, M, nullptr, nullptr, run_rows, s));
         DH_TRY(dh_gemm_gelu(act_q, act_scale, up.weight, up.w_scale, up.bias, down.inv_smooth, mlp, M, kMlp,
                             kHidden, run_rows, s));
-        DH_TRY(dh_quant_rows_bf16(mlp, nullptr, act_q, act_scale, M, kMlp, run_rows, s));
+        DH_TRY(dh_quant_rows_bf16(mlp, nullptr, nullptr, act_q, act_scale, M, kMlp, run_rows, s));
         DH_TRY(dh_gemm_residual(act_q, act_scale, down.weight, down.w_scale, down.bias, x, M, kHidden, kMlp,
                                 run_rows, s));
     }
@@ -253,7 +253,7 @@ uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids
         DH_TRY(enqueue_forward(w, tokens, B, L, x, workspace, o, fwd_rows, s));
         DH_TRY(dh_loop_select(B, L, k, seed, seq_offset, 0, final_pass ? 0 : thresholds_q32[t], final_pass, active,
                               eval_id, sel_rows, sel_pos, sel_key, sel_eval, sel_count, s));
-        DH_TRY(dh_ln_smooth_quant(x, w->head.smooth, head_q, head_scale, M, sel_rows, sel_count, nullptr, s));
+        DH_TRY(dh_ln_smooth_quant(x, w->head.smooth, w->head.inv_smooth, head_q, head_scale, M, sel_rows, sel_count, nullptr, s));
         DH_TRY(dh_head_argmax_i8(head_q, kHidden, w->head.weight, kHidden, M, sel_count, kHidden, w->head_rows,
                                  w->head_vocab_offset, w->mask_token_id, final_pass ? 2u : 1u, head_scale,
                                  w->head.w_scale, w->head.bias, nullptr, nullptr, nullptr, sel_pos, sel_key, sel_eval,

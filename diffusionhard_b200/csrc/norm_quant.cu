@@ -8,8 +8,12 @@
 //                          output, GELU output)
 // The quantiser divides as the reference does: a = x / s, scale = amax / 127,
 // q = round_half_even(a / scale) clamped to +-127, every quotient the
-// IEEE-rounded fp32 division (__fdiv_rn), so the same fp32 input row gives
-// the same bytes and row scale as fixed_mlp._quantize_symmetric.
+// IEEE-rounded fp32 quotient, so the same fp32 input row gives the same bytes
+// and row scale as fixed_mlp._quantize_symmetric.  Divisions by a value used
+// many times (the row scale, the per-column SmoothQuant scale) multiply by
+// the rounded reciprocal and correct the product once by its exact residual,
+// which yields the rounded quotient at the cost of three FMA-pipe operations
+// (see Divisor).
 // One warp per row; rows are read once (float4 / 16-byte vector loads) and
 // kept in registers between the statistics and the quantisation pass.
 #include <cuda_bf16.h>
@@ -33,16 +37,42 @@ constexpr uint32_t kWideRowWarps = 1;
 // conversion on the (quarter-rate) XU pipe; the result equals rintf / cvt.rni.
 DH_DEVINL uint32_t rint_bits(float v) { return __float_as_uint(__fadd_rn(v, 12582912.0f)); }
 
+// Division by b > 0 with its reciprocal r = RN(1 / b) precomputed: the
+// estimate q0 = RN(a r) is within an ulp of a / b, its residual a - q0 b is
+// exact in one FMA, and RN(q0 + (a - q0 b) r) is the correctly rounded
+// quotient (Markstein's correction step for a correctly rounded reciprocal,
+// with no overflow or underflow at these magnitudes).  A divisor whose
+// significand is all ones is divided directly instead, so that no
+// edge of the correction argument is relied on.
+struct Divisor {
+    float b, r;
+    bool direct;
+};
+DH_DEVINL Divisor make_divisor(float b, float r) {
+    return {b, r, (__float_as_uint(b) & 0x7FFFFFu) == 0x7FFFFFu};
+}
+DH_DEVINL Divisor make_divisor(float b) { return make_divisor(b, __frcp_rn(b)); }
+DH_DEVINL float divide(float a, const Divisor& d) {
+    if (d.direct) return __fdiv_rn(a, d.b);
+    const float q0 = __fmul_rn(a, d.r);
+    return __fmaf_rn(__fmaf_rn(-q0, d.b, a), d.r, q0);
+}
+
 // int8 of round_half_even(a / scale) clamped to +-127
 // (fixed_mlp._quantize_symmetric, fixed_mlp.py:24-35: torch.round(x /
 // scale).clamp(-127, 127); clamping the quotient first gives the same byte,
 // 127 being an integer).
-DH_DEVINL uint32_t q8_div_bits(float a, float scale) {
-    return rint_bits(fminf(fmaxf(__fdiv_rn(a, scale), -127.0f), 127.0f));
+DH_DEVINL uint32_t q8_div_bits(float a, const Divisor& scale) {
+    return rint_bits(fminf(fmaxf(divide(a, scale), -127.0f), 127.0f));
 }
 
 // Row scale of the reference: amax / 127 (fp32 division), 1 for an all-zero row.
 DH_DEVINL float row_scale(float amax) { return amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f; }
+
+// Per-column SmoothQuant divisor: s and, when the caller gives it, RN(1 / s).
+DH_DEVINL Divisor column_divisor(float s, const float* inv, uint32_t c) {
+    return inv ? make_divisor(s, __ldg(inv + c)) : make_divisor(s);
+}
 
 // four int8 (low bytes of a, b, c, d) into one word, a lowest
 DH_DEVINL uint32_t pack4_i8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -69,7 +99,7 @@ embed_gather_kernel(const int32_t* __restrict__ tokens, const float* __restrict_
 // input row rows_index[i] (used to project only selected rows).
 __global__ void __launch_bounds__(kRowWarps * 32)
 ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ smooth,
-                int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
+                const float* __restrict__ inv_smooth, int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
                 const uint32_t* __restrict__ rows_index, const uint32_t* __restrict__ rows_count,
                 const uint32_t* __restrict__ run_flag) {
     if (run_flag && *run_flag == 0u) return;
@@ -98,20 +128,22 @@ ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ smooth,
     float amax = 0.f;
 #pragma unroll
     for (uint32_t j = 0; j < kD / 128; ++j) {
+        const uint32_t c = 4 * (lane_id() + 32 * j);
         const float4 s = __ldg(sm + lane_id() + 32 * j);
-        v[j].x = __fdiv_rn((v[j].x - mean) * rstd, s.x);
-        v[j].y = __fdiv_rn((v[j].y - mean) * rstd, s.y);
-        v[j].z = __fdiv_rn((v[j].z - mean) * rstd, s.z);
-        v[j].w = __fdiv_rn((v[j].w - mean) * rstd, s.w);
+        v[j].x = divide((v[j].x - mean) * rstd, column_divisor(s.x, inv_smooth, c));
+        v[j].y = divide((v[j].y - mean) * rstd, column_divisor(s.y, inv_smooth, c + 1));
+        v[j].z = divide((v[j].z - mean) * rstd, column_divisor(s.z, inv_smooth, c + 2));
+        v[j].w = divide((v[j].w - mean) * rstd, column_divisor(s.w, inv_smooth, c + 3));
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
     }
     amax = warp_max_f32(amax);
     const float sc = row_scale(amax);
+    const Divisor dsc = make_divisor(sc);
     uint32_t* dst = reinterpret_cast<uint32_t*>(out + static_cast<uint64_t>(i) * kD);
 #pragma unroll
     for (uint32_t j = 0; j < kD / 128; ++j)
-        dst[lane_id() + 32 * j] = pack4_i8(q8_div_bits(v[j].x, sc), q8_div_bits(v[j].y, sc),
-                                           q8_div_bits(v[j].z, sc), q8_div_bits(v[j].w, sc));
+        dst[lane_id() + 32 * j] = pack4_i8(q8_div_bits(v[j].x, dsc), q8_div_bits(v[j].y, dsc),
+                                           q8_div_bits(v[j].z, dsc), q8_div_bits(v[j].w, dsc));
     if (lane_id() == 0) scale[i] = sc;
 }
 
@@ -125,7 +157,7 @@ ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ smooth,
 template <uint32_t C, bool kSmooth>
 __global__ void __launch_bounds__(kRowWarps * 32)
 quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __restrict__ smooth,
-                       int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
+                       const float* __restrict__ inv_smooth, int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
                        const uint32_t* __restrict__ run_flag) {
     if (run_flag && *run_flag == 0u) return;
     const uint32_t r = blockIdx.x * kRowWarps + warp_id();
@@ -149,19 +181,20 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
 #pragma unroll
             for (uint32_t e = 0; e < 4; ++e) {
                 const float2 f = __bfloat1622float2(h[e]);
-                a[j][2 * e] = __fdiv_rn(f.x, sv[2 * e]);
-                a[j][2 * e + 1] = __fdiv_rn(f.y, sv[2 * e + 1]);
+                a[j][2 * e] = divide(f.x, column_divisor(sv[2 * e], inv_smooth, 4 * c4 + 2 * e));
+                a[j][2 * e + 1] = divide(f.y, column_divisor(sv[2 * e + 1], inv_smooth, 4 * c4 + 2 * e + 1));
                 amax = fmaxf(amax, fmaxf(fabsf(a[j][2 * e]), fabsf(a[j][2 * e + 1])));
             }
         }
         const float sc = row_scale(warp_max_f32(amax));
+        const Divisor d = make_divisor(sc);
 #pragma unroll
         for (uint32_t j = 0; j < kVec; ++j)
             dst[lane_id() + 32 * j] =
-                make_uint2(pack4_i8(q8_div_bits(a[j][0], sc), q8_div_bits(a[j][1], sc), q8_div_bits(a[j][2], sc),
-                                    q8_div_bits(a[j][3], sc)),
-                           pack4_i8(q8_div_bits(a[j][4], sc), q8_div_bits(a[j][5], sc), q8_div_bits(a[j][6], sc),
-                                    q8_div_bits(a[j][7], sc)));
+                make_uint2(pack4_i8(q8_div_bits(a[j][0], d), q8_div_bits(a[j][1], d), q8_div_bits(a[j][2], d),
+                                    q8_div_bits(a[j][3], d)),
+                           pack4_i8(q8_div_bits(a[j][4], d), q8_div_bits(a[j][5], d), q8_div_bits(a[j][6], d),
+                                    q8_div_bits(a[j][7], d)));
         if (lane_id() == 0) scale[r] = sc;
         return;
     }
@@ -173,6 +206,7 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
         for (uint32_t e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
     }
     const float sc = row_scale(warp_max_f32(fmaxf(__low2float(m2), __high2float(m2))));
+    const Divisor d = make_divisor(sc);
 #pragma unroll
     for (uint32_t j = 0; j < kVec; ++j) {
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
@@ -180,8 +214,8 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
 #pragma unroll
         for (uint32_t e = 0; e < 4; e += 2) {
             const float2 f0 = __bfloat1622float2(h[e]), f1 = __bfloat1622float2(h[e + 1]);
-            packed[e >> 1] = pack4_i8(q8_div_bits(f0.x, sc), q8_div_bits(f0.y, sc), q8_div_bits(f1.x, sc),
-                                      q8_div_bits(f1.y, sc));
+            packed[e >> 1] = pack4_i8(q8_div_bits(f0.x, d), q8_div_bits(f0.y, d), q8_div_bits(f1.x, d),
+                                      q8_div_bits(f1.y, d));
         }
         dst[lane_id() + 32 * j] = make_uint2(packed[0], packed[1]);
     }
@@ -210,6 +244,7 @@ quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __rest
         for (uint32_t e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
     }
     const float sc = row_scale(warp_max_f32(fmaxf(__low2float(m2), __high2float(m2))));
+    const Divisor d = make_divisor(sc);
     uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * cols);
 #pragma unroll 4
     for (uint32_t j = lane_id(); j < nvec; j += 32) {
@@ -219,8 +254,8 @@ quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __rest
 #pragma unroll
         for (uint32_t e = 0; e < 4; e += 2) {
             const float2 f0 = __bfloat1622float2(h[e]), f1 = __bfloat1622float2(h[e + 1]);
-            packed[e >> 1] = pack4_i8(q8_div_bits(f0.x, sc), q8_div_bits(f0.y, sc), q8_div_bits(f1.x, sc),
-                                      q8_div_bits(f1.y, sc));
+            packed[e >> 1] = pack4_i8(q8_div_bits(f0.x, d), q8_div_bits(f0.y, d), q8_div_bits(f1.x, d),
+                                      q8_div_bits(f1.y, d));
         }
         dst[j] = make_uint2(packed[0], packed[1]);
     }
@@ -247,7 +282,7 @@ uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x
     return DH_OK;
 }
 
-uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, int8_t* out, float* scale,
+uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
                             const uint32_t* run_flag, void* stream) {
     if (!x || !smooth || !out || !scale) return DH_ERR_NULL_POINTER;
@@ -256,13 +291,13 @@ uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, int8_t* out, fl
          reinterpret_cast<uintptr_t>(out)) & 15u)
         return DH_ERR_ALIGNMENT;
     ln_quant_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
-                      static_cast<cudaStream_t>(stream)>>>(x, smooth, out, scale, rows,
+                      static_cast<cudaStream_t>(stream)>>>(x, smooth, inv_smooth, out, scale, rows,
                                                            rows_index, rows_count, run_flag);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }
 
-uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, int8_t* out, float* scale,
+uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream) {
     if (!in || !out || !scale) return DH_ERR_NULL_POINTER;
     if (rows == 0) return DH_OK;
@@ -273,13 +308,13 @@ uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, int8_t* out, fl
     const uint32_t grid = (rows + kRowWarps - 1) / kRowWarps;
     const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(in);
     if (cols == 768 && smooth)
-        quant_rows_bf16_kernel<768, true><<<grid, kRowWarps * 32, 0, st>>>(src, smooth, out, scale, rows,
+        quant_rows_bf16_kernel<768, true><<<grid, kRowWarps * 32, 0, st>>>(src, smooth, inv_smooth, out, scale, rows,
                                                                            run_flag);
     else if (cols == 768)
-        quant_rows_bf16_kernel<768, false><<<grid, kRowWarps * 32, 0, st>>>(src, nullptr, out, scale, rows,
+        quant_rows_bf16_kernel<768, false><<<grid, kRowWarps * 32, 0, st>>>(src, nullptr, nullptr, out, scale, rows,
                                                                             run_flag);
     else if (cols == 3072 && smooth)
-        quant_rows_bf16_kernel<3072, true><<<grid, kRowWarps * 32, 0, st>>>(src, smooth, out, scale, rows,
+        quant_rows_bf16_kernel<3072, true><<<grid, kRowWarps * 32, 0, st>>>(src, smooth, inv_smooth, out, scale, rows,
                                                                             run_flag);
     else if (cols == 3072)
         quant_rows_bf16_wide_kernel<<<(rows + kWideRowWarps - 1) / kWideRowWarps, kWideRowWarps * 32, 0, st>>>(

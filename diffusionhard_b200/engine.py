@@ -196,22 +196,22 @@ class MDLMEngine:
         call = _lib.call
         k, vt = self.kv_buffers[i]
         qkv, out, up, down = blk["qkv"], blk["out"], blk["up"], blk["down"]
-        call("dh_ln_smooth_quant", p(self.x), p(qkv.smooth), p(self.act_q), p(self.act_scale), M,
+        call("dh_ln_smooth_quant", p(self.x), p(qkv.smooth), p(qkv.inv_smooth), p(self.act_q), p(self.act_scale), M,
              None, None, rr, s)
         call("dh_gemm_qkv_rope", p(self.act_q), p(self.act_scale), p(qkv.w), p(qkv.w_scale), p(qkv.bias),
              p(self.rope_cos), p(self.rope_sin), p(out.inv_smooth), M, L, self.pos_offset, self.kv_stride, self.kv_offset,
              p(self.q), p(k), p(vt), rr, s)
         call("dh_attention", p(self.q), p(k), p(vt), p(self.attn), self.B, L, self.kv_len, self.kv_stride,
              rr, s)
-        call("dh_quant_rows_bf16", p(self.attn), None, p(self.act_q), p(self.act_scale), M,
+        call("dh_quant_rows_bf16", p(self.attn), None, None, p(self.act_q), p(self.act_scale), M,
              768, rr, s)
         call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(out.w), p(out.w_scale), p(out.bias),
              p(self.x), M, 768, 768, rr, s)
-        call("dh_ln_smooth_quant", p(self.x), p(up.smooth), p(self.act_q), p(self.act_scale), M,
+        call("dh_ln_smooth_quant", p(self.x), p(up.smooth), p(up.inv_smooth), p(self.act_q), p(self.act_scale), M,
              None, None, rr, s)
         call("dh_gemm_gelu", p(self.act_q), p(self.act_scale), p(up.w), p(up.w_scale), p(up.bias),
              p(down.inv_smooth), p(self.mlp), M, 3072, 768, rr, s)
-        call("dh_quant_rows_bf16", p(self.mlp), None, p(self.act_q), p(self.act_scale), M,
+        call("dh_quant_rows_bf16", p(self.mlp), None, None, p(self.act_q), p(self.act_scale), M,
              3072, rr, s)
         call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(down.w), p(down.w_scale),
              p(down.bias), p(self.x), M, 768, 3072, rr, s)
@@ -220,7 +220,7 @@ class MDLMEngine:
     def final_hidden_q(self, rows_index: Any = None, rows_count: Any = None):
         """Final LayerNorm + head SmoothQuant + int8 of (selected) rows."""
         s = _lib.stream_handle()
-        _lib.call("dh_ln_smooth_quant", self._p(self.x), self._p(self.head.smooth),
+        _lib.call("dh_ln_smooth_quant", self._p(self.x), self._p(self.head.smooth), self._p(self.head.inv_smooth),
                   self._p(self.head_q), self._p(self.head_scale), self.M,
                   self._p(rows_index) if rows_index is not None else None,
                   self._p(rows_count) if rows_count is not None else None, None, s)

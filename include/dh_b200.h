@@ -339,20 +339,23 @@ uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x
 /* LayerNorm (no affine, eps 1e-5) -> SmoothQuant division by smooth[768]
  * -> per-token int8 (K3): a = LN(x) / s, scale = amax(|a|) / 127 (1 for a
  * zero row), q = round_half_even(a / scale) clamped to +-127, each quotient
- * an IEEE fp32 division as in fixed_mlp._quantize_symmetric
- * (fixed_mlp.py:11-35) and quantized_linear (:82-90).  The adaLN affine is
- * folded into the following linear (model_specialization.py:10-29).
- * Optional gather: output row i reads input row rows_index[i] for
- * i < *rows_count. */
-uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, int8_t* out, float* scale,
+ * the IEEE-rounded fp32 quotient as in fixed_mlp._quantize_symmetric
+ * (fixed_mlp.py:11-35) and quantized_linear (:82-90).  inv_smooth (may be
+ * NULL) holds the fp32 reciprocals 1/s rounded to nearest: with them the
+ * division by s costs three FMAs per element instead of a full division and
+ * gives the same quotients (other values than the rounded reciprocals give
+ * quotients within an ulp).  The adaLN affine is folded into the following
+ * linear (model_specialization.py:10-29).  Optional gather: output row i
+ * reads input row rows_index[i] for i < *rows_count. */
+uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
                             const uint32_t* run_flag, void* stream);
 
 /* bf16 rows (cols = 768 or 3072) -> per-token int8 (K3'), the quantiser of
- * dh_ln_smooth_quant on fp32(in) / smooth.  smooth may be NULL when the
- * producer already applied the SmoothQuant scale (see v_scale / out_scale
- * below). */
-uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, int8_t* out, float* scale,
+ * dh_ln_smooth_quant on fp32(in) / smooth (inv_smooth as there).  smooth may
+ * be NULL when the producer already applied the SmoothQuant scale (see
+ * v_scale / out_scale below). */
+uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream);
 
 /* QKV projection (K4): [m, 768] x [2304, 768]^T, dequant, rotate-half rotary

@@ -43,22 +43,49 @@ def test_oracle_quantiser_matches_reference_golden():
     del torch
 
 
-@pytest.mark.gpu
-@pytest.mark.parametrize("name", ["bf16_768", "bf16_768_smooth", "bf16_3072", "bf16_3072_smooth", "edge_768"])
-def test_quant_rows_bit_exact(cuda, name):
-    torch = cuda
-    x, s, _, g = _cases()[name]
+def _quant_rows(torch, x, s, with_reciprocal=True):
     rows, cols = x.shape
     xin = x.to(torch.bfloat16).cuda()
     sd = None if s is None else s.cuda()
+    inv = None if s is None or not with_reciprocal else (1.0 / s).cuda()  # fp32 reciprocals, rounded
     q = torch.empty((rows, cols), dtype=torch.int8, device="cuda")
     sc = torch.empty(rows, dtype=torch.float32, device="cuda")
-    _lib.call("dh_quant_rows_bf16", _lib.ptr(xin), _lib.ptr(sd), _lib.ptr(q), _lib.ptr(sc), rows, cols, None, None)
+    _lib.call("dh_quant_rows_bf16", _lib.ptr(xin), _lib.ptr(sd), _lib.ptr(inv), _lib.ptr(q), _lib.ptr(sc), rows, cols,
+              None, None)
     torch.cuda.synchronize()
-    assert np.array_equal(q.cpu().numpy(), g["q"]), name
-    assert np.array_equal(sc.cpu().numpy(), g["scale"]), name
+    return q.cpu().numpy(), sc.cpu().numpy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["bf16_768", "bf16_768_smooth", "bf16_3072", "bf16_3072_smooth", "edge_768"])
+@pytest.mark.parametrize("with_reciprocal", [True, False])
+def test_quant_rows_bit_exact(cuda, name, with_reciprocal):
+    torch = cuda
+    x, s, _, g = _cases()[name]
+    q, sc = _quant_rows(torch, x, s, with_reciprocal)
+    assert np.array_equal(q, g["q"]), name
+    assert np.array_equal(sc, g["scale"]), name
     oq, osc = model_oracle.quantize_rows(x, None if s is None else s.numpy())
-    assert np.array_equal(q.cpu().numpy(), oq.numpy()) and np.array_equal(sc.cpu().numpy(), osc.numpy())
+    assert np.array_equal(q, oq.numpy()) and np.array_equal(sc, osc.numpy())
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cols", [768, 3072])
+def test_quant_rows_bit_exact_on_many_rows(cuda, cols):
+    """4,096 rows over 2^-20 .. 2^20 magnitudes (12.6 M quotients at 3,072
+    columns): the corrected-reciprocal division equals the CPU oracle's IEEE
+    division everywhere."""
+    torch = cuda
+    g = torch.Generator().manual_seed(cols)
+    rows = 4096
+    mag = 2.0 ** (torch.randint(-20, 21, (rows, 1), generator=g).float())
+    x = (torch.randn((rows, cols), generator=g) * mag).to(torch.bfloat16).float()
+    s = torch.rand(cols, generator=g) * 9.9 + 0.1
+    for smooth in (None, s):
+        q, sc = _quant_rows(torch, x, smooth)
+        oq, osc = model_oracle.quantize_rows(x, None if smooth is None else smooth.numpy())
+        assert np.array_equal(sc, osc.numpy())
+        assert np.array_equal(q, oq.numpy())
 
 
 @pytest.mark.gpu
@@ -66,11 +93,11 @@ def test_ln_smooth_quant_matches_reference(cuda):
     torch = cuda
     x, s, _, g = _cases()["ln_768"]
     rows = x.shape[0]
-    xd, sd = x.cuda(), s.cuda()
+    xd, sd, inv = x.cuda(), s.cuda(), (1.0 / s).cuda()
     q = torch.empty((rows, 768), dtype=torch.int8, device="cuda")
     sc = torch.empty(rows, dtype=torch.float32, device="cuda")
-    _lib.call("dh_ln_smooth_quant", _lib.ptr(xd), _lib.ptr(sd), _lib.ptr(q), _lib.ptr(sc), rows, None, None, None,
-              None)
+    _lib.call("dh_ln_smooth_quant", _lib.ptr(xd), _lib.ptr(sd), _lib.ptr(inv), _lib.ptr(q), _lib.ptr(sc), rows, None,
+              None, None, None)
     torch.cuda.synchronize()
     gq = q.cpu().numpy().astype(np.int32)
     diff = np.abs(gq - g["q"].astype(np.int32))
