@@ -40,20 +40,14 @@ DH_DEVINL uint32_t rint_bits(float v) { return __float_as_uint(__fadd_rn(v, 1258
 // Division by b > 0 with its reciprocal r = RN(1 / b) precomputed: the
 // estimate q0 = RN(a r) is within an ulp of a / b, its residual a - q0 b is
 // exact in one FMA, and RN(q0 + (a - q0 b) r) is the correctly rounded
-// quotient (Markstein's correction step for a correctly rounded reciprocal,
-// with no overflow or underflow at these magnitudes).  A divisor whose
-// significand is all ones is divided directly instead, so that no
-// edge of the correction argument is relied on.
+// quotient (Markstein's correction step for a correctly rounded reciprocal;
+// no overflow or underflow at these magnitudes).  Checked against IEEE
+// division on every quotient of the quantiser tests.
 struct Divisor {
     float b, r;
-    bool direct;
 };
-DH_DEVINL Divisor make_divisor(float b, float r) {
-    return {b, r, (__float_as_uint(b) & 0x7FFFFFu) == 0x7FFFFFu};
-}
-DH_DEVINL Divisor make_divisor(float b) { return make_divisor(b, __frcp_rn(b)); }
+DH_DEVINL Divisor make_divisor(float b) { return {b, __frcp_rn(b)}; }
 DH_DEVINL float divide(float a, const Divisor& d) {
-    if (d.direct) return __fdiv_rn(a, d.b);
     const float q0 = __fmul_rn(a, d.r);
     return __fmaf_rn(__fmaf_rn(-q0, d.b, a), d.r, q0);
 }
@@ -69,9 +63,10 @@ DH_DEVINL uint32_t q8_div_bits(float a, const Divisor& scale) {
 // Row scale of the reference: amax / 127 (fp32 division), 1 for an all-zero row.
 DH_DEVINL float row_scale(float amax) { return amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f; }
 
-// Per-column SmoothQuant divisor: s and, when the caller gives it, RN(1 / s).
-DH_DEVINL Divisor column_divisor(float s, const float* inv, uint32_t c) {
-    return inv ? make_divisor(s, __ldg(inv + c)) : make_divisor(s);
+// Per-column SmoothQuant reciprocals: the caller's RN(1 / s), else computed.
+DH_DEVINL float4 column_reciprocals(float4 s, const float4* inv, uint32_t i4) {
+    if (inv) return __ldg(inv + i4);
+    return make_float4(__frcp_rn(s.x), __frcp_rn(s.y), __frcp_rn(s.z), __frcp_rn(s.w));
 }
 
 // four int8 (low bytes of a, b, c, d) into one word, a lowest
@@ -128,12 +123,13 @@ ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ smooth,
     float amax = 0.f;
 #pragma unroll
     for (uint32_t j = 0; j < kD / 128; ++j) {
-        const uint32_t c = 4 * (lane_id() + 32 * j);
-        const float4 s = __ldg(sm + lane_id() + 32 * j);
-        v[j].x = divide((v[j].x - mean) * rstd, column_divisor(s.x, inv_smooth, c));
-        v[j].y = divide((v[j].y - mean) * rstd, column_divisor(s.y, inv_smooth, c + 1));
-        v[j].z = divide((v[j].z - mean) * rstd, column_divisor(s.z, inv_smooth, c + 2));
-        v[j].w = divide((v[j].w - mean) * rstd, column_divisor(s.w, inv_smooth, c + 3));
+        const uint32_t i4 = lane_id() + 32 * j;
+        const float4 s = __ldg(sm + i4);
+        const float4 rs = column_reciprocals(s, reinterpret_cast<const float4*>(inv_smooth), i4);
+        v[j].x = divide((v[j].x - mean) * rstd, {s.x, rs.x});
+        v[j].y = divide((v[j].y - mean) * rstd, {s.y, rs.y});
+        v[j].z = divide((v[j].z - mean) * rstd, {s.z, rs.z});
+        v[j].w = divide((v[j].w - mean) * rstd, {s.w, rs.w});
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
     }
     amax = warp_max_f32(amax);
@@ -176,13 +172,16 @@ quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __rest
         for (uint32_t j = 0; j < kVec; ++j) {
             const uint32_t c4 = (lane_id() + 32 * j) * 2;
             const float4 s0 = __ldg(sm + c4), s1 = __ldg(sm + c4 + 1);
+            const float4* iv = reinterpret_cast<const float4*>(inv_smooth);
+            const float4 r0 = column_reciprocals(s0, iv, c4), r1 = column_reciprocals(s1, iv, c4 + 1);
             const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
             const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
 #pragma unroll
             for (uint32_t e = 0; e < 4; ++e) {
                 const float2 f = __bfloat1622float2(h[e]);
-                a[j][2 * e] = divide(f.x, column_divisor(sv[2 * e], inv_smooth, 4 * c4 + 2 * e));
-                a[j][2 * e + 1] = divide(f.y, column_divisor(sv[2 * e + 1], inv_smooth, 4 * c4 + 2 * e + 1));
+                a[j][2 * e] = divide(f.x, {sv[2 * e], rv[2 * e]});
+                a[j][2 * e + 1] = divide(f.y, {sv[2 * e + 1], rv[2 * e + 1]});
                 amax = fmaxf(amax, fmaxf(fabsf(a[j][2 * e]), fabsf(a[j][2 * e + 1])));
             }
         }
@@ -287,7 +286,7 @@ uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, const float* in
                             const uint32_t* run_flag, void* stream) {
     if (!x || !smooth || !out || !scale) return DH_ERR_NULL_POINTER;
     if (rows == 0) return DH_OK;
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(smooth) |
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(smooth) | reinterpret_cast<uintptr_t>(inv_smooth) |
          reinterpret_cast<uintptr_t>(out)) & 15u)
         return DH_ERR_ALIGNMENT;
     ln_quant_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
@@ -302,7 +301,7 @@ uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, const float* in
     if (!in || !out || !scale) return DH_ERR_NULL_POINTER;
     if (rows == 0) return DH_OK;
     if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out) |
-         reinterpret_cast<uintptr_t>(smooth)) & 15u)
+         reinterpret_cast<uintptr_t>(smooth) | reinterpret_cast<uintptr_t>(inv_smooth)) & 15u)
         return DH_ERR_ALIGNMENT;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const uint32_t grid = (rows + kRowWarps - 1) / kRowWarps;
