@@ -336,8 +336,9 @@ def kernel_breakdown(eng) -> dict:
         "gemm_out_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(out.w),
                                        p(out.w_scale), p(out.bias), p(eng.x), M, 768, 768, None, s),
         "gemm_up_gelu": lambda: c("dh_gemm_gelu", p(eng.act_q), p(eng.act_scale), p(up.w), p(up.w_scale),
-                                  p(up.bias), p(down.inv_smooth), p(eng.mlp), M, 3072, 768, None, s),
-        "quant_rows_3072": lambda: c("dh_quant_rows_bf16", p(eng.mlp), None, None, p(eng.act_q),
+                                  p(up.bias), p(down.inv_smooth), p(eng.mlp), p(eng.row_amax), M, 3072, 768,
+                                  None, s),
+        "quant_rows_3072": lambda: c("dh_quant_rows_bf16_amax", p(eng.mlp), p(eng.row_amax), p(eng.act_q),
                                      p(eng.act_scale), M, 3072, None, s),
         "gemm_down_residual": lambda: c("dh_gemm_residual", p(eng.act_q), p(eng.act_scale), p(down.w),
                                         p(down.w_scale), p(down.bias), p(eng.x), M, 768, 3072, None, s),

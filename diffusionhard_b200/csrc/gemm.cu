@@ -392,9 +392,15 @@ struct EpiGelu : EpiBase {
         const float* out_scale;  // per-column factor (SmoothQuant 1/s of the next linear) or null
         __nv_bfloat16* out;
         uint32_t n;
+        // or null: per output row, the bits of max |out| over the row (as
+        // stored, bf16) are merged in with atomicMax -- the row amax the
+        // per-token quantiser of the next linear needs, so that it reads the
+        // row once; the buffer must hold 0 (the quantiser clears it again)
+        uint32_t* row_amax;
     };
     struct TileState {
         float ab;
+        __nv_bfloat162 amax2;  // running max |out| of this thread's row over the tile's chunks
     };
     static DH_DEVINL void init_smem(const Params& p, uint8_t* extra) {
         const uint32_t pieces = p.n / 4;  // 16-byte pieces per vector
@@ -412,6 +418,7 @@ struct EpiGelu : EpiBase {
     // Row scale of this tile (carried from the previous tile's prefetch), and
     // an asynchronous copy of the next tile's row scales into the carry slot.
     static DH_DEVINL bool tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t) {
+        st.amax2 = __float2bfloat162_rn(0.f);
         float* carry = carry_slot(ctx);
         if (ctx.first_tile) {
             st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
@@ -466,6 +473,11 @@ struct EpiGelu : EpiBase {
                 pk[2 * q + hh] = pack_bf16x2(g.x, g.y);
             }
         }
+        if (p.row_amax) {
+#pragma unroll
+            for (uint32_t w = 0; w < 16; ++w)
+                st.amax2 = __hmax2(st.amax2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&pk[w])));
+        }
         uint8_t* src = ctx.stage;
         if (lane == 0) tc::tma_store_wait_read<0>();  // the previous chunk's store has read `src`
         __syncwarp();
@@ -493,7 +505,12 @@ struct EpiGelu : EpiBase {
             __syncwarp();
         }
     }
-    static DH_DEVINL void tile_end(const Params&, TileState&, const EpiCtx&) {}
+    static DH_DEVINL void tile_end(const Params& p, TileState& st, const EpiCtx& ctx) {
+        // non-negative floats order like their bit patterns
+        if (p.row_amax && ctx.row_ok)
+            atomicMax(p.row_amax + ctx.row,
+                      __float_as_uint(fmaxf(__low2float(st.amax2), __high2float(st.amax2))));
+    }
     static DH_DEVINL void finish(uint32_t lane) {
         if (lane == 0) tc::tma_store_wait_all();
     }
@@ -710,7 +727,7 @@ extern "C" uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, cons
 
 extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
                                  const float* w_scale, const float* bias, const float* out_scale,
-                                 void* out, uint32_t m,
+                                 void* out, uint32_t* row_amax, uint32_t m,
                                  uint32_t n, uint32_t k, const uint32_t* run_rows, void* stream) {
     if (!a_scale || !w_scale || !bias || !out) return DH_ERR_NULL_POINTER;
     if (n % 256 != 0 || n > EpiGelu::kMaxCols) return DH_ERR_UNSUPPORTED_SHAPE;
@@ -730,6 +747,7 @@ extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const in
     p.out_scale = out_scale;
     p.out = static_cast<__nv_bfloat16*>(out);
     p.n = n;
+    p.row_amax = row_amax;
     GemmShape shape{m, n, k, run_rows};
     const uint32_t tiles = ((m + 127) / 128) * (n / 256);
     if (launch_gemm_i8<256, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=

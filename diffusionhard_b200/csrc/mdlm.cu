@@ -40,7 +40,7 @@ inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255);
 // Offsets of the workspace regions (256-byte aligned), forward first; the
 // loop adds the residual stream, the head input and the loop state.
 struct Layout {
-    size_t act_q, act_scale, q, k, vt, attn, mlp, fwd_end;
+    size_t act_q, act_scale, q, k, vt, attn, mlp, row_amax, fwd_end;
     size_t x, head_q, head_scale, packed, active, need_eval, eval_id, fwd_rows, sel_count;
     size_t sel_rows, sel_pos, sel_key, sel_eval, loop_end;
 };
@@ -62,6 +62,7 @@ Layout layout(uint32_t B, uint32_t L) {
     o.vt = take(bhl * 2);
     o.attn = take(M * kHidden * 2);
     o.mlp = take(M * kMlp * 2);
+    o.row_amax = take(M * 4);
     o.fwd_end = at;
     o.x = take(M * kHidden * 4);
     o.head_q = take(M * kHidden);
@@ -132,6 +133,7 @@ uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32
     void* vt = at<void>(ws, o.vt);
     void* attn = at<void>(ws, o.attn);
     void* mlp = at<void>(ws, o.mlp);
+    uint32_t* row_amax = at<uint32_t>(ws, o.row_amax);
     DH_TRY(dh_embed_gather(tokens, w->embedding, x, M, w->vocabulary_size, run_rows, s));
     for (uint32_t i = 0; i < w->blocks; ++i) {
         const dh_linear_weights& qkv = w->block_linears[4 * i];
@@ -146,9 +148,9 @@ uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32
         DH_TRY(dh_gemm_residual(act_q, act_scale, out.weight, out.w_scale, out.bias, x, M, kHidden, kHidden,
                                 run_rows, s));
         DH_TRY(dh_ln_smooth_quant(x, up.smooth, up.inv_smooth, act_q, act_scale, M, nullptr, nullptr, run_rows, s));
-        DH_TRY(dh_gemm_gelu(act_q, act_scale, up.weight, up.w_scale, up.bias, down.inv_smooth, mlp, M, kMlp,
-                            kHidden, run_rows, s));
-        DH_TRY(dh_quant_rows_bf16(mlp, nullptr, nullptr, act_q, act_scale, M, kMlp, run_rows, s));
+        DH_TRY(dh_gemm_gelu(act_q, act_scale, up.weight, up.w_scale, up.bias, down.inv_smooth, mlp, row_amax, M,
+                            kMlp, kHidden, run_rows, s));
+        DH_TRY(dh_quant_rows_bf16_amax(mlp, row_amax, act_q, act_scale, M, kMlp, run_rows, s));
         DH_TRY(dh_gemm_residual(act_q, act_scale, down.weight, down.w_scale, down.bias, x, M, kHidden, kMlp,
                                 run_rows, s));
     }
@@ -191,6 +193,10 @@ uint32_t dh_ddit_forward(const dh_mdlm_weights* weights, const int32_t* tokens, 
     if (!aligned16(x) || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return DH_ERR_ALIGNMENT;
     const Layout o = layout(sequences, positions);
     if (workspace_bytes < o.fwd_end) return DH_ERR_WORKSPACE;
+    // the MLP row-amax words start at 0 (each quantiser launch clears them again)
+    if (cudaMemsetAsync(at<uint8_t>(workspace, o.row_amax), 0, static_cast<size_t>(sequences) * positions * 4,
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return DH_ERR_CUDA;
     return enqueue_forward(weights, tokens, sequences, positions, x, workspace, o, run_rows, stream);
 }
 
@@ -245,6 +251,9 @@ uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids
     uint32_t* sel_key = at<uint32_t>(workspace, o.sel_key);
     uint32_t* sel_eval = at<uint32_t>(workspace, o.sel_eval);
     void* s = stream;
+    if (cudaMemsetAsync(at<uint8_t>(workspace, o.row_amax), 0, static_cast<size_t>(M) * 4,
+                        static_cast<cudaStream_t>(s)) != cudaSuccess)
+        return DH_ERR_CUDA;
     DH_TRY(dh_loop_init(input_ids, B, L, w->mask_token_id, steps, tokens, active, need_eval, eval_id, counters, s));
     for (uint32_t t = 0; t <= steps; ++t) {
         const uint32_t final_pass = t == steps ? 1u : 0u;

@@ -261,6 +261,42 @@ quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __rest
     if (lane_id() == 0) scale[r] = sc;
 }
 
+// bf16 rows whose amax the producer already merged into row_amax (bits of a
+// non-negative float, see dh_gemm_gelu): one streaming pass quantises the
+// row with scale = amax / 127, then the word is cleared for the producer's
+// next launch.  Same bytes and scales as quant_rows_bf16_wide_kernel.
+__global__ void __launch_bounds__(kRowWarps * 32)
+quant_rows_bf16_amax_kernel(const __nv_bfloat16* __restrict__ in, uint32_t* __restrict__ row_amax,
+                            int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows, uint32_t cols,
+                            const uint32_t* __restrict__ run_flag) {
+    if (run_flag && *run_flag == 0u) return;
+    const uint32_t r = blockIdx.x * kRowWarps + warp_id();
+    if (r >= rows) return;
+    const float sc = row_scale(__uint_as_float(row_amax[r]));
+    const Divisor d = make_divisor(sc);
+    const uint32_t nvec = cols / 8;
+    const uint4* src = reinterpret_cast<const uint4*>(in + static_cast<uint64_t>(r) * cols);
+    uint2* dst = reinterpret_cast<uint2*>(out + static_cast<uint64_t>(r) * cols);
+#pragma unroll 4
+    for (uint32_t j = lane_id(); j < nvec; j += 32) {
+        const uint4 raw = __ldcs(src + j);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        uint32_t packed[2];
+#pragma unroll
+        for (uint32_t e = 0; e < 4; e += 2) {
+            const float2 f0 = __bfloat1622float2(h[e]), f1 = __bfloat1622float2(h[e + 1]);
+            packed[e >> 1] = pack4_i8(q8_div_bits(f0.x, d), q8_div_bits(f0.y, d), q8_div_bits(f1.x, d),
+                                      q8_div_bits(f1.y, d));
+        }
+        dst[j] = make_uint2(packed[0], packed[1]);
+    }
+    __syncwarp();
+    if (lane_id() == 0) {
+        scale[r] = sc;
+        row_amax[r] = 0u;
+    }
+}
+
 }  // namespace
 }  // namespace dh
 
@@ -320,6 +356,19 @@ uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, const float* in
             src, out, scale, rows, cols, run_flag);
     else
         return DH_ERR_UNSUPPORTED_SHAPE;
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+uint32_t dh_quant_rows_bf16_amax(const void* in, uint32_t* row_amax, int8_t* out, float* scale, uint32_t rows,
+                                 uint32_t cols, const uint32_t* run_flag, void* stream) {
+    if (!in || !row_amax || !out || !scale) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if (cols == 0 || cols % 256 != 0) return DH_ERR_UNSUPPORTED_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u) return DH_ERR_ALIGNMENT;
+    quant_rows_bf16_amax_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(static_cast<const __nv_bfloat16*>(in),
+                                                                       row_amax, out, scale, rows, cols, run_flag);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }

@@ -114,6 +114,7 @@ class MDLMEngine:
             raise ValueError("K / V buffers too short")
         self.attn = torch.empty((M, 768), dtype=bf16, device=d)
         self.mlp = torch.empty((M, 3072), dtype=bf16, device=d)
+        self.row_amax = torch.zeros(M, dtype=torch.int32, device=d)  # MLP-up row amax (cleared by its quantiser)
         # head input (gathered rows) and loop state
         self.head_q = torch.empty((M, 768), dtype=torch.int8, device=d)
         self.head_scale = torch.empty(M, dtype=torch.float32, device=d)
@@ -210,8 +211,8 @@ class MDLMEngine:
         call("dh_ln_smooth_quant", p(self.x), p(up.smooth), p(up.inv_smooth), p(self.act_q), p(self.act_scale), M,
              None, None, rr, s)
         call("dh_gemm_gelu", p(self.act_q), p(self.act_scale), p(up.w), p(up.w_scale), p(up.bias),
-             p(down.inv_smooth), p(self.mlp), M, 3072, 768, rr, s)
-        call("dh_quant_rows_bf16", p(self.mlp), None, None, p(self.act_q), p(self.act_scale), M,
+             p(down.inv_smooth), p(self.mlp), p(self.row_amax), M, 3072, 768, rr, s)
+        call("dh_quant_rows_bf16_amax", p(self.mlp), p(self.row_amax), p(self.act_q), p(self.act_scale), M,
              3072, rr, s)
         call("dh_gemm_residual", p(self.act_q), p(self.act_scale), p(down.w), p(down.w_scale),
              p(down.bias), p(self.x), M, 768, 3072, rr, s)

@@ -380,13 +380,23 @@ uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, const int8_t* w
                           uint32_t k, const uint32_t* run_rows, void* stream);
 
 /* out[m, n] = bf16(gelu_tanh(dequant(A . W^T) + bias) * out_scale[n]): MLP-up
- * (K7); out_scale (may be NULL) is the SmoothQuant 1/s of MLP-down.  n is a
- * multiple of 256 and at most 3584 (the column parameters stay in shared
- * memory); DH_ERR_UNSUPPORTED_SHAPE otherwise. */
+ * (K7); out_scale (may be NULL) is the SmoothQuant 1/s of MLP-down.
+ * row_amax (device uint32 [m], may be NULL; must hold 0 on entry): the bits
+ * of each row's max |out| (non-negative fp32, so atomicMax on the bits orders
+ * them) for dh_quant_rows_bf16_amax.  n is a multiple of 256 and at most
+ * 3584 (the column parameters stay in shared memory);
+ * DH_ERR_UNSUPPORTED_SHAPE otherwise. */
 uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const int8_t* w,
                       const float* w_scale, const float* bias, const float* out_scale, void* out,
-                      uint32_t m, uint32_t n,
+                      uint32_t* row_amax, uint32_t m, uint32_t n,
                       uint32_t k, const uint32_t* run_rows, void* stream);
+
+/* The per-token quantiser of dh_quant_rows_bf16 (no smoothing) for bf16 rows
+ * whose max |x| the producer already left in row_amax (dh_gemm_gelu): one
+ * streaming pass instead of two, the same bytes and scales; row_amax[r] is
+ * reset to 0 afterwards.  cols a multiple of 256. */
+uint32_t dh_quant_rows_bf16_amax(const void* in, uint32_t* row_amax, int8_t* out, float* scale, uint32_t rows,
+                                 uint32_t cols, const uint32_t* run_flag, void* stream);
 
 /* Bidirectional attention softmax(Q K^T / 8) V (K5) over the first kv_len
  * keys of K / V^T buffers of kv_stride rows per (sequence, head); Q, K bf16,

@@ -104,3 +104,38 @@ def test_ln_smooth_quant_matches_reference(cuda):
     assert diff.max() <= 1
     assert (diff == 0).mean() >= 0.998
     assert np.allclose(sc.cpu().numpy(), g["scale"], rtol=4e-6, atol=0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m", [4096, 1000])
+def test_gelu_row_amax_and_single_pass_quantiser(cuda, m):
+    """dh_gemm_gelu merges each row's max |out| into row_amax (the bits of
+    the max over the stored bf16 values); dh_quant_rows_bf16_amax then gives
+    the same bytes and scales as the two-pass dh_quant_rows_bf16 and clears
+    the words for the next launch.  m = 4,096 gives every persistent CTA
+    several tiles; 1,000 ends in a ragged tile."""
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(m)
+    n, k = 3072, 768
+    a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda", generator=g)
+    w = torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+    a_scale = torch.rand(m, device="cuda", generator=g) * 1e-3 + 1e-4
+    w_scale = torch.rand(n, device="cuda", generator=g) * 1e-3 + 1e-4
+    bias = torch.randn(n, device="cuda", generator=g) * 0.1
+    out_scale = torch.rand(n, device="cuda", generator=g) + 0.5
+    mlp = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    amax = torch.zeros(m, dtype=torch.int32, device="cuda")
+    _lib.call("dh_gemm_gelu", _lib.ptr(a), _lib.ptr(a_scale), _lib.ptr(w), _lib.ptr(w_scale), _lib.ptr(bias),
+              _lib.ptr(out_scale), _lib.ptr(mlp), _lib.ptr(amax), m, n, k, None, None)
+    torch.cuda.synchronize()
+    expect = mlp.float().abs().amax(dim=1)
+    assert torch.equal(amax.view(torch.float32), expect)
+    q1 = torch.empty((m, n), dtype=torch.int8, device="cuda")
+    s1 = torch.empty(m, dtype=torch.float32, device="cuda")
+    q2, s2 = torch.empty_like(q1), torch.empty_like(s1)
+    _lib.call("dh_quant_rows_bf16", _lib.ptr(mlp), None, None, _lib.ptr(q1), _lib.ptr(s1), m, n, None, None)
+    _lib.call("dh_quant_rows_bf16_amax", _lib.ptr(mlp), _lib.ptr(amax), _lib.ptr(q2), _lib.ptr(s2), m, n, None,
+              None)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2) and torch.equal(s1, s2)
+    assert int(amax.abs().sum()) == 0
