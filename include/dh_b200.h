@@ -409,6 +409,29 @@ uint32_t dh_attention(const void* q, const void* k, const void* vt, void* out, u
                       uint32_t q_len, uint32_t kv_len, uint32_t kv_stride, const uint32_t* run_flag,
                       void* stream);
 
+/* ---------------------------- final layer with per-sequence conditioning */
+
+/* adaLN modulation of the final layer (mlx_mdlm._FinalLayer.prepare,
+ * mlx_mdlm.py:466-471): out[b, n] = bias[n] + sum_c cond[b, c] weight[n, c]
+ * (fp32, c summed in order); with outputs = 2 d the first d are the shift,
+ * the next d the scale.  bias may be NULL. */
+uint32_t dh_adaln_modulation(const float* cond, const float* weight, const float* bias, float* out,
+                             uint32_t sequences, uint32_t condition_size, uint32_t outputs, void* stream);
+
+/* The head's input when the conditioning varies per sequence
+ * (mlx_mdlm._FinalLayer.hidden, mlx_mdlm.py:487-493, then the per-token
+ * int8 of fixed_mlp._quantize_symmetric, fixed_mlp.py:11-35): for output row
+ * i < min(rows, *rows_count) the hidden row r = rows_index[i] (bf16 [*, 768];
+ * identity when rows_index is NULL) of sequence b = r / rows_per_sequence is
+ * LayerNorm-ed (eps 1e-5, times ln_weight, NULL = ones), modulated
+ * h = n (1 + scale_b) + shift_b with modulation[b] = [shift | scale] (fp32
+ * [sequences, 1536], dh_adaln_modulation), and quantised per token: out[i]
+ * int8 [768] and scale[i] = amax / 127. */
+uint32_t dh_ln_modulate_quant_bf16(const void* hidden, const float* ln_weight, const float* modulation,
+                                   uint32_t rows_per_sequence, const uint32_t* rows_index,
+                                   const uint32_t* rows_count, uint32_t rows, int8_t* out, float* scale,
+                                   void* stream);
+
 /* ------------------------------------------------ fused int8 head (K9) */
 
 /* Head + noisy argmax over `rows` int8 hidden rows (ld_hidden bytes apart)

@@ -154,3 +154,32 @@ def logits(qm, h):
     """Head logits from the final hidden (reference W8A8 output, fp32)."""
     B, L, d = h.shape
     return w8a8_linear(h.reshape(B * L, d), qm.head).view(B, L, -1)
+
+
+def final_layer_candidates(hidden, cond, ada_weight, ada_bias, ln_weight, head_weight_q, head_w_scale, head_bias,
+                           masked, mask_id: int, seed: int):
+    """Candidates of the masked positions of a [B, L] canvas when the
+    conditioning varies per sequence: mlx_mdlm._FinalLayer (mlx_mdlm.py:
+    456-498) unfolded -- [shift | scale] = adaLN(cond), h = LayerNorm(x)
+    (eps 1e-5, weight) * (1 + scale_b) + shift_b -- then the per-token int8 of
+    fixed_mlp._quantize_symmetric and the int8 head's noisy argmax
+    (pyoracle.head_i8 mode 1, Philox counter (v/4, p, 0, 0), key (seed, b)).
+    hidden: fp32 [B, L, 768]; returns (rows b * L + p in position-major
+    order, ids, int8 rows, row scales)."""
+    import torch
+    import torch.nn.functional as F
+
+    from oracle import pyoracle
+
+    B, L, d = hidden.shape
+    mod = torch.nn.functional.linear(cond, ada_weight, ada_bias)
+    shift, scale = mod.chunk(2, dim=-1)
+    n = F.layer_norm(hidden, [d], ln_weight)
+    h = n * (1 + scale[:, None]) + shift[:, None]
+    rows = np.nonzero(np.asarray(masked).reshape(-1))[0]
+    q, s = quantize_rows(h.reshape(B * L, d)[torch.from_numpy(rows)])
+    qn, sn = q.numpy(), s.numpy()
+    ids, _ = pyoracle.head_i8(1, qn, head_weight_q, mask_id, a_scale=sn, w_scale=head_w_scale, bias=head_bias,
+                              row_position=rows % L, row_key_hi=rows // L, row_eval=np.zeros(rows.size),
+                              key_lo=seed)
+    return rows, ids, qn, sn
