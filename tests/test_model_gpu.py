@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from diffusionhard_b200 import _lib
-from diffusionhard_b200.engine import MDLMEngine
+from diffusionhard_b200.engine import MDLMEngine, to_vt_order
 from diffusionhard_b200.model import MDLMConfig, build_quantized
 from diffusionhard_b200.sampler import reveal_thresholds_q32
 from oracle import model_oracle, pyoracle
@@ -177,9 +177,10 @@ def test_attention_matches_sdpa(cuda):
     k = torch.randn((B, H, kv_stride, 64), device="cuda", generator=g).to(torch.bfloat16)
     vt = torch.randn((B, H, 64, kv_stride), device="cuda", generator=g).to(torch.float16)
     k[:, :, :P] *= 3  # a prefix with larger scores exercises the rescale path
+    vt_dev = to_vt_order(vt)  # the key order the kernel reads
     for kv_len in (Lq, kv_stride):
         out = torch.empty((B * Lq, 768), dtype=torch.bfloat16, device="cuda")
-        _lib.call("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt), _lib.ptr(out), B, Lq, kv_len,
+        _lib.call("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt_dev), _lib.ptr(out), B, Lq, kv_len,
                   kv_stride, None, None)
         torch.cuda.synchronize()
         ref = F.scaled_dot_product_attention(q.float(), k[:, :, :kv_len].float(),
@@ -209,7 +210,8 @@ def test_attention_ragged_lengths(cuda, Lq, P):
     guard = 4096
     buf = torch.full((B * Lq * 768 + guard,), 7.0, dtype=torch.bfloat16, device="cuda")
     out = buf[: B * Lq * 768].view(B * Lq, 768)
-    _lib.call("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt), _lib.ptr(out), B, Lq, kv_len,
+    vt_dev = to_vt_order(vt)  # the key order the kernel reads
+    _lib.call("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt_dev), _lib.ptr(out), B, Lq, kv_len,
               kv_stride, None, None)
     torch.cuda.synchronize()
     ref = F.scaled_dot_product_attention(q.float(), k[:, :, :kv_len].float(),
@@ -218,7 +220,7 @@ def test_attention_ragged_lengths(cuda, Lq, P):
     assert ((got - ref).norm() / ref.norm()).item() < 1e-2
     assert bool((buf[B * Lq * 768:] == 7.0).all())
     assert _device_error() == 0
-    assert _lib.raw("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt), _lib.ptr(out), B, 48, kv_len,
+    assert _lib.raw("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt_dev), _lib.ptr(out), B, 48, kv_len,
                     kv_stride, None, None) == 103
 
 
