@@ -158,7 +158,10 @@ DH_DEVINL Item item_of(uint32_t w, uint32_t n_qt) {
 __global__ void __launch_bounds__(kThreads, 2)
 attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const AttnArgs args) {
-    if (args.run_flag && *args.run_flag == 0u) return;
+    // sequences processed: all, or those of the first *run_flag query rows
+    const uint32_t live_seqs =
+        args.run_flag ? min(args.sequences, *args.run_flag / args.q_len) : args.sequences;
+    if (live_seqs == 0) return;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -173,7 +176,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
     const uint32_t n_qt = (args.q_len + kQTile - 1) / kQTile;
     // keys of the last tile that exist (kKT when kv_len is a multiple of it)
     const uint32_t kv_rem = args.kv_len - (n_kv - 1) * kKT;
-    const uint32_t total = args.sequences * kHeads * n_qt;
+    const uint32_t total = live_seqs * kHeads * n_qt;
 
     if (warp == 0 && lane == 0) {
         for (uint32_t i = 0; i < kNumBars; ++i) {

@@ -24,42 +24,72 @@
 namespace dh {
 namespace {
 
-// Single CTA: B sequences x W bitmap words.
+// Single CTA: B sequences x W bitmap words.  A sequence refills when it has
+// masked positions and its canvas changed at the previous transition (every
+// sequence with masked positions on the final pass).  Without a sequence
+// list the forward covers the whole batch whenever one sequence refills
+// (fwd_rows = B * L or 0); with one, seq_list[0 .. n) receives the refilling
+// sequences in ascending order and fwd_rows = n * L, so the forward runs
+// over those sequences only, packed together.
 __global__ void __launch_bounds__(1024)
 loop_plan_kernel(uint32_t B, uint32_t L, uint32_t step, uint32_t final_pass,
                  const uint64_t* __restrict__ active, uint32_t* __restrict__ need_eval,
                  uint32_t* __restrict__ eval_id, uint32_t* __restrict__ fwd_rows,
-                 uint32_t* __restrict__ sel_count, int32_t* __restrict__ counters) {
-    __shared__ uint32_t any_refill, total_active;
+                 uint32_t* __restrict__ sel_count, int32_t* __restrict__ counters,
+                 uint32_t* __restrict__ seq_list) {
+    __shared__ uint32_t any_refill, total_active, listed;
+    __shared__ uint32_t warp_base[32];
     if (threadIdx.x == 0) {
         any_refill = 0;
         total_active = 0;
+        listed = 0;
         *sel_count = 0;
     }
     __syncthreads();
     const uint32_t W = (L + 63) / 64;
-    for (uint32_t b = warp_id(); b < B; b += blockDim.x / 32) {
-        uint32_t cnt = 0;
-        for (uint32_t w = lane_id(); w < W; w += 32) cnt += __popcll(active[static_cast<uint64_t>(b) * W + w]);
+    const uint32_t warps = blockDim.x / 32;
+    // rounds of `warps` sequences: warp i takes sequence round * warps + i,
+    // so the list stays in ascending order
+    for (uint32_t base = 0; base < B; base += warps) {
+        const uint32_t b = base + warp_id();
+        uint32_t refill = 0;
+        if (b < B) {
+            uint32_t cnt = 0;
+            for (uint32_t w = lane_id(); w < W; w += 32) cnt += __popcll(active[static_cast<uint64_t>(b) * W + w]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
-        if (lane_id() == 0) {
-            if (cnt) atomicAdd(&total_active, cnt);
-            if (final_pass) {
-                if (cnt) any_refill = 1;
-            } else {
-                const uint32_t refill = (cnt > 0 && need_eval[b]) ? 1u : 0u;
+            for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xFFFFFFFFu, cnt, o);
+            refill = (cnt > 0 && (final_pass || need_eval[b])) ? 1u : 0u;
+            if (lane_id() == 0) {
+                if (cnt) atomicAdd(&total_active, cnt);
                 if (refill) {
-                    eval_id[b] = step;
-                    need_eval[b] = 0;
                     any_refill = 1;
+                    if (!final_pass) {
+                        eval_id[b] = step;
+                        need_eval[b] = 0;
+                    }
                 }
             }
+        }
+        if (seq_list) {
+            if (lane_id() == 0) warp_base[warp_id()] = refill;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                uint32_t run = listed;
+                for (uint32_t i = 0; i < warps; ++i) {
+                    const uint32_t f = warp_base[i];
+                    warp_base[i] = run;
+                    run += f;
+                }
+                listed = run;
+            }
+            __syncthreads();
+            if (refill && lane_id() == 0) seq_list[warp_base[warp_id()]] = b;
+            __syncthreads();
         }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        *fwd_rows = any_refill ? B * L : 0u;
+        *fwd_rows = seq_list ? listed * L : (any_refill ? B * L : 0u);
         if (!final_pass) {
             counters[3 * step] = static_cast<int32_t>(total_active);
             counters[3 * step + 2] = static_cast<int32_t>(any_refill);
@@ -210,13 +240,22 @@ uint32_t dh_loop_plan(uint32_t sequences, uint32_t positions, uint32_t step, uin
                       uint32_t final_pass, const uint64_t* active, uint32_t* need_eval,
                       uint32_t* eval_id, uint32_t* fwd_rows, uint32_t* sel_count,
                       int32_t* counters, void* stream) {
+    return dh_loop_plan_seqs(sequences, positions, step, steps, final_pass, active, need_eval, eval_id, fwd_rows,
+                             sel_count, counters, nullptr, stream);
+}
+
+uint32_t dh_loop_plan_seqs(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t steps,
+                           uint32_t final_pass, const uint64_t* active, uint32_t* need_eval,
+                           uint32_t* eval_id, uint32_t* fwd_rows, uint32_t* sel_count,
+                           int32_t* counters, uint32_t* seq_list, void* stream) {
     if (!active || !need_eval || !eval_id || !fwd_rows || !sel_count || !counters)
         return DH_ERR_NULL_POINTER;
     if (sequences == 0 || positions == 0 || (!final_pass && step >= steps))
         return DH_ERR_INVALID_ARGUMENT;
+    if (static_cast<uint64_t>(sequences) * positions > 0xFFFFFFFFull) return DH_ERR_UNSUPPORTED_SHAPE;
     loop_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
         sequences, positions, step, final_pass, active, need_eval, eval_id, fwd_rows, sel_count,
-        counters);
+        counters, seq_list);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }

@@ -42,7 +42,7 @@ inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255);
 struct Layout {
     size_t act_q, act_scale, q, k, vt, attn, mlp, row_amax, fwd_end;
     size_t x, head_q, head_scale, packed, active, need_eval, eval_id, fwd_rows, sel_count;
-    size_t sel_rows, sel_pos, sel_key, sel_eval, loop_end;
+    size_t sel_rows, sel_pos, sel_key, sel_eval, seq_list, head_all, head_all_scale, loop_end;
 };
 
 Layout layout(uint32_t B, uint32_t L) {
@@ -77,6 +77,9 @@ Layout layout(uint32_t B, uint32_t L) {
     o.sel_pos = take(M * 4);
     o.sel_key = take(M * 4);
     o.sel_eval = take(M * 4);
+    o.seq_list = take(static_cast<size_t>(B) * 4);
+    o.head_all = take(M * kHidden);
+    o.head_all_scale = take(M * 4);
     o.loop_end = at;
     return o;
 }
@@ -122,9 +125,12 @@ T* at(void* base, size_t off) {
 }
 
 // The forward over B x L rows of `tokens`, residual stream into x.  run_rows:
-// device word, every launch returns at once when it holds 0.
+// device word, the launches process only its first *run_rows rows (0: none).
+// seq_list (device, may be NULL): the rows are the packed positions of the
+// listed sequences of `tokens` (the sequences that need a forward).
 uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32_t B, uint32_t L, float* x,
-                         void* ws, const Layout& o, const uint32_t* run_rows, void* s) {
+                         void* ws, const Layout& o, const uint32_t* run_rows, void* s,
+                         const uint32_t* seq_list = nullptr) {
     const uint32_t M = B * L;
     int8_t* act_q = at<int8_t>(ws, o.act_q);
     float* act_scale = at<float>(ws, o.act_scale);
@@ -134,7 +140,10 @@ uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32
     void* attn = at<void>(ws, o.attn);
     void* mlp = at<void>(ws, o.mlp);
     uint32_t* row_amax = at<uint32_t>(ws, o.row_amax);
-    DH_TRY(dh_embed_gather(tokens, w->embedding, x, M, w->vocabulary_size, run_rows, s));
+    if (seq_list)
+        DH_TRY(dh_embed_gather_seqs(tokens, seq_list, L, w->embedding, x, M, w->vocabulary_size, run_rows, s));
+    else
+        DH_TRY(dh_embed_gather(tokens, w->embedding, x, M, w->vocabulary_size, run_rows, s));
     for (uint32_t i = 0; i < w->blocks; ++i) {
         const dh_linear_weights& qkv = w->block_linears[4 * i];
         const dh_linear_weights& out = w->block_linears[4 * i + 1];
@@ -219,7 +228,7 @@ size_t dh_sample_loop_workspace_size(uint32_t sequences, uint32_t positions) {
 
 uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids, int32_t* tokens,
                         uint32_t sequences, uint32_t positions, uint32_t steps, const uint64_t* thresholds_q32,
-                        uint32_t seed, uint32_t seq_offset, int32_t* counters, void* nccl_comm,
+                        uint32_t seed, uint32_t seq_offset, int32_t* counters, void* nccl_comm, uint32_t compact,
                         void* workspace, size_t workspace_bytes, void* stream) {
     DH_TRY(check_model(weights, sequences, positions));
     const dh_mdlm_weights* w = weights;
@@ -250,6 +259,9 @@ uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids
     uint32_t* sel_pos = at<uint32_t>(workspace, o.sel_pos);
     uint32_t* sel_key = at<uint32_t>(workspace, o.sel_key);
     uint32_t* sel_eval = at<uint32_t>(workspace, o.sel_eval);
+    uint32_t* seq_list = compact ? at<uint32_t>(workspace, o.seq_list) : nullptr;
+    int8_t* head_all = at<int8_t>(workspace, o.head_all);
+    float* head_all_scale = at<float>(workspace, o.head_all_scale);
     void* s = stream;
     if (cudaMemsetAsync(at<uint8_t>(workspace, o.row_amax), 0, static_cast<size_t>(M) * 4,
                         static_cast<cudaStream_t>(s)) != cudaSuccess)
@@ -258,11 +270,19 @@ uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids
     for (uint32_t t = 0; t <= steps; ++t) {
         const uint32_t final_pass = t == steps ? 1u : 0u;
         const uint32_t k = final_pass ? steps - 1 : t;
-        DH_TRY(dh_loop_plan(B, L, k, steps, final_pass, active, need_eval, eval_id, fwd_rows, sel_count, counters, s));
-        DH_TRY(enqueue_forward(w, tokens, B, L, x, workspace, o, fwd_rows, s));
+        DH_TRY(dh_loop_plan_seqs(B, L, k, steps, final_pass, active, need_eval, eval_id, fwd_rows, sel_count,
+                                 counters, seq_list, s));
+        DH_TRY(enqueue_forward(w, tokens, B, L, x, workspace, o, fwd_rows, s, seq_list));
+        if (seq_list)  // every refilled row's head input, kept per sequence until its next forward
+            DH_TRY(dh_ln_smooth_quant_scatter(x, w->head.smooth, w->head.inv_smooth, head_all, head_all_scale, M,
+                                              seq_list, L, fwd_rows, s));
         DH_TRY(dh_loop_select(B, L, k, seed, seq_offset, 0, final_pass ? 0 : thresholds_q32[t], final_pass, active,
                               eval_id, sel_rows, sel_pos, sel_key, sel_eval, sel_count, s));
-        DH_TRY(dh_ln_smooth_quant(x, w->head.smooth, w->head.inv_smooth, head_q, head_scale, M, sel_rows, sel_count, nullptr, s));
+        if (seq_list)
+            DH_TRY(dh_gather_rows_i8(head_all, head_all_scale, sel_rows, sel_count, M, head_q, head_scale, s));
+        else
+            DH_TRY(dh_ln_smooth_quant(x, w->head.smooth, w->head.inv_smooth, head_q, head_scale, M, sel_rows,
+                                      sel_count, nullptr, s));
         DH_TRY(dh_head_argmax_i8(head_q, kHidden, w->head.weight, kHidden, M, sel_count, kHidden, w->head_rows,
                                  w->head_vocab_offset, w->mask_token_id, final_pass ? 2u : 1u, head_scale,
                                  w->head.w_scale, w->head.bias, nullptr, nullptr, nullptr, sel_pos, sel_key, sel_eval,

@@ -75,14 +75,25 @@ DH_DEVINL uint32_t pack4_i8(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
 }
 
 
+// Rows processed by a launch: all `rows`, or the first *run_rows of them
+// when the caller gives that device word (0 = none: a captured graph skips
+// the work of a transition that needs no forward).
+DH_DEVINL uint32_t live_rows(uint32_t rows, const uint32_t* run_rows) {
+    return run_rows ? min(rows, *run_rows) : rows;
+}
+
+// x[r] = embedding[tokens[src(r)]]: src(r) = r, or, with a sequence list,
+// the position r % positions of sequence seq_list[r / positions] (the
+// forward over the sequences that need one, packed together).
 __global__ void __launch_bounds__(kRowWarps * 32)
 embed_gather_kernel(const int32_t* __restrict__ tokens, const float* __restrict__ embed,
                     float* __restrict__ x, uint32_t rows, uint32_t vocab,
-                    const uint32_t* __restrict__ run_flag) {
-    if (run_flag && *run_flag == 0u) return;
+                    const uint32_t* __restrict__ run_flag, const uint32_t* __restrict__ seq_list,
+                    uint32_t positions) {
     const uint32_t r = blockIdx.x * kRowWarps + warp_id();
-    if (r >= rows) return;
-    uint32_t t = static_cast<uint32_t>(tokens[r]);
+    if (r >= live_rows(rows, run_flag)) return;
+    const uint32_t tr = seq_list ? seq_list[r / positions] * positions + r % positions : r;
+    uint32_t t = static_cast<uint32_t>(tokens[tr]);
     if (t >= vocab) t = vocab - 1;
     const float4* src = reinterpret_cast<const float4*>(embed + static_cast<uint64_t>(t) * kD);
     float4* dst = reinterpret_cast<float4*>(x + static_cast<uint64_t>(r) * kD);
@@ -96,12 +107,15 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ smooth,
                 const float* __restrict__ inv_smooth, int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
                 const uint32_t* __restrict__ rows_index, const uint32_t* __restrict__ rows_count,
-                const uint32_t* __restrict__ run_flag) {
-    if (run_flag && *run_flag == 0u) return;
+                const uint32_t* __restrict__ run_flag, const uint32_t* __restrict__ seq_list,
+                uint32_t positions) {
     const uint32_t i = blockIdx.x * kRowWarps + warp_id();
-    const uint32_t n = rows_count ? min(rows, *rows_count) : rows;
+    uint32_t n = live_rows(rows, run_flag);
+    if (rows_count) n = min(n, *rows_count);
     if (i >= n) return;
     const uint32_t r = rows_index ? rows_index[i] : i;
+    // output row: i, or scattered to the sequence's own rows
+    const uint32_t o = seq_list ? seq_list[i / positions] * positions + i % positions : i;
     const float4* src = reinterpret_cast<const float4*>(x + static_cast<uint64_t>(r) * kD);
     float4 v[kD / 128];
     float sum = 0.f;
@@ -135,12 +149,12 @@ ln_quant_kernel(const float* __restrict__ x, const float* __restrict__ smooth,
     amax = warp_max_f32(amax);
     const float sc = row_scale(amax);
     const Divisor dsc = make_divisor(sc);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(out + static_cast<uint64_t>(i) * kD);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(out + static_cast<uint64_t>(o) * kD);
 #pragma unroll
     for (uint32_t j = 0; j < kD / 128; ++j)
         dst[lane_id() + 32 * j] = pack4_i8(q8_div_bits(v[j].x, dsc), q8_div_bits(v[j].y, dsc),
                                            q8_div_bits(v[j].z, dsc), q8_div_bits(v[j].w, dsc));
-    if (lane_id() == 0) scale[i] = sc;
+    if (lane_id() == 0) scale[o] = sc;
 }
 
 // bf16 rows of C = 768 or 3072 columns -> per-token int8 + row scale.  The
@@ -155,9 +169,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 quant_rows_bf16_kernel(const __nv_bfloat16* __restrict__ in, const float* __restrict__ smooth,
                        const float* __restrict__ inv_smooth, int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows,
                        const uint32_t* __restrict__ run_flag) {
-    if (run_flag && *run_flag == 0u) return;
     const uint32_t r = blockIdx.x * kRowWarps + warp_id();
-    if (r >= rows) return;
+    if (r >= live_rows(rows, run_flag)) return;
     constexpr uint32_t kVec = C / 256;  // 8-element (16-byte) vectors per lane
     const uint4* src = reinterpret_cast<const uint4*>(in + static_cast<uint64_t>(r) * C);
     uint4 raw[kVec];
@@ -229,9 +242,8 @@ __global__ void __launch_bounds__(kWideRowWarps * 32)
 quant_rows_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, int8_t* __restrict__ out,
                             float* __restrict__ scale, uint32_t rows, uint32_t cols,
                             const uint32_t* __restrict__ run_flag) {
-    if (run_flag && *run_flag == 0u) return;
     const uint32_t r = blockIdx.x * kWideRowWarps + warp_id();
-    if (r >= rows) return;
+    if (r >= live_rows(rows, run_flag)) return;
     const uint32_t nvec = cols / 8;
     const uint4* src = reinterpret_cast<const uint4*>(in + static_cast<uint64_t>(r) * cols);
     __nv_bfloat162 m2 = __float2bfloat162_rn(0.f);
@@ -269,9 +281,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 quant_rows_bf16_amax_kernel(const __nv_bfloat16* __restrict__ in, uint32_t* __restrict__ row_amax,
                             int8_t* __restrict__ out, float* __restrict__ scale, uint32_t rows, uint32_t cols,
                             const uint32_t* __restrict__ run_flag) {
-    if (run_flag && *run_flag == 0u) return;
     const uint32_t r = blockIdx.x * kRowWarps + warp_id();
-    if (r >= rows) return;
+    if (r >= live_rows(rows, run_flag)) return;
     const float sc = row_scale(__uint_as_float(row_amax[r]));
     const Divisor d = make_divisor(sc);
     const uint32_t nvec = cols / 8;
@@ -312,7 +323,22 @@ uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x
         return DH_ERR_ALIGNMENT;
     embed_gather_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
                           static_cast<cudaStream_t>(stream)>>>(tokens, embedding, x, rows,
-                                                               vocabulary_size, run_flag);
+                                                               vocabulary_size, run_flag, nullptr, 1);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+uint32_t dh_embed_gather_seqs(const int32_t* tokens, const uint32_t* seq_list, uint32_t positions,
+                              const float* embedding, float* x, uint32_t rows, uint32_t vocabulary_size,
+                              const uint32_t* run_rows, void* stream) {
+    if (!tokens || !seq_list || !embedding || !x) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if (positions == 0) return DH_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(embedding) | reinterpret_cast<uintptr_t>(x)) & 15u)
+        return DH_ERR_ALIGNMENT;
+    embed_gather_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
+                          static_cast<cudaStream_t>(stream)>>>(tokens, embedding, x, rows, vocabulary_size,
+                                                               run_rows, seq_list, positions);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }
@@ -327,7 +353,48 @@ uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, const float* in
         return DH_ERR_ALIGNMENT;
     ln_quant_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
                       static_cast<cudaStream_t>(stream)>>>(x, smooth, inv_smooth, out, scale, rows,
-                                                           rows_index, rows_count, run_flag);
+                                                           rows_index, rows_count, run_flag, nullptr, 1);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+uint32_t dh_ln_smooth_quant_scatter(const float* x, const float* smooth, const float* inv_smooth, int8_t* out,
+                                    float* scale, uint32_t rows, const uint32_t* seq_list, uint32_t positions,
+                                    const uint32_t* run_rows, void* stream) {
+    if (!x || !smooth || !out || !scale || !seq_list) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if (positions == 0) return DH_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(smooth) | reinterpret_cast<uintptr_t>(inv_smooth) |
+         reinterpret_cast<uintptr_t>(out)) & 15u)
+        return DH_ERR_ALIGNMENT;
+    ln_quant_kernel<<<(rows + kRowWarps - 1) / kRowWarps, kRowWarps * 32, 0,
+                      static_cast<cudaStream_t>(stream)>>>(x, smooth, inv_smooth, out, scale, rows, nullptr,
+                                                           nullptr, run_rows, seq_list, positions);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
+// dst row i = src row rows_index[i] (768 int8 + its fp32 scale), i < *rows_count.
+__global__ void gather_rows_i8_kernel(const int8_t* __restrict__ src, const float* __restrict__ src_scale,
+                                      const uint32_t* __restrict__ rows_index, const uint32_t* __restrict__ rows_count,
+                                      uint32_t rows, int8_t* __restrict__ dst, float* __restrict__ dst_scale) {
+    const uint32_t i = blockIdx.x * (blockDim.x / 32) + warp_id();
+    if (i >= min(rows, *rows_count)) return;
+    const uint32_t r = rows_index[i];
+    const uint2* s = reinterpret_cast<const uint2*>(src + static_cast<uint64_t>(r) * kD);
+    uint2* d = reinterpret_cast<uint2*>(dst + static_cast<uint64_t>(i) * kD);
+#pragma unroll
+    for (uint32_t j = 0; j < kD / 256; ++j) d[lane_id() + 32 * j] = s[lane_id() + 32 * j];
+    if (lane_id() == 0) dst_scale[i] = src_scale[r];
+}
+
+uint32_t dh_gather_rows_i8(const int8_t* src, const float* src_scale, const uint32_t* rows_index,
+                           const uint32_t* rows_count, uint32_t rows, int8_t* dst, float* dst_scale, void* stream) {
+    if (!src || !src_scale || !rows_index || !rows_count || !dst || !dst_scale) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 7u) return DH_ERR_ALIGNMENT;
+    gather_rows_i8_kernel<<<(rows + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, src_scale, rows_index, rows_count, rows, dst, dst_scale);
     DH_LAUNCH_CHECK();
     return DH_OK;
 }

@@ -161,6 +161,13 @@ class MDLMEngine:
         self.head_group = None      # process group reducing the sharded head, or None
         self.head_reduce = None     # callable(packed) merging shard results (testing / custom groups)
         self.pre_forward = None     # callable(fwd_rows) enqueued before each transition's forward
+        # forward only the sequences that refill (True), the whole batch when
+        # one does (False), or choose per generation (None): packing pays when
+        # sequences often go a transition without a change, i.e. when the
+        # expected reveals per transition L / steps are few
+        self.compact: Optional[bool] = None
+        self._compact_now = False
+        self._compact_bufs: Optional[tuple] = None  # seq_list, per-row head input and scale
         self._graphs: Dict[Any, Any] = {}
         self._events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         self.launches_per_forward = 1 + 9 * len(self.blocks)
@@ -197,15 +204,21 @@ class MDLMEngine:
         return _lib.ptr(t)
 
     @_on_device
-    def forward(self, tokens: Any = None, run_rows: Any = None, hook: Any = None) -> None:
+    def forward(self, tokens: Any = None, run_rows: Any = None, hook: Any = None, seq_list: Any = None) -> None:
         """Forward over self.tokens (or `tokens`, int32 [M] on the device);
-        leaves the residual stream in self.x.  run_rows: device word, the
-        forward is skipped when it holds 0.  hook(i) runs after block i."""
+        leaves the residual stream in self.x.  run_rows: device word, only
+        its first *run_rows rows are computed (0: none).  seq_list: the rows
+        are the packed positions of the listed sequences.  hook(i) runs after
+        block i."""
         s = _lib.stream_handle()
         tok = self.tokens if tokens is None else tokens
         rr = self._p(run_rows) if run_rows is not None else None
-        _lib.call("dh_embed_gather", self._p(tok), self._p(self.embedding), self._p(self.x), self.M,
-                  self.cfg.vocab_size, rr, s)
+        if seq_list is not None:
+            _lib.call("dh_embed_gather_seqs", self._p(tok), self._p(seq_list), self.L, self._p(self.embedding),
+                      self._p(self.x), self.M, self.cfg.vocab_size, rr, s)
+        else:
+            _lib.call("dh_embed_gather", self._p(tok), self._p(self.embedding), self._p(self.x), self.M,
+                      self.cfg.vocab_size, rr, s)
         for i, blk in enumerate(self.blocks):
             self._forward_block(i, blk, rr, s)
             if hook is not None:
@@ -315,16 +328,25 @@ class MDLMEngine:
         call = _lib.call
         final = 1 if k == steps else 0
         kk = min(k, steps - 1)
-        call("dh_loop_plan", B, L, kk, steps, final, p(self.active), p(self.need_eval), p(self.eval_id),
-             p(self.fwd_rows), p(self.sel_count), p(self.counters), s)
+        seqs = self._compact_buffers()[0] if self._compact_now else None
+        call("dh_loop_plan_seqs", B, L, kk, steps, final, p(self.active), p(self.need_eval), p(self.eval_id),
+             p(self.fwd_rows), p(self.sel_count), p(self.counters), p(seqs), s)
         if self.pre_forward is not None:
             self.pre_forward(self.fwd_rows)
-        self.forward(run_rows=self.fwd_rows)
+        self.forward(run_rows=self.fwd_rows, seq_list=seqs)
+        if seqs is not None:
+            _, head_all, head_all_scale = self._compact_buffers()
+            call("dh_ln_smooth_quant_scatter", p(self.x), p(self.head.smooth), p(self.head.inv_smooth),
+                 p(head_all), p(head_all_scale), self.M, p(seqs), L, p(self.fwd_rows), s)
         call("dh_loop_select", B, L, kk, seed, self.seq_offset, self.pos_offset, 0 if final else threshold_q32,
              final,
              p(self.active), p(self.eval_id), p(self.sel_rows), p(self.sel_pos), p(self.sel_key),
              p(self.sel_eval), p(self.sel_count), s)
-        self.final_hidden_q(self.sel_rows, self.sel_count)
+        if seqs is not None:
+            call("dh_gather_rows_i8", p(head_all), p(head_all_scale), p(self.sel_rows), p(self.sel_count), self.M,
+                 p(self.head_q), p(self.head_scale), s)
+        else:
+            self.final_hidden_q(self.sel_rows, self.sel_count)
         self.head_argmax(self.M, 2 if final else 1, rows_count=self.sel_count, row_position=self.sel_pos,
                          row_key_hi=self.sel_key, row_eval=self.sel_eval, key_lo=seed)
         if self.head_reduce is not None:
@@ -335,6 +357,23 @@ class MDLMEngine:
             all_reduce_packed_max_(self.packed, self.head_group)
         call("dh_loop_commit", B, L, kk, steps, final, p(self.packed), p(self.sel_rows), p(self.sel_count),
              p(self.tokens), p(self.active), p(self.need_eval), p(self.counters), s)
+
+    def _compact_buffers(self) -> tuple:
+        if self._compact_bufs is None:
+            torch = self.torch
+            self._compact_bufs = (torch.empty(self.B, dtype=torch.int32, device=self.device),
+                                  torch.empty((self.M, 768), dtype=torch.int8, device=self.device),
+                                  torch.empty(self.M, dtype=torch.float32, device=self.device))
+        return self._compact_bufs
+
+    def compact_for(self, steps: int) -> bool:
+        """Whether a `steps`-transition generation packs the forward to the
+        refilling sequences: as set in `compact`, else when the batch holds
+        several sequences and fewer than 4 reveals per transition are expected
+        (L < 4 steps), so that a sequence often goes a transition unchanged."""
+        if self.compact is not None:
+            return bool(self.compact)
+        return self.B > 1 and self.L < 4 * steps
 
     def _enqueue_generation(self, steps: int, seed: int, thresholds: List[int]) -> None:
         for k in range(steps + 1):
@@ -410,7 +449,8 @@ class MDLMEngine:
         w = self.native_weights()
         _lib.call("dh_sample_loop", ctypes.addressof(w), _lib.ptr(self.ids_in), _lib.ptr(self.tokens), self.B,
                   self.L, steps, ctypes.addressof(thr), seed, self.seq_offset, _lib.ptr(self.counters),
-                  self._nccl_comm(), _lib.ptr(self._loop_ws), self._loop_ws.numel(), _lib.stream_handle())
+                  self._nccl_comm(), 1 if self._compact_now else 0, _lib.ptr(self._loop_ws), self._loop_ws.numel(),
+                  _lib.stream_handle())
 
     def launches_per_generation(self, steps: int) -> int:
         per_transition = 1 + self.launches_per_forward + 1 + 1 + 2 + 1
@@ -428,6 +468,7 @@ class MDLMEngine:
         torch = self.torch
         thresholds = reveal_thresholds_q32(steps, sampling_epsilon)
         native = self.native_loop_ok() if native is None else native
+        self._compact_now = self.compact_for(steps)
         if native:
             if input_ids.numel() != self.M:
                 raise ValueError("input_ids must be [batch, seq_len]")
@@ -442,7 +483,7 @@ class MDLMEngine:
             def enqueue() -> None:
                 self._enqueue_generation(steps, seed, thresholds)
         if graph:
-            key = (native, steps, seed, sampling_epsilon, self.seq_offset)
+            key = (native, self._compact_now, steps, seed, sampling_epsilon, self.seq_offset)
             g = self._graphs.get(key)
             if g is None:
                 # warm-up outside capture (function attributes, tensor maps)

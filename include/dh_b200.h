@@ -330,11 +330,20 @@ uint32_t dh_packed_int8_attention_q12(const int32_t* query_q12, const int32_t* k
  * (1 if 0), q = clamp(round(a' / a_scale), -127, 127); the linear output is
  * acc * (a_scale * w_scale) + bias with w_scale per output channel.  d = 768,
  * 12 heads x 64, MLP 3072.  `run_flag` / `run_rows` (device words, may be
- * NULL) let a captured graph skip a forward: 0 = do nothing. */
+ * NULL) limit a launch to its first *run_rows rows (the attention: to the
+ * sequences those rows cover), so a captured graph skips a forward with 0,
+ * or runs it over the sequences that need one, packed first. */
 
 /* x[r, :] = embedding[tokens[r], :]  (fp32 rows of 768; mlx_mdlm.py:262-268). */
 uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x, uint32_t rows,
                          uint32_t vocabulary_size, const uint32_t* run_flag, void* stream);
+
+/* dh_embed_gather over a packed list of sequences: row r of x is position
+ * r % positions of sequence seq_list[r / positions] of tokens [*, positions]
+ * (the forward of only the sequences that need one; dh_loop_plan_seqs). */
+uint32_t dh_embed_gather_seqs(const int32_t* tokens, const uint32_t* seq_list, uint32_t positions,
+                              const float* embedding, float* x, uint32_t rows, uint32_t vocabulary_size,
+                              const uint32_t* run_rows, void* stream);
 
 /* LayerNorm (no affine, eps 1e-5) -> SmoothQuant division by smooth[768]
  * -> per-token int8 (K3): a = LN(x) / s, scale = amax(|a|) / 127 (1 for a
@@ -350,6 +359,20 @@ uint32_t dh_embed_gather(const int32_t* tokens, const float* embedding, float* x
 uint32_t dh_ln_smooth_quant(const float* x, const float* smooth, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, const uint32_t* rows_index, const uint32_t* rows_count,
                             const uint32_t* run_flag, void* stream);
+
+/* dh_ln_smooth_quant of packed rows (the forward over seq_list, see
+ * dh_embed_gather_seqs), each output row written back to its sequence's own
+ * row seq_list[r / positions] * positions + r % positions of out / scale:
+ * the head's int8 input of every sequence stays available between the
+ * forwards of that sequence. */
+uint32_t dh_ln_smooth_quant_scatter(const float* x, const float* smooth, const float* inv_smooth, int8_t* out,
+                                    float* scale, uint32_t rows, const uint32_t* seq_list, uint32_t positions,
+                                    const uint32_t* run_rows, void* stream);
+
+/* dst row i = src row rows_index[i] (768 int8) and dst_scale[i] =
+ * src_scale[rows_index[i]] for i < min(rows, *rows_count). */
+uint32_t dh_gather_rows_i8(const int8_t* src, const float* src_scale, const uint32_t* rows_index,
+                           const uint32_t* rows_count, uint32_t rows, int8_t* dst, float* dst_scale, void* stream);
 
 /* bf16 rows (cols = 768 or 3072) -> per-token int8 (K3'), the quantiser of
  * dh_ln_smooth_quant on fp32(in) / smooth (inv_smooth as there).  smooth may
@@ -511,6 +534,14 @@ uint32_t dh_loop_plan(uint32_t sequences, uint32_t positions, uint32_t step, uin
                       uint32_t final_pass, const uint64_t* active, uint32_t* need_eval,
                       uint32_t* eval_id, uint32_t* fwd_rows, uint32_t* sel_count,
                       int32_t* counters, void* stream);
+/* dh_loop_plan that also lists the sequences that refill at this transition
+ * (seq_list [sequences], ascending) and sets *fwd_rows = their count *
+ * positions: the ddpm_cache skip per sequence (mdlm.py:1134-1174 invalidates
+ * the cache of a canvas that changed), so the forward covers only those. */
+uint32_t dh_loop_plan_seqs(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t steps,
+                           uint32_t final_pass, const uint64_t* active, uint32_t* need_eval,
+                           uint32_t* eval_id, uint32_t* fwd_rows, uint32_t* sel_count,
+                           int32_t* counters, uint32_t* seq_list, void* stream);
 uint32_t dh_loop_select(uint32_t sequences, uint32_t positions, uint32_t step, uint32_t seed,
                         uint32_t seq_offset, uint32_t position_offset, uint64_t threshold_q32, uint32_t final_pass, const uint64_t* active,
                         const uint32_t* eval_id, uint32_t* sel_rows, uint32_t* sel_pos,
@@ -580,13 +611,19 @@ uint32_t dh_ddit_forward(const dh_mdlm_weights* weights, const int32_t* tokens, 
  * shards of the head (weights->head_rows / head_vocab_offset); after every
  * head launch the packed per-row results are merged by
  * dh_vocab_shard_reduce over it, so every rank commits the unsharded argmax.
- * The whole generation is enqueued without host synchronisation (it can be
- * captured in a CUDA graph).  Status: DH_CAND_INVALID_THRESHOLD for a
- * threshold above 2^32, else DH_ERR_*. */
+ * compact: 0 -> a transition runs the forward over the whole batch when any
+ * sequence refills; 1 -> only over the sequences that refill, packed
+ * (dh_loop_plan_seqs), with every refilled row's head input kept per
+ * sequence -- the same tokens, fewer rows when canvases are small (a
+ * sequence with L/steps expected reveals per transition skips one with
+ * probability about exp(-L/steps)), one extra LayerNorm pass over the
+ * refilled rows otherwise.  The whole generation is enqueued without host
+ * synchronisation (it can be captured in a CUDA graph).  Status:
+ * DH_CAND_INVALID_THRESHOLD for a threshold above 2^32, else DH_ERR_*. */
 size_t dh_sample_loop_workspace_size(uint32_t sequences, uint32_t positions);
 uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids, int32_t* tokens,
                         uint32_t sequences, uint32_t positions, uint32_t steps, const uint64_t* thresholds_q32,
-                        uint32_t seed, uint32_t seq_offset, int32_t* counters, void* nccl_comm,
+                        uint32_t seed, uint32_t seq_offset, int32_t* counters, void* nccl_comm, uint32_t compact,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* Merge of the vocab-sharded head: packed (device uint64 [count], as written

@@ -34,7 +34,7 @@ def test_composite_argument_checks_need_no_gpu():
     assert _lib.raw("dh_ddit_forward", ctypes.addressof(w), 1, 1, 64, 1, 1, 1 << 20, None, None) == 100
     thr = (ctypes.c_uint64 * 2)(1 << 31, (1 << 32) + 1)
     assert _lib.raw("dh_sample_loop", ctypes.addressof(w), 1, 1, 1, 64, 2, ctypes.addressof(thr), 0, 0, 1,
-                    None, 1, 1 << 20, None) == 100
+                    None, 0, 1, 1 << 20, None) == 100
     assert _lib.lib().dh_sample_loop_workspace_size(4, 1024) > _lib.lib().dh_ddit_forward_workspace_size(4, 1024)
 
 
@@ -70,8 +70,8 @@ def test_ddit_forward_equals_per_kernel_forward(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B,L,steps", [(2, 256, 12), (3, 96, 8)])
-def test_sample_loop_equals_per_kernel_loop(cuda, B, L, steps):
+@pytest.mark.parametrize("B,L,steps,compact", [(2, 256, 12, 0), (3, 96, 8, 0), (3, 96, 8, 1), (4, 64, 64, 1)])
+def test_sample_loop_equals_per_kernel_loop(cuda, B, L, steps, compact):
     torch = cuda
     from diffusionhard_b200.engine import MDLMEngine
 
@@ -80,6 +80,7 @@ def test_sample_loop_equals_per_kernel_loop(cuda, B, L, steps):
     eng.seq_offset = 5
     ids = torch.full((B, L), SMALL.mask_token_id, dtype=torch.int64)
     ids[:, ::7] = 3  # a few clean positions
+    eng.compact = False
     ref, _ = eng.generate(ids.cuda(), steps=steps, seed=11, native=False)
     ref = ref.clone()
     ref_counters = eng.counters.clone()
@@ -91,12 +92,14 @@ def test_sample_loop_equals_per_kernel_loop(cuda, B, L, steps):
     ws = torch.empty(_lib.lib().dh_sample_loop_workspace_size(B, L), dtype=torch.uint8, device="cuda")
     thr = (ctypes.c_uint64 * steps)(*reveal_thresholds_q32(steps))
     _lib.call("dh_sample_loop", ctypes.addressof(w), _lib.ptr(ids_in), _lib.ptr(tokens), B, L, steps,
-              ctypes.addressof(thr), 11, 5, _lib.ptr(counters), None, _lib.ptr(ws), ws.numel(), _lib.stream_handle())
+              ctypes.addressof(thr), 11, 5, _lib.ptr(counters), None, compact, _lib.ptr(ws), ws.numel(),
+              _lib.stream_handle())
     torch.cuda.synchronize()
     assert torch.equal(tokens.view(B, L), ref)
     assert torch.equal(counters, ref_counters)
     assert not (tokens == SMALL.mask_token_id).any()
     # and engine.generate's default route (the composite) gives the same
+    eng.compact = bool(compact)
     out, _ = eng.generate(ids.cuda(), steps=steps, seed=11, graph=True)
     assert torch.equal(out, ref)
     err = np.zeros(1, np.uint32)
@@ -127,3 +130,37 @@ def test_vocab_shard_reduce_on_one_rank(cuda, tmp_path):
         assert torch.equal(packed, before)
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_packed_forward_computes_only_the_refilling_sequences(cuda):
+    """Per-sequence ddpm_cache skip (mdlm.py:1134-1174 per canvas): with half
+    of the batch already clean, the packed loop runs the forward over the
+    other half only -- half the rows of the whole-batch loop -- and commits
+    the same tokens.  Transition by transition through the per-kernel entry
+    points, reading the planned forward rows."""
+    torch = cuda
+    from diffusionhard_b200.engine import MDLMEngine
+
+    qm = build_quantized(SMALL, seed=0)
+    B, L, steps = 4, 64, 16
+    ids = torch.full((B, L), SMALL.mask_token_id, dtype=torch.int64)
+    ids[1] = torch.randint(0, 999, (L,), generator=torch.Generator().manual_seed(1))
+    ids[3] = torch.randint(0, 999, (L,), generator=torch.Generator().manual_seed(3))
+    thr = reveal_thresholds_q32(steps)
+    results = {}
+    for compact in (False, True):
+        eng = MDLMEngine(qm, B, L)
+        eng._compact_now = compact
+        eng.init_loop(ids.cuda(), steps)
+        rows = 0
+        for k in range(steps + 1):
+            eng.enqueue_transition(k, steps, 5, thr[k] if k < steps else 0)
+            torch.cuda.synchronize()
+            rows += int(eng.fwd_rows.item())
+        results[compact] = (eng.tokens.clone(), rows, eng.metadata(steps))
+    (t0, r0, m0), (t1, r1, m1) = results[False], results[True]
+    assert torch.equal(t0, t1)
+    assert r1 * 2 == r0 and r1 > 0
+    assert m0 == m1
+    assert not (t1 == SMALL.mask_token_id).any()
