@@ -138,7 +138,9 @@ def test_packed_forward_computes_only_the_refilling_sequences(cuda):
     of the batch already clean, the packed loop runs the forward over the
     other half only -- half the rows of the whole-batch loop -- and commits
     the same tokens.  Transition by transition through the per-kernel entry
-    points, reading the planned forward rows."""
+    points, reading the planned forward rows (at most half of the
+    whole-batch rows: fewer when one of the masked sequences also goes a
+    transition unchanged)."""
     torch = cuda
     from diffusionhard_b200.engine import MDLMEngine
 
@@ -161,6 +163,6 @@ def test_packed_forward_computes_only_the_refilling_sequences(cuda):
         results[compact] = (eng.tokens.clone(), rows, eng.metadata(steps))
     (t0, r0, m0), (t1, r1, m1) = results[False], results[True]
     assert torch.equal(t0, t1)
-    assert r1 * 2 == r0 and r1 > 0
+    assert 0 < r1 <= r0 // 2
     assert m0 == m1
     assert not (t1 == SMALL.mask_token_id).any()
