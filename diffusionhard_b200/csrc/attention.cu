@@ -7,7 +7,7 @@
 // bf16, V transposed [B, H, 64, kv_len] f16.  Output O [B * q_len, H * 64] bf16
 // (token-major, heads concatenated, the input of the attention-out linear).
 //
-// Persistent kernel, two CTAs per SM, 10 warps each.  A work item is
+// Persistent kernel, two CTAs per SM, 6 warps each.  A work item is
 // (128-query tile, head, sequence); keys are processed in tiles of 64:
 //   warp 0   TMA: Q once per item (staged in shared memory, copied into
 //            TMEM by the softmax warps), then K_j (4-deep ring) and V_j (3-deep)
@@ -17,21 +17,17 @@
 //            [O | l] += P_j [V_j | 1] (f16, 128 x 80 x 64) with P_j read from
 //            TMEM; a ones row under each V tile makes the tensor core also
 //            sum P into column 64.
-//   warps 2-9 softmax: two warps per TMEM lane quadrant, each reading 16
-//            query rows x 64 scores in the 16 x 256-bit fragment (two rows
-//            and 16 scores per thread; a row's maximum takes two shuffles),
-//            keeping the running max in registers (base-2 domain), and
-//            writing P_j = 2^(s*c - m) as packed f16 back over S_j in TMEM.
+//   warps 2-5 softmax: one thread per query row reads its 64 scores from
+//            TMEM, keeps the running max in a register (base-2 domain), and
+//            writes P_j = 2^(s*c - m) as packed f16 back over S_j in TMEM.
 //            O accumulates in TMEM across key tiles and is rescaled in place
-//            only when a row max grows by more than 2^8.
+//            only when the row max grows by more than 2^8.
 // Keeping Q and P in TMEM takes their reads (and P's write) off shared
 // memory, whose bandwidth (128 B/clk) the MMA operand reads otherwise
 // saturate at these shapes: per 64-key tile only K, V and their TMA writes
 // touch it.  Two S/P buffers let the softmax of tile j+1 run while PV_j
-// executes.  Writing P in the 16-lane fragment places each key at a fixed
-// permuted position of its 64-key block, and V^T holds its keys in that
-// order (vt_key_position, written so by the QKV epilogue).  ~78 KB shared
-// memory and 256 TMEM columns per CTA.  All waits are bounded.
+// executes.  ~78 KB shared memory and 256 TMEM columns per CTA.  All waits
+// are bounded.
 #include <cuda.h>
 #include <cuda_bf16.h>
 
@@ -47,7 +43,7 @@ constexpr uint32_t kHeads = 12;
 constexpr uint32_t kDh = 64;
 constexpr uint32_t kQTile = 128;                      // queries per work item
 constexpr uint32_t kKT = 64;                          // keys per tile
-constexpr uint32_t kThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
+constexpr uint32_t kThreads = 192;
 constexpr uint32_t kQBytes = kQTile * kDh * 2;        // 16 KB
 constexpr uint32_t kKBytes = kKT * kDh * 2;           // 8 KB (64 keys x 128 B)
 // V tile: [64 value rows ; 16 constant rows] x 64 keys, f16, SW128 K-major.
@@ -182,7 +178,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         for (uint32_t i = 0; i < kNumBars; ++i) {
             const bool softmax_side =
                 (i >= kPFull && i < kPFull + 2) || i == kOFree || i == kQEmpty || i == kQReady;
-            tc::mbar_init(&bars[i], softmax_side ? 256u : 1u);
+            tc::mbar_init(&bars[i], softmax_side ? 128u : 1u);
         }
         tc::fence_barrier_init();
         tc::prefetch_tmap(&tq);
@@ -290,47 +286,31 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         }
     } else {
         // ----------------------------------------------------------- softmax
-        // Eight warps.  Warp w reads TMEM lanes [32 q + 16 h, + 16) with
-        // q = w % 4 (its quadrant) and h = (w - 2) / 4, in the 16 x 256-bit
-        // fragment: thread t holds, of 8-column group g, columns 8g + 2(t%4)
-        // and 8g + 2(t%4) + 1 of query rows rA = base + t/4 and rB = rA + 8.
-        // A row's 64 scores lie in the four threads t/4 (two shuffles give
-        // its max).  p = 2^(s*c - m) with the running max m kept stale until
-        // a tile's max exceeds it by more than 8 (p <= 2^8 meanwhile); only
-        // then are O and l (accumulated in TMEM across tiles) rescaled -- a
-        // rare path.  P goes back into the S buffer as packed f16 in the same
-        // fragment with 4 instead of 8 columns per group, so key 8g + 2(t%4)
-        // + e lands at P position 16(g/2) + 4(t%4) + 2(g%2) + e; V^T carries
-        // its keys in that order (vt_key_position), so P V is unchanged.
+        // One thread per query row.  p = 2^(s*c - m) with the running max m
+        // kept stale until a tile's max exceeds it by more than 8 (p <= 2^8
+        // meanwhile); only then are O and l (accumulated in TMEM across
+        // tiles) rescaled -- a warp-uniform, rare path.
         const uint32_t quad = warp & 3u;
-        const uint32_t half = (warp - 2u) >> 2;
-        const uint32_t row_base = 32u * quad + 16u * half;  // first row of this warp's fragment
-        const uint32_t t4 = lane & 3u;
-        const uint32_t frag = tmem + (row_base << 16);
-        // one thread per row of the quadrant, columns split by `half`, for
-        // the Q copy and the output (32 x 32-bit shape)
-        const uint32_t r = quad * 32 + lane;
+        const uint32_t r = quad * 32 + lane;  // query row within the tile
         const uint32_t lane_base = (quad * 32u) << 16;
         const float c = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
         // Q row r of item `qi` from the TMA-staged (128-byte swizzled) tile into
-        // TMEM lane r, words [16 half, 16 half + 16), then release the staging
-        // buffer and signal the MMA warp.  Called before the item's first S and
-        // only after every S of the previous item completed (this thread saw
-        // their kSFull).
+        // TMEM lane r, then release the staging buffer and signal the MMA warp.
+        // Called before the item's first S and only after every S of the
+        // previous item completed (this thread saw their kSFull).
         auto copy_q = [&](uint32_t qi) -> bool {
             if (!tc::mbar_wait(&bars[kQFull], qi & 1u, tc::kErrTimeoutFull)) return false;
             const uint8_t* rowq = q_s + (r >> 3) * 1024 + (r & 7u) * 128;
-            uint32_t qv[16];
+            uint32_t qv[32];
 #pragma unroll
-            for (uint32_t cc = 0; cc < 4; ++cc) {
-                const uint32_t chunk = 4 * half + cc;
-                const uint4 v = *reinterpret_cast<const uint4*>(rowq + ((chunk ^ (r & 7u)) * 16));
+            for (uint32_t cc = 0; cc < 8; ++cc) {
+                const uint4 v = *reinterpret_cast<const uint4*>(rowq + ((cc ^ (r & 7u)) * 16));
                 qv[4 * cc] = v.x;
                 qv[4 * cc + 1] = v.y;
                 qv[4 * cc + 2] = v.z;
                 qv[4 * cc + 3] = v.w;
             }
-            tc::tmem_st_32x32b_x16(tmem + lane_base + kQCol + 16 * half, qv);
+            tc::tmem_st_32x32b_x32(tmem + lane_base + kQCol, qv);
             tc::tmem_st_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars[kQEmpty]);
@@ -341,83 +321,71 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
         bool ok = blockIdx.x >= total || copy_q(0);
         for (uint32_t w = blockIdx.x; w < total && ok; w += gridDim.x, ++it) {
             const Item item = item_of(w, n_qt);
-            float mA = 0.f, mB = 0.f;
+            float m = 0.f;
             for (uint32_t j = 0; j < n_kv; ++j, ++g) {
                 const uint32_t sb = g & 1u;
                 if (!tc::mbar_wait(&bars[kSFull + sb], (g >> 1) & 1u, tc::kErrTimeoutAccFull)) { ok = false; break; }
                 tc::tc_fence_after();
-                uint32_t sv[32];
-                tc::tmem_ld_16x256b_x8(frag + sb * kKT, sv);
+                uint32_t sv[64];
+                tc::tmem_ld_32x32b_x32(tmem + lane_base + sb * kKT, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+                tc::tmem_ld_32x32b_x32(tmem + lane_base + sb * kKT + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
                 tc::tmem_ld_wait();
                 // ragged key tail: keys past kv_len score -inf (p = 0); their
                 // K rows are whatever the tile read, V rows are finite (zero
                 // padding or other rows), so 0 * V adds nothing.
                 if (j + 1 == n_kv && kv_rem != kKT) {
 #pragma unroll
-                    for (uint32_t gg = 0; gg < 8; ++gg)
-#pragma unroll
-                        for (uint32_t e = 0; e < 2; ++e)
-                            if (8 * gg + 2 * t4 + e >= kv_rem) {
-                                sv[4 * gg + e] = 0xFF800000u;
-                                sv[4 * gg + 2 + e] = 0xFF800000u;
-                            }
+                    for (uint32_t e = 0; e < 64; ++e)
+                        if (e >= kv_rem) sv[e] = 0xFF800000u;
                 }
-                float xa = __uint_as_float(sv[0]), xb = __uint_as_float(sv[2]);
-                float ya = __uint_as_float(sv[1]), yb = __uint_as_float(sv[3]);
+                // row max with 8 independent partial maxima (short dependency chains)
+                float pm[8];
 #pragma unroll
-                for (uint32_t gg = 1; gg < 8; ++gg) {
-                    xa = fmaxf(xa, __uint_as_float(sv[4 * gg]));
-                    ya = fmaxf(ya, __uint_as_float(sv[4 * gg + 1]));
-                    xb = fmaxf(xb, __uint_as_float(sv[4 * gg + 2]));
-                    yb = fmaxf(yb, __uint_as_float(sv[4 * gg + 3]));
+                for (uint32_t q = 0; q < 8; ++q) pm[q] = __uint_as_float(sv[q]);
+#pragma unroll
+                for (uint32_t e = 8; e < 64; e += 16) {
+#pragma unroll
+                    for (uint32_t q = 0; q < 8; ++q) {
+                        const uint32_t i0 = e + q, i1 = e + 8 + q;
+                        if (i1 < 64) {
+                            float t3;
+                            asm("max.f32 %0, %1, %2, %3;" : "=f"(t3) : "f"(pm[q]), "f"(__uint_as_float(sv[i0])),
+                                "f"(__uint_as_float(sv[i1])));
+                            pm[q] = t3;
+                        } else {
+                            pm[q] = fmaxf(pm[q], __uint_as_float(sv[i0]));
+                        }
+                    }
                 }
-                float tA = fmaxf(xa, ya), tB = fmaxf(xb, yb);
-                tA = fmaxf(tA, __shfl_xor_sync(0xFFFFFFFFu, tA, 1));
-                tB = fmaxf(tB, __shfl_xor_sync(0xFFFFFFFFu, tB, 1));
-                tA = fmaxf(tA, __shfl_xor_sync(0xFFFFFFFFu, tA, 2));
-                tB = fmaxf(tB, __shfl_xor_sync(0xFFFFFFFFu, tB, 2));
-                const float mtA = tA * c, mtB = tB * c;
-                float alphaA = 1.f, alphaB = 1.f;
+                const float tmax = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                         fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+                const float mt = tmax * c;
+                float alpha = 1.f;
                 bool need = false;
                 if (j == 0) {
-                    mA = mtA;
-                    mB = mtB;
-                } else {
-                    if (mtA > mA + 8.0f) {
-                        need = true;
-                        alphaA = ex2_approx(mA - mtA);
-                        mA = mtA;
-                    }
-                    if (mtB > mB + 8.0f) {
-                        need = true;
-                        alphaB = ex2_approx(mB - mtB);
-                        mB = mtB;
-                    }
+                    m = mt;
+                } else if (mt > m + 8.0f) {
+                    need = true;
+                    alpha = ex2_approx(m - mt);
+                    m = mt;
                 }
                 // p = 2^(s*c - m) <= 2^8 as packed f16, stored over S_j in
                 // TMEM: the A operand of PV_j.
                 const float2 c2 = make_float2(c, c);
-                const float2 nmA = make_float2(-mA, -mA), nmB = make_float2(-mB, -mB);
-                uint32_t pk[16];
+                const float2 nm2 = make_float2(-m, -m);
+                uint32_t pk[32];
 #pragma unroll
-                for (uint32_t gg = 0; gg < 8; ++gg) {
-                    const float2 sa = make_float2(__uint_as_float(sv[4 * gg]), __uint_as_float(sv[4 * gg + 1]));
-                    const float2 sbv = make_float2(__uint_as_float(sv[4 * gg + 2]), __uint_as_float(sv[4 * gg + 3]));
-                    const float2 a = __ffma2_rn(sa, c2, nmA);
-                    const float2 b = __ffma2_rn(sbv, c2, nmB);
-                    uint32_t pa, pb;
-                    if ((kPolyPairMask >> gg) & 1u) {
-                        const float2 ya2 = exp2_poly2(a), yb2 = exp2_poly2(b);
-                        pa = pack_f16x2(ya2.x, ya2.y);
-                        pb = pack_f16x2(yb2.x, yb2.y);
+                for (uint32_t e = 0; e < 32; ++e) {
+                    const float2 sv2 = make_float2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1]));
+                    const float2 a = __ffma2_rn(sv2, c2, nm2);
+                    if ((kPolyPairMask >> (e & 7u)) & 1u) {
+                        const float2 y = exp2_poly2(a);
+                        pk[e] = pack_f16x2(y.x, y.y);
                     } else {
-                        pa = ex2_f16x2(pack_f16x2(a.x, a.y));
-                        pb = ex2_f16x2(pack_f16x2(b.x, b.y));
+                        pk[e] = ex2_f16x2(pack_f16x2(a.x, a.y));
                     }
-                    pk[4 * (gg >> 1) + (gg & 1u)] = pa;
-                    pk[4 * (gg >> 1) + 2 + (gg & 1u)] = pb;
                 }
-                tc::tmem_st_16x256b_x4(frag + sb * kKT, pk);
+                tc::tmem_st_32x32b_x32(tmem + lane_base + sb * kKT, pk);
                 if (__any_sync(0xFFFFFFFFu, need)) {
                     // O and l must be stable: PV_{g-1} (the only one that may
                     // still run; PV_g waits for this tile's kPFull) finished.
@@ -426,26 +394,16 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
                         break;
                     }
                     tc::tc_fence_after();
-                    uint32_t ov[32], ow[8];
-                    tc::tmem_ld_16x256b_x8(frag + kOCol, ov);
-                    tc::tmem_ld_16x256b_x2(frag + kOCol + 64, ow);
-                    tc::tmem_ld_wait();
 #pragma unroll
-                    for (uint32_t gg = 0; gg < 8; ++gg) {
-                        ov[4 * gg] = __float_as_uint(__uint_as_float(ov[4 * gg]) * alphaA);
-                        ov[4 * gg + 1] = __float_as_uint(__uint_as_float(ov[4 * gg + 1]) * alphaA);
-                        ov[4 * gg + 2] = __float_as_uint(__uint_as_float(ov[4 * gg + 2]) * alphaB);
-                        ov[4 * gg + 3] = __float_as_uint(__uint_as_float(ov[4 * gg + 3]) * alphaB);
-                    }
+                    for (uint32_t h2 = 0; h2 < 3; ++h2) {  // columns 128..223 (208.. unused)
+                        uint32_t ov[32];
+                        tc::tmem_ld_32x32b_x32(tmem + lane_base + kOCol + 32 * h2, ov);
+                        tc::tmem_ld_wait();
 #pragma unroll
-                    for (uint32_t gg = 0; gg < 2; ++gg) {
-                        ow[4 * gg] = __float_as_uint(__uint_as_float(ow[4 * gg]) * alphaA);
-                        ow[4 * gg + 1] = __float_as_uint(__uint_as_float(ow[4 * gg + 1]) * alphaA);
-                        ow[4 * gg + 2] = __float_as_uint(__uint_as_float(ow[4 * gg + 2]) * alphaB);
-                        ow[4 * gg + 3] = __float_as_uint(__uint_as_float(ow[4 * gg + 3]) * alphaB);
+                        for (uint32_t d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+                        tc::tmem_st_32x32b_x32(tmem + lane_base + kOCol + 32 * h2, ov);
                     }
-                    tc::tmem_st_16x256b_x8(frag + kOCol, ov);
-                    tc::tmem_st_16x256b_x2(frag + kOCol + 64, ow);
+                    tc::tmem_st_wait();
                 }
                 tc::tmem_st_wait();
                 tc::tc_fence_before();
@@ -454,12 +412,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             if (!ok) break;
             // next item's Q into TMEM before this item's epilogue, so its S can start
             if (w + gridDim.x < total && !copy_q(it + 1)) break;
-            // item done: O = accumulated P V, l in column 64; normalise and
-            // store this warp's 32 columns of its quadrant's rows
+            // item done: O = accumulated P V, l in column 64; normalise and store
             if (!tc::mbar_wait(&bars[kOFull], it & 1u, tc::kErrTimeoutAccFull)) break;
             tc::tc_fence_after();
-            uint32_t v0[32];
-            tc::tmem_ld_32x32b_x32(tmem + lane_base + kOCol + 32 * half, v0);
+            uint32_t v0[32], v1[32];
+            tc::tmem_ld_32x32b_x32(tmem + lane_base + kOCol, v0);
+            tc::tmem_ld_32x32b_x32(tmem + lane_base + kOCol + 32, v1);
             const uint32_t l_bits = tc::tmem_ld_32x32b_x1(tmem + lane_base + kOCol + kDh);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
@@ -467,15 +425,20 @@ attention_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
             const float inv_l = 1.0f / __uint_as_float(l_bits);
             if (item.q_tile * kQTile + r >= args.q_len) continue;  // ragged query tail
             const uint64_t tok = static_cast<uint64_t>(item.seq) * args.q_len + item.q_tile * kQTile + r;
-            __nv_bfloat16* dst = args.out + tok * (kHeads * kDh) + item.head * kDh + 32 * half;
+            __nv_bfloat16* dst = args.out + tok * (kHeads * kDh) + item.head * kDh;
 #pragma unroll
             for (uint32_t d = 0; d < 32; d += 8) {
-                uint4 a;
+                uint4 a, b;
                 a.x = pack_bf16(__uint_as_float(v0[d]) * inv_l, __uint_as_float(v0[d + 1]) * inv_l);
                 a.y = pack_bf16(__uint_as_float(v0[d + 2]) * inv_l, __uint_as_float(v0[d + 3]) * inv_l);
                 a.z = pack_bf16(__uint_as_float(v0[d + 4]) * inv_l, __uint_as_float(v0[d + 5]) * inv_l);
                 a.w = pack_bf16(__uint_as_float(v0[d + 6]) * inv_l, __uint_as_float(v0[d + 7]) * inv_l);
+                b.x = pack_bf16(__uint_as_float(v1[d]) * inv_l, __uint_as_float(v1[d + 1]) * inv_l);
+                b.y = pack_bf16(__uint_as_float(v1[d + 2]) * inv_l, __uint_as_float(v1[d + 3]) * inv_l);
+                b.z = pack_bf16(__uint_as_float(v1[d + 4]) * inv_l, __uint_as_float(v1[d + 5]) * inv_l);
+                b.w = pack_bf16(__uint_as_float(v1[d + 6]) * inv_l, __uint_as_float(v1[d + 7]) * inv_l);
                 *reinterpret_cast<uint4*>(dst + d) = a;
+                *reinterpret_cast<uint4*>(dst + 32 + d) = b;
             }
         }
     }
@@ -524,5 +487,3 @@ extern "C" uint32_t dh_attention(const void* q, const void* k, const void* vt, v
     DH_LAUNCH_CHECK();
     return DH_OK;
 }
-
-extern "C" uint32_t dh_vt_key_position(uint32_t key) { return vt_key_position(key); }

@@ -48,17 +48,6 @@ inline cudaError_t smem_optin_once(Kernel kernel, uint32_t bytes, std::atomic<ui
     return e;
 }
 
-// Key order of V^T inside each block of 64 keys: key a = 8g + 2t + e
-// (g < 8, t < 4, e < 2) is stored at position 16(g/2) + 4t + 2(g%2) + e.
-// The attention kernel writes P over its scores in a 16-lane TMEM fragment
-// whose 32-bit columns hold two f16 each, which puts key a at that P
-// position; V^T stored in the same order keeps P V the plain sum over keys.
-// Each 32-key half maps onto itself, so 32 consecutive keys still fill one
-// 64-byte run.
-__host__ __device__ __forceinline__ uint32_t vt_key_position(uint32_t a) {
-    return (a & ~63u) | (a & 0x31u) | ((a & 0x06u) << 1) | ((a & 0x08u) >> 2);
-}
-
 DH_DEVINL uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

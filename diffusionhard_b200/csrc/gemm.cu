@@ -234,11 +234,9 @@ struct EpiQKV : EpiBase {
             // one 64-byte run, so lane = token stores are already coalesced
             // (measured faster than staging the transpose through shared
             // memory, which the tensor core's operand reads also use).
-            // Keys stay in their 64-key block, permuted as the attention
-            // kernel's P fragment expects (vt_key_position).
             if (live) {
-                __half* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride +
-                              vt_key_position(t0 + lane + p.kv_offset);
+                __half* dst = p.vt + (static_cast<uint64_t>(b) * heads + h) * 64 * p.kv_stride + t0 + lane +
+                              p.kv_offset;
 #pragma unroll
                 for (uint32_t d = 0; d < 64; ++d)
                     dst[static_cast<uint64_t>(d) * p.kv_stride] = __float2half_rn(y[d]);

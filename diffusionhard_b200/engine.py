@@ -40,26 +40,6 @@ class _DevLinear:
         self.out_features, self.in_features = ql.weight_q.shape
 
 
-def vt_key_positions(keys: int) -> np.ndarray:
-    """Position of each key in V^T's key order (vt_key_position of the C
-    library): inside each 64-key block, key a = 8g + 2t + e sits at
-    16(g/2) + 4t + 2(g%2) + e, the order in which the attention kernel writes
-    P.  `keys` is a multiple of 32."""
-    a = np.arange(keys, dtype=np.int64)
-    return (a & ~63) | (a & 0x31) | ((a & 0x06) << 1) | ((a & 0x08) >> 2)
-
-
-def to_vt_order(vt: Any) -> Any:
-    """V^T [..., keys] with keys in natural order -> the layout dh_attention
-    reads (keys permuted inside each 64-key block)."""
-    import torch
-
-    pos = torch.from_numpy(vt_key_positions(vt.shape[-1])).to(vt.device)
-    out = torch.empty_like(vt)
-    out[..., pos] = vt
-    return out
-
-
 def _on_device(method):
     """Run an engine method with the engine's GPU as the current device.
     Every launch goes to the current device's current stream and reads the

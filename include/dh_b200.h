@@ -384,8 +384,8 @@ uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, const float* in
 /* QKV projection (K4): [m, 768] x [2304, 768]^T, dequant, rotate-half rotary
  * on q and k at position (row % seq_len) + pos_offset (mlx_mdlm.py:298-329),
  * written as bf16 Q [B, 12, seq_len, 64] and K [B, 12, kv_stride, 64] and f16
- * V^T [B, 12, 64, kv_stride] (keys in the order of dh_vt_key_position) at key
- * offset kv_offset (a multiple of 32) -- the layout of a cached
+ * V^T [B, 12, 64, kv_stride] at key offset kv_offset (a multiple of 32) --
+ * the layout of a cached
  * prefix followed by the active rows (prefix_drift.py:155-238).
  * rope_cos / rope_sin: [positions, 32] fp32.  v_scale (768, may be NULL)
  * multiplies V per channel: with the SmoothQuant 1/s of the attention-out
@@ -425,21 +425,13 @@ uint32_t dh_quant_rows_bf16_amax(const void* in, uint32_t* row_amax, int8_t* out
 /* Bidirectional attention softmax(Q K^T / 8) V (K5) over the first kv_len
  * keys of K / V^T buffers of kv_stride rows per (sequence, head); Q, K bf16,
  * V^T f16, fp32 scores and row sums, P in f16, bf16 out [sequences * q_len, 768].  q_len, kv_len multiples
- * of 32, kv_stride a multiple of 8.  V^T holds the keys of each 64-key block
- * in the order of dh_vt_key_position (as dh_gemm_qkv_rope writes them); K is
- * in natural order.  Keys are read in tiles of 64: when kv_len is not a
- * multiple of 64, the V^T columns from kv_len up to the next multiple of 64
- * that lie inside kv_stride must hold finite values (zero-fill the buffers
- * once); those keys are masked. */
+ * of 32, kv_stride a multiple of 8.  Keys are read in tiles of 64: when
+ * kv_len is not a multiple of 64, the V^T columns from kv_len up to the next
+ * multiple of 64 that lie inside kv_stride must hold finite values (zero-fill
+ * the buffers once); those keys are masked. */
 uint32_t dh_attention(const void* q, const void* k, const void* vt, void* out, uint32_t sequences,
                       uint32_t q_len, uint32_t kv_len, uint32_t kv_stride, const uint32_t* run_flag,
                       void* stream);
-
-/* Column of key `key` in V^T (host function): inside each block of 64 keys,
- * key 8g + 2t + e (g < 8, t < 4, e < 2) is stored at 16(g/2) + 4t + 2(g%2) + e
- * -- the position at which the attention kernel's 16-lane TMEM fragment
- * writes that key's probability; each 32-key half maps onto itself. */
-uint32_t dh_vt_key_position(uint32_t key);
 
 /* ---------------------------- final layer with per-sequence conditioning */
 

@@ -35,11 +35,3 @@ def test_pinned_method_enters_the_engine_device():
     assert launch(fake, 41) == 42
     assert seen == [("enter", "cuda:1"), ("body", 41), ("exit", "cuda:1")]
 
-
-def test_vt_key_order_matches_the_library():
-    from diffusionhard_b200 import _lib
-
-    pos = engine_mod.vt_key_positions(256)
-    assert sorted(pos.tolist()) == list(range(256))  # a permutation
-    assert (pos[:32] < 32).all() and (pos[32:64] >= 32).all() and (pos[64:] >= 64).all()  # halves stay put
-    assert [_lib.lib().dh_vt_key_position(int(k)) for k in range(256)] == pos.tolist()

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from diffusionhard_b200 import _lib
-from diffusionhard_b200.engine import MDLMEngine, to_vt_order
+from diffusionhard_b200.engine import MDLMEngine
 from diffusionhard_b200.model import MDLMConfig, build_quantized
 from diffusionhard_b200.sampler import reveal_thresholds_q32
 from oracle import model_oracle, pyoracle
@@ -177,7 +177,7 @@ def test_attention_matches_sdpa(cuda):
     k = torch.randn((B, H, kv_stride, 64), device="cuda", generator=g).to(torch.bfloat16)
     vt = torch.randn((B, H, 64, kv_stride), device="cuda", generator=g).to(torch.float16)
     k[:, :, :P] *= 3  # a prefix with larger scores exercises the rescale path
-    vt_dev = to_vt_order(vt)  # the key order the kernel reads
+    vt_dev = vt
     for kv_len in (Lq, kv_stride):
         out = torch.empty((B * Lq, 768), dtype=torch.bfloat16, device="cuda")
         _lib.call("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt_dev), _lib.ptr(out), B, Lq, kv_len,
@@ -210,7 +210,7 @@ def test_attention_ragged_lengths(cuda, Lq, P):
     guard = 4096
     buf = torch.full((B * Lq * 768 + guard,), 7.0, dtype=torch.bfloat16, device="cuda")
     out = buf[: B * Lq * 768].view(B * Lq, 768)
-    vt_dev = to_vt_order(vt)  # the key order the kernel reads
+    vt_dev = vt
     _lib.call("dh_attention", _lib.ptr(q), _lib.ptr(k), _lib.ptr(vt_dev), _lib.ptr(out), B, Lq, kv_len,
               kv_stride, None, None)
     torch.cuda.synchronize()
