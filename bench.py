@@ -453,6 +453,34 @@ def profile_forward(args) -> None:
     print("profile-forward done", flush=True)
 
 
+def profile_head(args) -> None:
+    """The head microbench's pipeline (adaLN, masked-row compaction,
+    LayerNorm + modulation + int8, fused head) on --batch x 1024 bf16 hidden
+    states, 50% masked, three times: a short launch list for ncu."""
+    import numpy as np
+    import torch
+
+    from diffusionhard_b200.final_head import ConditionedHead
+
+    B, L, V, C = args.batch, 1024, 50258, 128
+    g = torch.Generator().manual_seed(0)
+    masked = torch.rand((B, L), generator=g) < 0.5
+    gd = torch.Generator(device="cuda").manual_seed(0)
+    hidden = torch.randn((B, L, 768), device="cuda", generator=gd).to(torch.bfloat16)
+    cond = torch.randn((B, C), device="cuda", generator=gd)
+    rng = np.random.default_rng(0)
+    ada_w = (rng.standard_normal((1536, C)) * 0.02).astype(np.float32)
+    w = np.clip(np.round(rng.normal(0, 40, (V, 768))), -127, 127).astype(np.int8)
+    w_scale = rng.uniform(0.5e-3, 2e-3, V).astype(np.float32)
+    bias = (rng.standard_normal(V) * 0.02).astype(np.float32)
+    head = ConditionedHead(w, w_scale, bias, ada_w, None, None, V - 1, B, L)
+    for _ in range(3):
+        head.load_mask(masked.cuda())
+        head.enqueue(hidden, cond, seed=0)
+    torch.cuda.synchronize()
+    print("profile-head done:", int(head.sel_count.item()), "masked rows", flush=True)
+
+
 def run_vocab_shard(args, world: int, rank: int) -> None:
     """Single-sequence latency: every rank runs the same backbone forward and
     projects its slice of the head; the packed (score, ~id) words are
@@ -670,6 +698,9 @@ def main() -> None:
     ap.add_argument("--profile-forward", action="store_true",
                     help="run one warm-up forward, then one forward + one head call "
                          "(a short launch list for ncu)")
+    ap.add_argument("--profile-head", action="store_true",
+                    help="run the conditioned head pipeline of the head microbench three times on "
+                         "--batch x 1024 canvases (a short launch list for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -694,6 +725,9 @@ def main() -> None:
     peaks, peaks_kind = load_peaks()
     if args.profile_forward:
         profile_forward(args)
+        return
+    if args.profile_head:
+        profile_head(args)
         return
     if args.vocab_shard:
         run_vocab_shard(args, world, rank)
