@@ -245,7 +245,8 @@ def strong_sweep(qm, world: int, rank: int, global_batch: int = 512, steps: int 
             "model_evaluations": meta["model_evaluations"]}
 
 
-def vocab_shard_latency(qm, world: int, rank: int, steps: int = 64, warmup: int = 3, iters: int = 3) -> dict:
+def vocab_shard_latency(qm, world: int, rank: int, steps: int = 64, warmup: int = 3, iters: int = 3,
+                        graph: bool = True) -> dict:
     """Single-sequence latency with the head split over the ranks and merged
     by dh_vocab_shard_reduce (NCCL all-reduce of the packed per-row words)
     after every head launch; beside it, the time of that all-reduce alone
@@ -265,13 +266,13 @@ def vocab_shard_latency(qm, world: int, rank: int, steps: int = 64, warmup: int 
         eng.shard_head(v0, v1, group=dist.group.WORLD)
     ids = torch.full((1, L), qm.config.mask_token_id, dtype=torch.int64, device="cuda")
     for _ in range(warmup):
-        eng.generate(ids, steps=steps, seed=0, graph=False)
+        eng.generate(ids, steps=steps, seed=0, graph=graph)
     torch.cuda.synchronize()
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(iters):
-        eng.generate(ids, steps=steps, seed=0, graph=False)
+        eng.generate(ids, steps=steps, seed=0, graph=graph)
     e.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e), world) / iters
@@ -298,12 +299,14 @@ def vocab_shard_latency(qm, world: int, rank: int, steps: int = 64, warmup: int 
         torch.cuda.synchronize()
         reduce_us = max_over_ranks(s.elapsed_time(e), world) / n * 1e3
     meta = eng.metadata(steps)
+    eng._graphs.clear()  # graphs holding NCCL calls go before the process group does
     del eng
     torch.cuda.empty_cache()
     out = {"value": round(L / (ms * 1e-3), 1), "unit": "tok/s", "ms_per_generation": round(ms, 3),
            "n_gpus": world, "head_split": world, "seq_len": L, "steps": steps,
            "model_evaluations": meta["model_evaluations"], "ranks_agree_on_tokens": agree,
-           "loop": "dh_sample_loop, eager launches (no graph)"}
+           "loop": "dh_sample_loop" + (" in a CUDA graph (the all-reduce captured with it)" if graph else
+                                       ", eager launches")}
     if reduce_us is not None:
         transitions = steps + 1
         out["allreduce_us_per_transition"] = round(reduce_us, 2)
@@ -503,13 +506,13 @@ def run_vocab_shard(args, world: int, rank: int) -> None:
         eng.shard_head(v0, v1, group=dist.group.WORLD)
     ids = torch.full((1, L), cfg.mask_token_id, dtype=torch.int64, device="cuda")
     for _ in range(args.warmup):
-        eng.generate(ids, steps=S, seed=0, graph=False)
+        eng.generate(ids, steps=S, seed=0, graph=True)
     torch.cuda.synchronize()
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
-        eng.generate(ids, steps=S, seed=0, graph=False)
+        eng.generate(ids, steps=S, seed=0, graph=True)
     end.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(end), world)
@@ -534,6 +537,7 @@ def run_vocab_shard(args, world: int, rank: int) -> None:
                        "steps": S, "parallelism": f"vocab{world}"},
             "ranks_agree_on_tokens": consistent,
             "model_evaluations": eng.metadata(S)["model_evaluations"]}), flush=True)
+    eng._graphs.clear()  # graphs holding NCCL calls go before the process group does
     if world > 1:
         import torch.distributed as dist
 
