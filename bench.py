@@ -421,6 +421,16 @@ def head_microbench(qm, peaks: dict, peaks_kind: str, int8: dict) -> dict:
                   _lib.stream_handle())
 
     head_ms = time_kernel(head_only, iters=10)
+    # the head's noise alone over the same rows, vocabulary and Philox keys,
+    # on every SM with nothing else to compute: the integer-pipe floor
+    packed_n = torch.zeros(rows, dtype=torch.int64, device="cuda")
+
+    def noise_only():
+        packed_n.zero_()
+        _lib.call("dh_noise_argmax", rows, V, qm.config.mask_token_id, p(head.sel_pos), p(head.sel_key),
+                  p(head.sel_eval), 0, 0, 0, 0, p(packed_n), None, _lib.stream_handle())
+
+    noise_ms = time_kernel(noise_only, iters=10)
     ops = 2.0 * rows * V * 768
     ach = ops / (head_ms * 1e-3) / 1e12
     return {"workload": "64 x 1024 bf16 hidden, 50% masked (Bernoulli, seed 0), adaLN final LayerNorm + per-token "
@@ -429,6 +439,10 @@ def head_microbench(qm, peaks: dict, peaks_kind: str, int8: dict) -> dict:
             "prologue_ms": round(ms - head_ms, 4), "rows_per_s": round(rows / (ms * 1e-3), 1),
             "achieved_top_s": round(ach, 1), "int8_peak_top_s": int8["tops"],
             "tensor_frac": round(ach / int8["tops"], 4),
+            "integer_roofline": {"noise_only_ms": round(noise_ms, 4), "frac": round(noise_ms / head_ms, 4),
+                                 "how": "dh_noise_argmax over the same rows x vocabulary and Philox keys (the "
+                                        "head's Philox-4x32-10 / Gumbel Q10 race with zero logits, all SMs, no "
+                                        "GEMM) over the fused head's time"},
             "note": "per logit: 1/4 of a Philox4x32-10 block, the Gumbel Q10 lookup, the exact fp64 dequant and "
                     "the Q10 rounding on the integer / fp64 pipes; see profiles/ for the pipe utilisation"}
 

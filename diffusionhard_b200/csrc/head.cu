@@ -145,10 +145,12 @@ DH_DEVINL Philox4 philox_row_block(uint32_t c0, const PhiloxRow& pr, uint32_t ke
 }
 
 // gumbel_q10 with the mantissa taken from d normalised to bit 31 (one
-// variable shift instead of two shift directions): same table index.
+// variable shift instead of two shift directions): same table index.  The
+// lookup happens before the d == 0 select, so e is kept to 0..31 (clz of 0
+// is 32, whose row lies past the 32 x 256 table).
 DH_DEVINL int32_t gumbel_q10_norm(uint32_t word, const int16_t* smem_table) {
     const uint32_t d = ~word;
-    const uint32_t e = __clz(d);
+    const uint32_t e = __clz(d) & 31u;
     const uint32_t m = ((d << e) >> 23) & 0xFFu;
     const int32_t v = smem_table[(e << 8) | m];
     return d == 0u ? DH_GUMBEL_TOP_Q10 : v;
@@ -380,12 +382,108 @@ uint32_t launch_head(const int8_t* hidden, uint64_t ld_hidden, const int8_t* wei
     return DH_OK;
 }
 
+// The head's noise path alone: the (score, lowest id) race of the Philox /
+// Gumbel Q10 noise over rows x vocab with every logit zero -- the same
+// counters, key, words, table lookup and tie rule as the fused head, and no
+// GEMM, dequantisation or logit.  One thread per (row, segment of
+// kNoiseSeg tokens), all SMs full; per-segment winners merge with one
+// 64-bit atomicMax per thread into `packed` (zero-initialised).  Its time
+// over the head's rows and vocabulary is what generating the noise costs
+// with nothing else competing for the integer pipes.
+constexpr uint32_t kNoiseSeg = 512;
+
+__global__ void __launch_bounds__(256)
+noise_argmax_kernel(uint32_t rows, uint32_t vocab, uint32_t mask_id, const uint32_t* __restrict__ row_position,
+                    const uint32_t* __restrict__ row_key_hi, const uint32_t* __restrict__ row_eval,
+                    uint32_t const_eval, uint32_t const_key_hi, uint32_t key_lo, uint32_t stream_id,
+                    unsigned long long* __restrict__ packed) {
+    __shared__ int16_t table[32 * 256];
+    load_gumbel_table(table);
+    __syncthreads();
+    const uint32_t segs = (vocab + kNoiseSeg - 1) / kNoiseSeg;
+    const uint64_t work = static_cast<uint64_t>(rows) * segs;
+    for (uint64_t t = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; t < work;
+         t += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t row = static_cast<uint32_t>(t / segs);
+        const uint32_t s0 = static_cast<uint32_t>(t % segs) * kNoiseSeg;
+        const uint32_t end = min(vocab, s0 + kNoiseSeg);
+        const uint32_t key_hi = row_key_hi ? row_key_hi[row] : const_key_hi;
+        const PhiloxRow pr = philox_row(row_position ? row_position[row] : row, row_eval ? row_eval[row] : const_eval,
+                                        stream_id, key_lo, key_hi);
+        int32_t best_s = INT32_MIN;
+        uint32_t best_id = 0;
+#pragma unroll 1
+        for (uint32_t v0 = s0; v0 < end; v0 += 8) {
+            uint32_t wd[8];
+#pragma unroll
+            for (uint32_t g = 0; g < 2; ++g) {
+                const Philox4 r = philox_row_block((v0 >> 2) + g, pr, key_lo, key_hi);
+                wd[4 * g] = r.x;
+                wd[4 * g + 1] = r.y;
+                wd[4 * g + 2] = r.z;
+                wd[4 * g + 3] = r.w;
+            }
+            int32_t sc[8];
+            uint32_t ix[8];
+#pragma unroll
+            for (uint32_t j = 0; j < 8; ++j) {
+                const uint32_t id = v0 + j;
+                sc[j] = (id < end && id != mask_id) ? gumbel_q10_norm(wd[j], table) : INT32_MIN;
+                ix[j] = id;
+            }
+            // tree over the 8 columns, the lower id winning ties
+#pragma unroll
+            for (uint32_t stride = 1; stride < 8; stride <<= 1) {
+#pragma unroll
+                for (uint32_t j = 0; j < 8; j += 2 * stride) {
+                    const bool right = sc[j + stride] > sc[j];
+                    sc[j] = right ? sc[j + stride] : sc[j];
+                    ix[j] = right ? ix[j + stride] : ix[j];
+                }
+            }
+            if (sc[0] > best_s) {
+                best_s = sc[0];
+                best_id = ix[0];
+            }
+        }
+        if (best_s != INT32_MIN) atomicMax(packed + row, pack_score_id(best_s, best_id));
+    }
+}
+
 }  // namespace
 }  // namespace dh
 
 using namespace dh;
 
 extern "C" {
+
+uint32_t dh_noise_argmax(uint32_t rows, uint32_t vocabulary_size, uint32_t mask_token_id,
+                         const uint32_t* row_position, const uint32_t* row_key_hi, const uint32_t* row_eval,
+                         uint32_t const_eval, uint32_t const_key_hi, uint32_t key_lo, uint32_t stream_id,
+                         uint64_t* packed, int32_t* out_ids, void* stream) {
+    if (rows == 0) return DH_RNG_INVALID_POSITION_COUNT;
+    if (vocabulary_size == 0 || vocabulary_size > 65535 || mask_token_id >= vocabulary_size)
+        return DH_RNG_INVALID_VOCABULARY_SIZE;
+    if (!packed) return DH_ERR_NULL_POINTER;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int sms = kNumSMs, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    }
+    const uint64_t work = static_cast<uint64_t>(rows) * ((vocabulary_size + kNoiseSeg - 1) / kNoiseSeg);
+    const uint32_t blocks = static_cast<uint32_t>(std::min<uint64_t>((work + 255) / 256, 8ull * sms));
+    noise_argmax_kernel<<<blocks, 256, 0, st>>>(rows, vocabulary_size, mask_token_id, row_position, row_key_hi,
+                                               row_eval, const_eval, const_key_hi, key_lo, stream_id,
+                                               reinterpret_cast<unsigned long long*>(packed));
+    DH_LAUNCH_CHECK();
+    if (out_ids) {
+        head_finalize_kernel<<<std::min<uint32_t>((rows + 255) / 256, 1024u), 256, 0, st>>>(
+            reinterpret_cast<unsigned long long*>(packed), rows, nullptr, 0u, out_ids, nullptr, nullptr);
+        DH_LAUNCH_CHECK();
+    }
+    return DH_OK;
+}
 
 uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_t* weights,
                            uint64_t ld_weights, uint32_t rows, const uint32_t* rows_count,

@@ -488,6 +488,19 @@ uint32_t dh_head_argmax_i8(const int8_t* hidden, uint64_t ld_hidden, const int8_
                            uint32_t const_eval, uint32_t key_lo, uint32_t stream_id,
                            uint64_t* packed, int32_t* out_ids, int32_t* out_scores, void* stream);
 
+/* The noise half of dh_head_argmax_i8 alone: per row, the (score, lowest id)
+ * race of the Philox / Gumbel Q10 noise with every logit zero (the same
+ * counters, key, table and tie rule; mask token skipped), merged into
+ * packed[row] (zero on entry) and, if given, out_ids.  Equals
+ * dh_noisy_argmax_f32 of all-zero logits.  With no GEMM or logit to compute,
+ * its time over the head's rows and vocabulary is the cost of the noise with
+ * the integer pipes to itself: the floor of the fused head on the SMs'
+ * integer units.  Status: RNG family codes, then DH_ERR_*. */
+uint32_t dh_noise_argmax(uint32_t rows, uint32_t vocabulary_size, uint32_t mask_token_id,
+                         const uint32_t* row_position, const uint32_t* row_key_hi, const uint32_t* row_eval,
+                         uint32_t const_eval, uint32_t const_key_hi, uint32_t key_lo, uint32_t stream_id,
+                         uint64_t* packed, int32_t* out_ids, void* stream);
+
 /* Mirror of output_head_int8_kernel (output_head.cpp:23-157): same arguments,
  * limits and status codes (1 <= positions <= 64, 1 <= hidden <= 768,
  * 1 <= vocab <= 65535, mask < vocab); `noise` is the [positions, vocab] race

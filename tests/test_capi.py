@@ -62,3 +62,12 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
         monkeypatch.undo()
         _lib.lib.cache_clear()
         _lib.lib()
+
+
+def test_noise_argmax_status_codes():
+    # RNG family first (row count, vocabulary / mask), then the null sink
+    assert _lib.raw("dh_noise_argmax", 0, 10, 0, None, None, None, 0, 0, 0, 0, None, None, None) == 1
+    assert _lib.raw("dh_noise_argmax", 1, 0, 0, None, None, None, 0, 0, 0, 0, None, None, None) == 2
+    assert _lib.raw("dh_noise_argmax", 1, 65536, 0, None, None, None, 0, 0, 0, 0, None, None, None) == 2
+    assert _lib.raw("dh_noise_argmax", 1, 10, 10, None, None, None, 0, 0, 0, 0, None, None, None) == 2
+    assert _lib.raw("dh_noise_argmax", 1, 10, 9, None, None, None, 0, 0, 0, 0, None, None, None) == 100

@@ -217,3 +217,37 @@ def test_candidate_cache_loop_bit_exact_per_step(cuda, positions, vocab, steps):
     assert meta["model_evaluations"] == o["evaluations"]
     assert mask not in ids.cpu().numpy().tolist()
     assert meta["hardware_candidate_cache_bytes"] == positions * 2 + 2 * (positions // 8)
+
+
+@pytest.mark.parametrize("rows,vocab,mask", [(64, 50258, 50257), (3, 19, 18), (2, 1, 0), (300, 1000, 3),
+                                             (7, 513, 512), (5, 1024, 0)])
+def test_noise_only_argmax_is_the_race_over_zero_logits(cuda, rows, vocab, mask):
+    """dh_noise_argmax: the head's noise race with every logit zero equals
+    the oracle's noisy argmax of an all-zero logit matrix, ids and scores."""
+    torch = cuda
+    rng = np.random.default_rng(rows + vocab)
+    pos = rng.integers(0, 1024, rows)
+    khi = rng.integers(0, 512, rows)
+    ev = rng.integers(0, 64, rows)
+    zeros = np.zeros((rows, vocab), np.float32)
+    oids, oscores = pyoracle.noisy_argmax_f32(zeros, mask, pos, khi, ev, key_lo=11, stream_id=2)
+    arr = lambda a: _dev(torch, np.asarray(a, np.uint32).view(np.int32))  # noqa: E731
+    packed = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    ids = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
+    p_, k_, e_ = arr(pos), arr(khi), arr(ev)
+    _lib.call("dh_noise_argmax", rows, vocab, mask, _lib.ptr(p_), _lib.ptr(k_), _lib.ptr(e_), 0, 0, 11, 2,
+              _lib.ptr(packed), _lib.ptr(ids), None)
+    torch.cuda.synchronize()
+    assert np.array_equal(ids.cpu().numpy(), oids)
+    if vocab > 1:
+        got = packed.cpu().numpy().view(np.uint64)
+        score = ((got >> np.uint64(32)).astype(np.uint32) ^ np.uint32(0x80000000)).view(np.int32)
+        assert np.array_equal(score, oscores)
+    # constant key / evaluation instead of per-row arrays
+    packed.zero_()
+    _lib.call("dh_noise_argmax", rows, vocab, mask, None, None, None, 9, 5, 11, 2, _lib.ptr(packed),
+              _lib.ptr(ids), None)
+    torch.cuda.synchronize()
+    cids, _ = pyoracle.noisy_argmax_f32(zeros, mask, None, np.full(rows, 5), np.full(rows, 9), key_lo=11,
+                                        stream_id=2)
+    assert np.array_equal(ids.cpu().numpy(), cids)
