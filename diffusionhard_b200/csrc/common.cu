@@ -41,8 +41,25 @@ __global__ void wait_selftest_kernel(uint32_t spin_limit, uint32_t arrive, uint3
     *completed = ok ? 1u : 0u;
 }
 
+__global__ void wait_suspend_selftest_kernel(uint64_t limit_ns, uint32_t arrive, uint32_t* completed) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+    if (arrive) tc::mbar_arrive(&bar);
+    *completed = tc::mbar_wait_suspend(&bar, 0, tc::kErrTimeoutFull, limit_ns) ? 1u : 0u;
+}
+
 }  // namespace
 }  // namespace dh
+
+extern "C" uint32_t dh_wait_suspend_selftest(uint64_t limit_ns, uint32_t arrive, uint32_t* completed, void* stream) {
+    if (!completed) return DH_ERR_NULL_POINTER;
+    if (limit_ns == 0 || limit_ns > dh::tc::kWaitLimitNs) return DH_ERR_INVALID_ARGUMENT;
+    dh::wait_suspend_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, arrive, completed);
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
 
 extern "C" uint32_t dh_wait_selftest(uint32_t spin_limit, uint32_t arrive, uint32_t* completed, void* stream) {
     if (!completed) return DH_ERR_NULL_POINTER;

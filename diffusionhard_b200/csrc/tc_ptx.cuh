@@ -58,6 +58,46 @@ DH_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Wall-clock bound of the suspending waits below.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+DH_DEVINL uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended until it completes (or 1 ms passes) instead of returning at once
+// to poll again.
+DH_DEVINL bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for pipelines whose waiting threads share schedulers with the
+// threads doing the work: the waiter sleeps instead of taking issue slots.
+// Gives up (records `code`, returns false) after limit_ns of wall time.
+DH_DEVINL bool mbar_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t code,
+                                 uint64_t limit_ns = kWaitLimitNs) {
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            report_error(code);
+            return false;
+        }
+    }
+}
+
 // Bounded wait: returns false (and records `code`) when the spin limit expires.
 DH_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t code) {
     for (uint32_t i = 0; i < kSpinLimit; ++i)

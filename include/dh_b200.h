@@ -657,6 +657,12 @@ uint32_t dh_device_error(uint32_t* out, uint32_t clear);
  * HLS kernels report status codes but have no device waits. */
 uint32_t dh_wait_selftest(uint32_t spin_limit, uint32_t arrive, uint32_t* completed, void* stream);
 
+/* The same check for the suspending waits (the attention kernel's): the
+ * waiting thread sleeps on the mbarrier and gives up after limit_ns
+ * nanoseconds of wall time (1 <= limit_ns <= 2e9, the kernels' own bound),
+ * with the same error word and *completed as dh_wait_selftest. */
+uint32_t dh_wait_suspend_selftest(uint64_t limit_ns, uint32_t arrive, uint32_t* completed, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

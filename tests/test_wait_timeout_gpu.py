@@ -2,7 +2,8 @@
 never complete (nothing arrives) gives up after its poll limit, records the
 expired-wait code in the device error word and returns; the host reads it
 (DHDeviceError) and the context stays usable.  The same give-up path bounds
-every pipeline wait of the GEMM, attention and head kernels."""
+every pipeline wait of the GEMM and head kernels; the attention kernel's
+suspending waits give up after a wall-time limit, checked the same way."""
 
 import pytest
 
@@ -33,9 +34,38 @@ def test_expired_wait_is_reported_and_the_context_survives(cuda):
     _lib.check_device_error()
 
 
+def test_expired_suspending_wait_is_reported(cuda):
+    """The attention kernel's waits sleep on the mbarrier and are bounded by
+    wall time: a wait nothing completes gives up after its limit (here 20 ms)
+    with the same code, and a completed one returns at once."""
+    torch = cuda
+    import time
+
+    from diffusionhard_b200 import _lib
+
+    _lib.check_device_error()
+    done = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    _lib.call("dh_wait_suspend_selftest", 20_000_000, 1, done.data_ptr(), None)
+    assert int(done.item()) == 1
+    _lib.check_device_error()
+    t0 = time.perf_counter()
+    _lib.call("dh_wait_suspend_selftest", 20_000_000, 0, done.data_ptr(), None)
+    assert int(done.item()) == 0
+    assert time.perf_counter() - t0 >= 0.02
+    with pytest.raises(_lib.DHDeviceError) as err:
+        _lib.check_device_error()
+    assert err.value.code == 1
+    _lib.call("dh_wait_suspend_selftest", 20_000_000, 1, done.data_ptr(), None)
+    assert int(done.item()) == 1
+    _lib.check_device_error()
+
+
 def test_selftest_argument_checks(cuda):
     from diffusionhard_b200 import _lib
 
     assert _lib.raw("dh_wait_selftest", 4096, 1, None, None) == 100
     assert _lib.raw("dh_wait_selftest", 0, 1, 16, None) == 105
     assert _lib.raw("dh_wait_selftest", (1 << 16) + 1, 1, 16, None) == 105
+    assert _lib.raw("dh_wait_suspend_selftest", 1000, 1, None, None) == 100
+    assert _lib.raw("dh_wait_suspend_selftest", 0, 1, 16, None) == 105
+    assert _lib.raw("dh_wait_suspend_selftest", 2_000_000_001, 1, 16, None) == 105
