@@ -183,11 +183,22 @@ def measure_int8_peak() -> dict:
 # Algorithmic work of one forward, per row (SURVEY-style units of the MDLM
 # specification, model_spec.py:29-84): backbone int8 ops, attention FLOP per
 # key, and the bytes the memory-bound row kernels must move.
-BACKBONE_OPS_PER_ROW = 2 * 12 * (768 * 2304 + 768 * 768 + 2 * 768 * 3072)  # 169,869,312
+# The forward runs every block over every row up to the last block's
+# attention; the rest of the last block (attention-out, MLP, their
+# quantisers) runs only for the rows whose candidates are drawn (the head's
+# rows), which is all the head reads.
+QKV_OPS_PER_ROW = 2 * 768 * 2304
+POST_ATTN_OPS_PER_ROW = 2 * (768 * 768 + 2 * 768 * 3072)
+BACKBONE_OPS_PER_ROW = 11 * (QKV_OPS_PER_ROW + POST_ATTN_OPS_PER_ROW) + QKV_OPS_PER_ROW  # 159,252,480
 ATTN_FLOP_PER_ROW_PER_KEY = 36864
-HEAD_OPS_PER_ROW = 2 * 768 * 50258  # 77,196,288
-STREAM_BYTES_PER_ROW = (12 * (2 * (768 * 4 + 768 + 4) + (768 * 2 + 768 + 4) + (3072 * 2 + 3072 + 4))
-                        + (768 * 4 * 2 + 4))
+HEAD_OPS_PER_ROW = 2 * 768 * 50258 + POST_ATTN_OPS_PER_ROW  # 87,813,120
+LN_BYTES = 768 * 4 + 768 + 4
+Q768_BYTES = 768 * 2 + 768 + 4
+Q3072_BYTES = 3072 * 2 + 3072 + 4
+STREAM_BYTES_PER_ROW = 11 * (2 * LN_BYTES + Q768_BYTES + Q3072_BYTES) + LN_BYTES + (768 * 4 * 2 + 4)
+# per head row: the last block's LayerNorm and quantisers, the final
+# LayerNorm, and the gather of its residual row and attention output
+HEAD_STREAM_BYTES_PER_ROW = 2 * LN_BYTES + Q768_BYTES + Q3072_BYTES + 768 * 4 * 2 + 768 * 2 * 2
 
 
 def step_roofline(ms_per_generation: float, rows: int, kv_len: int, evaluations: int, head_rows: int,
@@ -198,7 +209,7 @@ def step_roofline(ms_per_generation: float, rows: int, kv_len: int, evaluations:
     the measured time."""
     int8_ops = evaluations * rows * BACKBONE_OPS_PER_ROW + head_rows * HEAD_OPS_PER_ROW
     bf16_flop = evaluations * rows * ATTN_FLOP_PER_ROW_PER_KEY * kv_len
-    stream = evaluations * rows * STREAM_BYTES_PER_ROW
+    stream = evaluations * rows * STREAM_BYTES_PER_ROW + head_rows * HEAD_STREAM_BYTES_PER_ROW
     t = {"int8": int8_ops / (int8_tops * 1e12), "bf16": bf16_flop / (bf16_tflops * 1e12),
          "hbm": stream / (hbm_gbs * 1e9)}
     ideal_ms = sum(t.values()) * 1e3
@@ -347,6 +358,23 @@ def kernel_breakdown(eng) -> dict:
                                         p(down.w_scale), p(down.bias), p(eng.x), M, 768, 3072, None, s),
     }
     return {name: time_kernel(fn) for name, fn in fns.items()}
+
+
+# The kernels that finish the last block run over the head's rows only (a
+# few hundred of the 32,768 per evaluation): per forward, the full-size
+# launches of kernel_breakdown are those of the other blocks.
+LAST_BLOCK_ROWS_ONLY = ("quant_rows_768", "gemm_out_residual", "gemm_up_gelu", "quant_rows_3072",
+                        "gemm_down_residual")
+
+
+def launches_per_forward(name: str, blocks: int) -> int:
+    if name == "embed_gather":
+        return 1
+    if name == "ln_smooth_quant":
+        return 2 * blocks - 1
+    if name in LAST_BLOCK_ROWS_ONLY:
+        return blocks - 1
+    return blocks
 
 
 def roofline_for(name: str, ms: float, eng, peaks: dict, peaks_kind: str, int8: dict) -> dict:
@@ -812,8 +840,7 @@ def main() -> None:
     # ------------------------------------------------ kernel breakdown / roofline
     int8 = measure_int8_peak()
     bd = kernel_breakdown(eng)
-    per_gen = {k: v * (1 if k == "embed_gather" else (len(eng.blocks) * (2 if k == "ln_smooth_quant" else 1)))
-               for k, v in bd.items()}
+    per_gen = {k: v * launches_per_forward(k, len(eng.blocks)) for k, v in bd.items()}
     dominant = max(per_gen, key=per_gen.get)
     roof = roofline_for(dominant, bd[dominant], eng, peaks, peaks_kind, int8)
     traffic_file = ROOT / "profiles" / "traffic.json"

@@ -41,7 +41,7 @@ inline size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255);
 // loop adds the residual stream, the head input and the loop state.
 struct Layout {
     size_t act_q, act_scale, q, k, vt, attn, mlp, row_amax, fwd_end;
-    size_t x, head_q, head_scale, packed, active, need_eval, eval_id, fwd_rows, sel_count;
+    size_t x, xs, head_q, head_scale, packed, active, need_eval, eval_id, fwd_rows, sel_count;
     size_t sel_rows, sel_pos, sel_key, sel_eval, seq_list, head_all, head_all_scale, loop_end;
 };
 
@@ -65,6 +65,7 @@ Layout layout(uint32_t B, uint32_t L) {
     o.row_amax = take(M * 4);
     o.fwd_end = at;
     o.x = take(M * kHidden * 4);
+    o.xs = take(M * kHidden * 4);
     o.head_q = take(M * kHidden);
     o.head_scale = take(M * 4);
     o.packed = take(M * 8);
@@ -130,7 +131,7 @@ T* at(void* base, size_t off) {
 // listed sequences of `tokens` (the sequences that need a forward).
 uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32_t B, uint32_t L, float* x,
                          void* ws, const Layout& o, const uint32_t* run_rows, void* s,
-                         const uint32_t* seq_list = nullptr) {
+                         const uint32_t* seq_list = nullptr, bool stop_at_last_attention = false) {
     const uint32_t M = B * L;
     int8_t* act_q = at<int8_t>(ws, o.act_q);
     float* act_scale = at<float>(ws, o.act_scale);
@@ -153,6 +154,10 @@ uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32
         DH_TRY(dh_gemm_qkv_rope(act_q, act_scale, qkv.weight, qkv.w_scale, qkv.bias, w->rope_cos, w->rope_sin,
                                 out.inv_smooth, M, L, 0, L, 0, q, k, vt, run_rows, s));
         DH_TRY(dh_attention(q, k, vt, attn, B, L, L, L, run_rows, s));
+        // the loop finishes the last block for the revealed rows only
+        // (enqueue_last_block_rows): x keeps the input of the last block and
+        // attn its attention output, for every row
+        if (stop_at_last_attention && i + 1 == w->blocks) break;
         DH_TRY(dh_quant_rows_bf16(attn, nullptr, nullptr, act_q, act_scale, M, kHidden, run_rows, s));
         DH_TRY(dh_gemm_residual(act_q, act_scale, out.weight, out.w_scale, out.bias, x, M, kHidden, kHidden,
                                 run_rows, s));
@@ -163,6 +168,46 @@ uint32_t enqueue_forward(const dh_mdlm_weights* w, const int32_t* tokens, uint32
         DH_TRY(dh_gemm_residual(act_q, act_scale, down.weight, down.w_scale, down.bias, x, M, kHidden, kMlp,
                                 run_rows, s));
     }
+    return DH_OK;
+}
+
+// The rest of the last block (requant, attention-out + residual, LayerNorm,
+// MLP + residual) and the final LayerNorm + head quantisation, for the
+// *sel_count rows listed in sel_rows only: the head reads nothing else, and
+// every one of these steps is row-wise, so the rows get the bits the whole-
+// batch block would give them.  Inputs: x = the residual stream entering
+// the last block and attn = its attention output, both for every row (the
+// last forward's, also when this transition ran none).  The rows are
+// gathered into xs and q (free after the attention); head_q / head_scale
+// receive the head's int8 input rows 0 .. *sel_count.
+uint32_t enqueue_last_block_rows(const dh_mdlm_weights* w, uint32_t B, uint32_t L, void* ws, const Layout& o,
+                                 const uint32_t* sel_rows, const uint32_t* sel_count, void* s) {
+    const uint32_t M = B * L;
+    const uint32_t i = w->blocks - 1;
+    const dh_linear_weights& out = w->block_linears[4 * i + 1];
+    const dh_linear_weights& up = w->block_linears[4 * i + 2];
+    const dh_linear_weights& down = w->block_linears[4 * i + 3];
+    const float* x = at<float>(ws, o.x);
+    float* xs = at<float>(ws, o.xs);
+    const void* attn = at<void>(ws, o.attn);
+    void* attn_rows = at<void>(ws, o.q);
+    int8_t* act_q = at<int8_t>(ws, o.act_q);
+    float* act_scale = at<float>(ws, o.act_scale);
+    void* mlp = at<void>(ws, o.mlp);
+    uint32_t* row_amax = at<uint32_t>(ws, o.row_amax);
+    DH_TRY(dh_gather_rows(x, kHidden * 4, sel_rows, sel_count, M, xs, s));
+    DH_TRY(dh_gather_rows(attn, kHidden * 2, sel_rows, sel_count, M, attn_rows, s));
+    DH_TRY(dh_quant_rows_bf16(attn_rows, nullptr, nullptr, act_q, act_scale, M, kHidden, sel_count, s));
+    DH_TRY(dh_gemm_residual(act_q, act_scale, out.weight, out.w_scale, out.bias, xs, M, kHidden, kHidden, sel_count,
+                            s));
+    DH_TRY(dh_ln_smooth_quant(xs, up.smooth, up.inv_smooth, act_q, act_scale, M, nullptr, nullptr, sel_count, s));
+    DH_TRY(dh_gemm_gelu(act_q, act_scale, up.weight, up.w_scale, up.bias, down.inv_smooth, mlp, row_amax, M, kMlp,
+                        kHidden, sel_count, s));
+    DH_TRY(dh_quant_rows_bf16_amax(mlp, row_amax, act_q, act_scale, M, kMlp, sel_count, s));
+    DH_TRY(dh_gemm_residual(act_q, act_scale, down.weight, down.w_scale, down.bias, xs, M, kHidden, kMlp, sel_count,
+                            s));
+    DH_TRY(dh_ln_smooth_quant(xs, w->head.smooth, w->head.inv_smooth, at<int8_t>(ws, o.head_q),
+                              at<float>(ws, o.head_scale), M, nullptr, nullptr, sel_count, s));
     return DH_OK;
 }
 
@@ -272,7 +317,7 @@ uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids
         const uint32_t k = final_pass ? steps - 1 : t;
         DH_TRY(dh_loop_plan_seqs(B, L, k, steps, final_pass, active, need_eval, eval_id, fwd_rows, sel_count,
                                  counters, seq_list, s));
-        DH_TRY(enqueue_forward(w, tokens, B, L, x, workspace, o, fwd_rows, s, seq_list));
+        DH_TRY(enqueue_forward(w, tokens, B, L, x, workspace, o, fwd_rows, s, seq_list, seq_list == nullptr));
         if (seq_list)  // every refilled row's head input, kept per sequence until its next forward
             DH_TRY(dh_ln_smooth_quant_scatter(x, w->head.smooth, w->head.inv_smooth, head_all, head_all_scale, M,
                                               seq_list, L, fwd_rows, s));
@@ -281,8 +326,7 @@ uint32_t dh_sample_loop(const dh_mdlm_weights* weights, const int32_t* input_ids
         if (seq_list)
             DH_TRY(dh_gather_rows_i8(head_all, head_all_scale, sel_rows, sel_count, M, head_q, head_scale, s));
         else
-            DH_TRY(dh_ln_smooth_quant(x, w->head.smooth, w->head.inv_smooth, head_q, head_scale, M, sel_rows,
-                                      sel_count, nullptr, s));
+            DH_TRY(enqueue_last_block_rows(w, B, L, workspace, o, sel_rows, sel_count, s));
         DH_TRY(dh_head_argmax_i8(head_q, kHidden, w->head.weight, kHidden, M, sel_count, kHidden, w->head_rows,
                                  w->head_vocab_offset, w->mask_token_id, final_pass ? 2u : 1u, head_scale,
                                  w->head.w_scale, w->head.bias, nullptr, nullptr, nullptr, sel_pos, sel_key, sel_eval,

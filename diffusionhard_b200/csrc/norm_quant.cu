@@ -312,6 +312,29 @@ uint32_t dh_gather_rows_i8(const int8_t* src, const float* src_scale, const uint
     return DH_OK;
 }
 
+// dst row i = src row rows_index[i]: one warp per row, 16-byte vectors.
+__global__ void gather_rows_kernel(const uint4* __restrict__ src, uint32_t row_vecs,
+                                   const uint32_t* __restrict__ rows_index, const uint32_t* __restrict__ rows_count,
+                                   uint32_t rows, uint4* __restrict__ dst) {
+    const uint32_t i = blockIdx.x * (blockDim.x / 32) + warp_id();
+    if (i >= min(rows, *rows_count)) return;
+    const uint4* s = src + static_cast<uint64_t>(rows_index[i]) * row_vecs;
+    uint4* d = dst + static_cast<uint64_t>(i) * row_vecs;
+    for (uint32_t j = lane_id(); j < row_vecs; j += 32) d[j] = s[j];
+}
+
+uint32_t dh_gather_rows(const void* src, uint32_t row_bytes, const uint32_t* rows_index, const uint32_t* rows_count,
+                        uint32_t rows, void* dst, void* stream) {
+    if (!src || !rows_index || !rows_count || !dst) return DH_ERR_NULL_POINTER;
+    if (rows == 0) return DH_OK;
+    if (row_bytes == 0 || row_bytes % 16 != 0) return DH_ERR_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) return DH_ERR_ALIGNMENT;
+    gather_rows_kernel<<<(rows + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(src), row_bytes / 16, rows_index, rows_count, rows, static_cast<uint4*>(dst));
+    DH_LAUNCH_CHECK();
+    return DH_OK;
+}
+
 uint32_t dh_quant_rows_bf16(const void* in, const float* smooth, const float* inv_smooth, int8_t* out, float* scale,
                             uint32_t rows, uint32_t cols, const uint32_t* run_flag, void* stream) {
     if (!in || !out || !scale) return DH_ERR_NULL_POINTER;

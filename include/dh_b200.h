@@ -374,6 +374,13 @@ uint32_t dh_ln_smooth_quant_scatter(const float* x, const float* smooth, const f
 uint32_t dh_gather_rows_i8(const int8_t* src, const float* src_scale, const uint32_t* rows_index,
                            const uint32_t* rows_count, uint32_t rows, int8_t* dst, float* dst_scale, void* stream);
 
+/* dst row i = src row rows_index[i] for i < min(rows, *rows_count): rows of
+ * row_bytes bytes (a multiple of 16; both buffers 16-byte aligned).  The
+ * revealed rows' residual stream and attention output, gathered for the
+ * last block, which the loop computes for those rows only. */
+uint32_t dh_gather_rows(const void* src, uint32_t row_bytes, const uint32_t* rows_index,
+                        const uint32_t* rows_count, uint32_t rows, void* dst, void* stream);
+
 /* bf16 rows (cols = 768 or 3072) -> per-token int8 (K3'), the quantiser of
  * dh_ln_smooth_quant on fp32(in) / smooth (inv_smooth as there).  smooth may
  * be NULL when the producer already applied the SmoothQuant scale (see
