@@ -139,3 +139,38 @@ def test_gelu_row_amax_and_single_pass_quantiser(cuda, m):
     torch.cuda.synchronize()
     assert torch.equal(q1, q2) and torch.equal(s1, s2)
     assert int(amax.abs().sum()) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("row_bytes", [16, 1536, 3072, 12288])
+def test_gather_rows_copies_the_listed_rows(cuda, row_bytes):
+    """dh_gather_rows / dh_gather_rows_i8: dst row i = src row rows_index[i]
+    for i < min(rows, *rows_count), nothing past the count."""
+    torch = cuda
+    from diffusionhard_b200 import _lib
+
+    rows = 300
+    g = torch.Generator().manual_seed(row_bytes)
+    src = torch.randint(0, 256, (rows, row_bytes), generator=g, dtype=torch.uint8).cuda()
+    index = torch.randperm(rows, generator=g)[:200].to(torch.int32).cuda()
+    count = torch.tensor([173], dtype=torch.int32, device="cuda")
+    dst = torch.full((rows, row_bytes), 7, dtype=torch.uint8, device="cuda")
+    _lib.call("dh_gather_rows", _lib.ptr(src), row_bytes, _lib.ptr(index), _lib.ptr(count), 200, _lib.ptr(dst), None)
+    torch.cuda.synchronize()
+    assert torch.equal(dst[:173], src[index[:173].long()])
+    assert bool((dst[173:] == 7).all())
+    if row_bytes == 16:
+        assert _lib.raw("dh_gather_rows", _lib.ptr(src), 8, _lib.ptr(index), _lib.ptr(count), 200, _lib.ptr(dst),
+                        None) == 105
+        assert _lib.raw("dh_gather_rows", None, 16, _lib.ptr(index), _lib.ptr(count), 200, _lib.ptr(dst), None) == 100
+    # the int8 head-input form carries each row's scale along
+    if row_bytes == 1536:
+        q = torch.randint(-127, 128, (rows, 768), generator=g, dtype=torch.int8).cuda()
+        sc = torch.rand(rows, generator=g).cuda()
+        dq = torch.zeros((rows, 768), dtype=torch.int8, device="cuda")
+        ds = torch.zeros(rows, device="cuda")
+        _lib.call("dh_gather_rows_i8", _lib.ptr(q), _lib.ptr(sc), _lib.ptr(index), _lib.ptr(count), 200, _lib.ptr(dq),
+                  _lib.ptr(ds), None)
+        torch.cuda.synchronize()
+        sel = index[:173].long()
+        assert torch.equal(dq[:173], q[sel]) and torch.equal(ds[:173], sc[sel])
