@@ -180,7 +180,7 @@ def measure_int8_peak() -> dict:
             "how": "torch._int_mm (cuBLASLt) int8 x int8 -> int32, 8192^3, best of 10 launches, CUDA events"}
 
 
-# Algorithmic work of one forward, per row (SURVEY-style units of the MDLM
+# Algorithmic work of one forward, per row (the units of the MDLM
 # specification, model_spec.py:29-84): backbone int8 ops, attention FLOP per
 # key, and the bytes the memory-bound row kernels must move.
 # The forward runs every block over every row up to the last block's
