@@ -357,6 +357,10 @@ struct EpiResidualT : EpiBase {
 using EpiResidual = EpiResidualT<3, 96, true, 2>;  // K = 768
 using EpiResidualDeep = EpiResidualT<4, 96>;  // K = 3072: deeper TMA pipeline
 using EpiResidual256 = EpiResidualT<3, 128>;  // other N, multiples of 256
+// 128 x 64 tiles for a forward of few rows, where 128 x 192 tiles would
+// leave most SMs idle (1,024 rows: 32 tiles; 128 x 64: 96)
+using EpiResidualNarrow = EpiResidualT<3, 32, true, 1>;  // K = 768
+using EpiResidualNarrowDeep = EpiResidualT<4, 32>;       // K = 3072
 
 DH_DEVINL float gelu_tanh(float x) {
     // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))   (nn.GELU(approx="tanh"))
@@ -706,7 +710,15 @@ extern "C" uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, cons
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w_scale) |
          reinterpret_cast<uintptr_t>(bias)) & 15u)
         return DH_ERR_ALIGNMENT;
-    const uint32_t bn = n % 192 == 0 ? 192u : 256u;
+    uint32_t bn = n % 192 == 0 ? 192u : 256u;
+    // when even the 128 x 64 tiles fit one wave of the SMs, they spread the
+    // rows over three (or four) times as many SMs (one 1,024-row sequence:
+    // 96 tiles instead of 32, 853 -> 737 us per forward); with more rows the
+    // wide tiles' shorter epilogue per byte wins (4 sequences: 1,282 against
+    // 1,375 us with narrow tiles)
+    int sms = kNumSMs, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (((m + 127) / 128) * (n / 64) <= static_cast<uint32_t>(sms)) bn = 64;
     CUtensorMap ta, tb;
     uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, bn);
     if (st != DH_OK) return st;
@@ -714,7 +726,12 @@ extern "C" uint32_t dh_gemm_residual(const int8_t* a, const float* a_scale, cons
     const uint32_t tiles = ((m + 127) / 128) * (n / bn);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e;
-    if (bn == 256) {
+    if (bn == 64) {
+        if (k > 1024)
+            e = launch_gemm_i8<64, EpiResidualNarrowDeep>(ta, tb, shape, {a_scale, w_scale, bias, x, n}, tiles, s);
+        else
+            e = launch_gemm_i8<64, EpiResidualNarrow>(ta, tb, shape, {a_scale, w_scale, bias, x, n}, tiles, s);
+    } else if (bn == 256) {
         e = launch_gemm_i8<256, EpiResidual256>(ta, tb, shape, {a_scale, w_scale, bias, x, n}, tiles, s);
     } else if (k > 1024) {
         e = launch_gemm_i8<192, EpiResidualDeep>(ta, tb, shape, {a_scale, w_scale, bias, x, n}, tiles, s);

@@ -50,3 +50,36 @@ def test_gemm_i8_extreme_values(cuda):
     a[::2] = 127
     got = _gemm(cuda, a, w)
     assert np.array_equal(got, _ref(a, w))
+
+
+@pytest.mark.parametrize("k", [768, 3072])
+def test_residual_narrow_tiles_match_wide_tiles(cuda, k):
+    """dh_gemm_residual takes 128 x 64 tiles when they fit one wave of the
+    SMs (a forward of one sequence), 128 x 192 otherwise: the same rows give
+    the same bits either way (here 1,000 rows alone, and as the live rows of
+    an 8,192-row launch)."""
+    torch = cuda
+    g = torch.Generator().manual_seed(k)
+    m, big = 1000, 8192
+    a = torch.randint(-127, 128, (big, k), generator=g, dtype=torch.int8).cuda()
+    a_scale = (torch.rand(big, generator=g) * 1e-2 + 1e-3).cuda()
+    w = torch.randint(-127, 128, (768, k), generator=g, dtype=torch.int8).cuda()
+    w_scale = (torch.rand(768, generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(768, generator=g) * 0.02).cuda()
+    x0 = torch.randn((big, 768), generator=g).cuda()
+    p = _lib.ptr
+    narrow = x0.clone()
+    _lib.call("dh_gemm_residual", p(a), p(a_scale), p(w), p(w_scale), p(bias), p(narrow), m, 768, k, None, None)
+    wide = x0.clone()
+    live = torch.tensor([m], dtype=torch.int32, device="cuda")
+    _lib.call("dh_gemm_residual", p(a), p(a_scale), p(w), p(w_scale), p(bias), p(wide), big, 768, k, p(live), None)
+    torch.cuda.synchronize()
+    assert torch.equal(narrow[:m], wide[:m])
+    assert torch.equal(narrow[m:], x0[m:]) and torch.equal(wide[m:], x0[m:])
+    # and the values are the dequantised products plus the residual
+    acc = (a[:m].double() @ w.double().T)
+    ref = x0[:m].double() + acc * (a_scale[:m].double()[:, None] * w_scale.double()[None, :]) + bias.double()
+    assert float((narrow[:m].double() - ref).abs().max()) < 1e-3
+    err = np.zeros(1, np.uint32)
+    _lib.call("dh_device_error", err.ctypes.data, 1)
+    assert err[0] == 0
