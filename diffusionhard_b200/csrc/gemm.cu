@@ -95,7 +95,30 @@ DH_DEVINL uint32_t pack_bf16x2(float a, float b) {
 // q / k / v.  A warp's 32 rows are 32 consecutive tokens of one sequence, so
 // its Q / K block is 4 KB contiguous and its V^T block is 64 runs of 64 bytes:
 // both are written through the warp's staging buffer with full-line stores.
-struct EpiQKV : EpiBase {
+struct QKVParams {
+    CUtensorMap q_map;   // Q as [B * 12 * seq_len, 64] bf16, box 32 x 64, 128-byte swizzle
+    CUtensorMap k_map;   // K as [B * 12 * kv_stride, 64] bf16, same box
+    const float* a_scale;
+    const float* w_scale;
+    const float* bias;
+    const float* rope_cos;  // [max_pos, 32]
+    const float* rope_sin;
+    const float* v_scale;   // [768] per-channel factor on V (SmoothQuant 1/s of attn-out), or null
+    uint32_t seq_len;       // rows per sequence in this forward
+    uint32_t pos_offset;    // rotary position of the first row of a sequence
+    uint32_t kv_stride;     // rows per (sequence, head) in the K / V buffers
+    uint32_t kv_offset;     // where this forward's rows go in K / V
+    __nv_bfloat16* q;
+    __nv_bfloat16* k;
+    __half* vt;  // V^T, f16
+};
+
+// kHalf: columns per epilogue warp, half the tile (128 for 128 x 256 tiles;
+// 64 for the 128 x 128 tiles of a forward of one sequence).
+template <uint32_t kHalf_>
+struct EpiQKVT : EpiBase {
+    static constexpr uint32_t kHalf = kHalf_;
+    static_assert(kHalf == 64 || kHalf == 128, "a tile half is one or two heads");
     static constexpr uint32_t kStages = 3;
     static constexpr uint32_t kChunk = 64;
     // per warp: the 4 KB source of its q / k TMA stores, then its 128
@@ -106,23 +129,7 @@ struct EpiQKV : EpiBase {
     // warps that cover that quadrant's rows: [quadrant][cos 4 KB | sin 4 KB],
     // row r's 16-byte piece c at swz128(r, c).
     static constexpr uint32_t kExtraSmem = 4 * 8192;
-    struct Params {
-        CUtensorMap q_map;   // Q as [B * 12 * seq_len, 64] bf16, box 32 x 64, 128-byte swizzle
-        CUtensorMap k_map;   // K as [B * 12 * kv_stride, 64] bf16, same box
-        const float* a_scale;
-        const float* w_scale;
-        const float* bias;
-        const float* rope_cos;  // [max_pos, 32]
-        const float* rope_sin;
-        const float* v_scale;   // [768] per-channel factor on V (SmoothQuant 1/s of attn-out), or null
-        uint32_t seq_len;       // rows per sequence in this forward
-        uint32_t pos_offset;    // rotary position of the first row of a sequence
-        uint32_t kv_stride;     // rows per (sequence, head) in the K / V buffers
-        uint32_t kv_offset;     // where this forward's rows go in K / V
-        __nv_bfloat16* q;
-        __nv_bfloat16* k;
-        __half* vt;  // V^T, f16
-    };
+    using Params = QKVParams;
     struct TileState {
         float ab;  // a_scale of this thread's row
     };
@@ -136,7 +143,7 @@ struct EpiQKV : EpiBase {
         st.ab = ctx.row_ok ? p.a_scale[ctx.row] : 0.f;
         // the warp's 128 columns of w_scale / bias (/ v_scale, indexed from 0 at the v block)
         stage_columns(ctx.stage + 4096, ctx.lane, p.w_scale + col_start, p.bias + col_start,
-                      col_start >= 1536u && p.v_scale ? p.v_scale + (col_start - 1536u) : nullptr);
+                      col_start >= 1536u && p.v_scale ? p.v_scale + (col_start - 1536u) : nullptr, kHalf);
         if (col_start >= 1536u) return true;
         const uint32_t quad = (ctx.row0 / 32u) & 3u;
         const uint32_t half = static_cast<uint32_t>(ctx.stage - ctx.extra - kExtraSmem) / kStagingPerWarp / 4u;
@@ -162,7 +169,7 @@ struct EpiQKV : EpiBase {
         const uint32_t which = col0 / 768u;
         const uint32_t h = (col0 % 768u) / 64u;
         float y[64];
-        const uint32_t cw = (col0 % 128u) * 4u;  // byte offset of this chunk in the warp's parameters
+        const uint32_t cw = (col0 % kHalf) * 4u;  // byte offset of this chunk in the warp's parameters
         const float4* w4 = reinterpret_cast<const float4*>(ctx.stage + 4096 + cw);
         const float4* b4 = reinterpret_cast<const float4*>(ctx.stage + 4096 + 512 + cw);
 #pragma unroll
@@ -248,6 +255,8 @@ struct EpiQKV : EpiBase {
         if (lane == 0) tc::tma_store_wait_all();
     }
 };
+using EpiQKV = EpiQKVT<128>;
+using EpiQKVNarrow = EpiQKVT<64>;
 
 // x[row, col] += acc * (a_scale * w_scale) + bias  (attention out, MLP down).
 // The residual read-modify-write goes through the staging buffer with one
@@ -672,8 +681,13 @@ extern "C" uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, cons
          reinterpret_cast<uintptr_t>(rope_cos) | reinterpret_cast<uintptr_t>(rope_sin) |
          reinterpret_cast<uintptr_t>(v_scale)) & 15u)
         return DH_ERR_ALIGNMENT;
+    // 128 x 128 tiles when they fit one wave of the SMs (a forward of one
+    // sequence: 144 tiles instead of 72), else 128 x 256
+    int sms = kNumSMs, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t bn = ((m + 127) / 128) * (2304 / 128) <= static_cast<uint32_t>(sms) ? 128u : 256u;
     CUtensorMap ta, tb;
-    uint32_t st = make_i8_operand_maps(&ta, &tb, a, 768, w, 768, m, 2304, 768, 256);
+    uint32_t st = make_i8_operand_maps(&ta, &tb, a, 768, w, 768, m, 2304, 768, bn);
     if (st != DH_OK) return st;
     const uint64_t bh = static_cast<uint64_t>(m / seq_len) * 12;
     EpiQKV::Params p{};
@@ -694,10 +708,11 @@ extern "C" uint32_t dh_gemm_qkv_rope(const int8_t* a, const float* a_scale, cons
     p.k = static_cast<__nv_bfloat16*>(k);
     p.vt = static_cast<__half*>(vt);
     GemmShape shape{m, 2304, 768, run_rows};
-    const uint32_t tiles = ((m + 127) / 128) * 9;
-    if (launch_gemm_i8<256, EpiQKV>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=
-        cudaSuccess)
-        return DH_ERR_CUDA;
+    const uint32_t tiles = ((m + 127) / 128) * (2304 / bn);
+    const cudaError_t e = bn == 128
+        ? launch_gemm_i8<128, EpiQKVNarrow>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream))
+        : launch_gemm_i8<256, EpiQKV>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return DH_ERR_CUDA;
     return DH_OK;
 }
 

@@ -83,3 +83,39 @@ def test_residual_narrow_tiles_match_wide_tiles(cuda, k):
     err = np.zeros(1, np.uint32)
     _lib.call("dh_device_error", err.ctypes.data, 1)
     assert err[0] == 0
+
+
+def test_qkv_narrow_tiles_match_wide_tiles(cuda):
+    """dh_gemm_qkv_rope takes 128 x 128 tiles when they fit one wave (one
+    1,024-token sequence), 128 x 256 otherwise: q, k and V^T of the same
+    rows are the same bits either way (one sequence alone, and as the live
+    rows of an eight-sequence launch)."""
+    torch = cuda
+    from diffusionhard_b200.model import MDLMConfig, build_quantized
+    from diffusionhard_b200.engine import MDLMEngine
+
+    qm = build_quantized(MDLMConfig(vocab_size=1000, mask_token_id=999, blocks=1), seed=0)
+    L = 1024
+    g = torch.Generator().manual_seed(3)
+    a_all = torch.randint(-127, 128, (8 * L, 768), generator=g, dtype=torch.int8)
+    s_all = torch.rand(8 * L, generator=g) * 1e-2 + 1e-3
+    outs = []
+    for B in (1, 8):
+        eng = MDLMEngine(qm, B, L)
+        # the GEMM reads the activations as [rows, 768], row after row
+        eng.act_q.view(-1)[: B * L * 768].view(B * L, 768).copy_(a_all[: B * L])
+        eng.act_scale.copy_(s_all[: B * L])
+        qkv, out = eng.blocks[0]["qkv"], eng.blocks[0]["out"]
+        k, vt = eng.kv_buffers[0]
+        live = torch.tensor([L], dtype=torch.int32, device="cuda")
+        p = _lib.ptr
+        _lib.call("dh_gemm_qkv_rope", p(eng.act_q), p(eng.act_scale), p(qkv.w), p(qkv.w_scale), p(qkv.bias),
+                  p(eng.rope_cos), p(eng.rope_sin), p(out.inv_smooth), B * L, L, 0, eng.kv_stride, 0, p(eng.q), p(k),
+                  p(vt), p(live) if B > 1 else None, None)
+        torch.cuda.synchronize()
+        outs.append((eng.q[0].clone(), k[0].clone(), vt[0].clone()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    err = np.zeros(1, np.uint32)
+    _lib.call("dh_device_error", err.ctypes.data, 1)
+    assert err[0] == 0
