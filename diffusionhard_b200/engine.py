@@ -433,7 +433,17 @@ class MDLMEngine:
                   _lib.stream_handle())
 
     def launches_per_generation(self, steps: int) -> int:
-        per_transition = 1 + self.launches_per_forward + 1 + 1 + 2 + 1
+        """Kernels one generation launches (the loop set-up, then per
+        transition: plan, the forward, select, the head's input rows, the head
+        (zeroing + fused GEMM) and commit).  The composite loop over an
+        unpacked batch stops the forward after the last block's attention (six
+        launches fewer) and finishes that block for the revealed rows: two row
+        gathers, the block's six remaining kernels and the final LayerNorm.
+        Packed, the head input is also scattered per sequence."""
+        compact = self.compact_for(steps)
+        per_transition = 1 + self.launches_per_forward + 1 + 1 + 2 + 1 + (1 if compact else 0)
+        if self.native_loop_ok() and not compact:
+            per_transition += -6 + (2 + 6 + 1) - 1
         return 1 + (steps + 1) * per_transition
 
     @_on_device

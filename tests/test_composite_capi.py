@@ -166,3 +166,37 @@ def test_packed_forward_computes_only_the_refilling_sequences(cuda):
     assert 0 < r1 <= r0 // 2
     assert m0 == m1
     assert not (t1 == SMALL.mask_token_id).any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,steps", [(2, 256, 8), (4, 64, 64)])
+def test_launch_count_is_the_captured_kernel_count(cuda, B, L, steps):
+    """engine.launches_per_generation (the bench's gpu_launches claim) equals
+    the kernel nodes of the CUDA graph that captures one whole generation
+    through dh_sample_loop, unpacked (the last block finished for the revealed
+    rows only) and packed."""
+    torch = cuda
+    from cuda.bindings import runtime as rt
+
+    from diffusionhard_b200.engine import MDLMEngine
+
+    qm = build_quantized(SMALL, seed=0)
+    eng = MDLMEngine(qm, B, L)
+    ids = torch.full((B, L), SMALL.mask_token_id, dtype=torch.int64, device="cuda")
+    eng.generate(ids, steps=steps, seed=1)  # sets the loop buffers up, eagerly
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph(keep_graph=True)
+    with torch.cuda.graph(g):
+        eng._enqueue_native(steps, 1, reveal_thresholds_q32(steps))
+    graph = rt.cudaGraph_t(init_value=g.raw_cuda_graph())
+    err, _, count = rt.cudaGraphGetNodes(graph, 0)
+    assert err == rt.cudaError_t.cudaSuccess
+    err, nodes, count = rt.cudaGraphGetNodes(graph, count)
+    assert err == rt.cudaError_t.cudaSuccess
+    kernels = 0
+    for node in nodes[:count]:
+        err, kind = rt.cudaGraphNodeGetType(node)
+        assert err == rt.cudaError_t.cudaSuccess
+        kernels += kind == rt.cudaGraphNodeType.cudaGraphNodeTypeKernel
+    assert kernels == eng.launches_per_generation(steps)
+    del g
