@@ -766,8 +766,14 @@ extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const in
     if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(w_scale) |
          reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(out_scale)) & 15u)
         return DH_ERR_ALIGNMENT;
+    // when 128 x 128 tiles give every CTA at most one tile per epilogue
+    // group (one 1,024-row sequence: 192 tiles on 148 SMs), the two groups
+    // drain them side by side where 128 x 256 tiles leave one group idle
+    int sms = kNumSMs, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint32_t bn = ((m + 127) / 128) * (n / 128) <= 2u * static_cast<uint32_t>(sms) ? 128u : 256u;
     CUtensorMap ta, tb;
-    uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, 256);
+    uint32_t st = make_i8_operand_maps(&ta, &tb, a, k, w, k, m, n, k, bn);
     if (st != DH_OK) return st;
     EpiGelu::Params p{};
     if (!make_tmap_2d_sw64(&p.out_map, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m, n,
@@ -781,10 +787,11 @@ extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const in
     p.n = n;
     p.row_amax = row_amax;
     GemmShape shape{m, n, k, run_rows};
-    const uint32_t tiles = ((m + 127) / 128) * (n / 256);
-    if (launch_gemm_i8<256, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream)) !=
-        cudaSuccess)
-        return DH_ERR_CUDA;
+    const uint32_t tiles = ((m + 127) / 128) * (n / bn);
+    const cudaError_t e = bn == 128
+        ? launch_gemm_i8<128, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream))
+        : launch_gemm_i8<256, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return DH_ERR_CUDA;
     return DH_OK;
 }
 

@@ -85,6 +85,43 @@ def test_residual_narrow_tiles_match_wide_tiles(cuda, k):
     assert err[0] == 0
 
 
+@pytest.mark.parametrize("m", [1000, 64])
+def test_gelu_narrow_tiles_match_wide_tiles(cuda, m):
+    """dh_gemm_gelu takes 128 x 128 tiles when every CTA then holds at most
+    one tile per epilogue group (one 1,024-token sequence, or a 64-token
+    canvas), 128 x 256 otherwise: the same rows give the same bf16 outputs
+    and row maxima either way (the rows alone, and as the live rows of an
+    8,192-row launch)."""
+    torch = cuda
+    g = torch.Generator().manual_seed(m)
+    big, n, k = 8192, 3072, 768
+    a = torch.randint(-127, 128, (big, k), generator=g, dtype=torch.int8).cuda()
+    a_scale = (torch.rand(big, generator=g) * 1e-3 + 1e-4).cuda()
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8).cuda()
+    w_scale = (torch.rand(n, generator=g) * 1e-3 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.1).cuda()
+    out_scale = (torch.rand(n, generator=g) + 0.5).cuda()
+    p = _lib.ptr
+    outs = []
+    for rows, live in ((m, None), (big, torch.tensor([m], dtype=torch.int32, device="cuda"))):
+        out = torch.full((big, n), 3.0, dtype=torch.bfloat16, device="cuda")
+        amax = torch.zeros(big, dtype=torch.int32, device="cuda")
+        _lib.call("dh_gemm_gelu", p(a), p(a_scale), p(w), p(w_scale), p(bias), p(out_scale), p(out), p(amax), rows,
+                  n, k, p(live), None)
+        torch.cuda.synchronize()
+        assert bool((out[m:] == 3.0).all()) and int(amax[m:].abs().sum()) == 0
+        outs.append((out[:m].clone(), amax[:m].clone()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert torch.equal(outs[0][1].view(torch.float32), outs[0][0].float().abs().amax(dim=1))
+    # and the values are bias + dequantised products through GELU(tanh), times out_scale
+    x = (a[:m].double() @ w.double().T) * (a_scale[:m].double()[:, None] * w_scale.double()[None, :]) + bias.double()
+    ref = 0.5 * x * (1 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3))) * out_scale.double()
+    assert float(((outs[0][0].double() - ref).norm() / ref.norm())) < 1e-2
+    err = np.zeros(1, np.uint32)
+    _lib.call("dh_device_error", err.ctypes.data, 1)
+    assert err[0] == 0
+
+
 def test_qkv_narrow_tiles_match_wide_tiles(cuda):
     """dh_gemm_qkv_rope takes 128 x 128 tiles when they fit one wave (one
     1,024-token sequence), 128 x 256 otherwise: q, k and V^T of the same
