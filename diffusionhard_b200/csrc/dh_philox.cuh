@@ -73,13 +73,15 @@ DH_DEVINL uint32_t philox_lane(const Philox4& r, uint32_t i) {
     return i == 0 ? r.x : i == 1 ? r.y : i == 2 ? r.z : r.w;
 }
 
-// Copies the merged Gumbel table into shared memory (call from all threads,
-// followed by __syncthreads()).
-DH_DEVINL void load_gumbel_table(int16_t* smem_table) {
+// Copies the merged Gumbel table into shared memory, word i by thread
+// i % count of the `count` threads that call it (the one-argument form: all
+// threads of the block); those threads synchronise before reading it.
+DH_DEVINL void load_gumbel_table(int16_t* smem_table, uint32_t tid, uint32_t count) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(DH_GUMBEL_MERGED_Q10_DEV);
     uint32_t* dst = reinterpret_cast<uint32_t*>(smem_table);
-    for (uint32_t i = threadIdx.x; i < 32u * 256u / 2u; i += blockDim.x) dst[i] = src[i];
+    for (uint32_t i = tid; i < 32u * 256u / 2u; i += count) dst[i] = src[i];
 }
+DH_DEVINL void load_gumbel_table(int16_t* smem_table) { load_gumbel_table(smem_table, threadIdx.x, blockDim.x); }
 
 // Score of one word using the shared-memory merged table.
 DH_DEVINL int32_t gumbel_q10(uint32_t word, const int16_t* smem_table) {

@@ -415,9 +415,9 @@ struct EpiGelu : EpiBase {
         float ab;
         __nv_bfloat162 amax2;  // running max |out| of this thread's row over the tile's chunks
     };
-    static DH_DEVINL void init_smem(const Params& p, uint8_t* extra) {
+    static DH_DEVINL void init_smem(const Params& p, uint8_t* extra, uint32_t tid, uint32_t count) {
         const uint32_t pieces = p.n / 4;  // 16-byte pieces per vector
-        for (uint32_t i = threadIdx.x; i < 3 * pieces; i += blockDim.x) {
+        for (uint32_t i = tid; i < 3 * pieces; i += count) {
             const uint32_t v = i / pieces, j = i % pieces;
             const float* src = v == 0 ? p.w_scale : (v == 1 ? p.bias : p.out_scale);
             if (src) cp_async16(extra + v * (kMaxCols * 4) + j * 16, src + j * 4);

@@ -25,7 +25,9 @@
 namespace dh {
 
 // Default hooks for epilogue policies: extra shared memory (bytes, placed
-// after the pipeline stages) initialised once per CTA by all threads.
+// after the pipeline stages) initialised once per CTA by the epilogue threads
+// (thread `tid` of `count`), while the TMA and MMA warps already start the
+// first tile's pipeline.
 struct EpiBase {
     static constexpr uint32_t kStages = 4;          // TMA pipeline depth
     // epilogue warp groups of 8: with 2, group g takes the tiles accumulated
@@ -35,7 +37,7 @@ struct EpiBase {
     static constexpr uint32_t kExtraSmem = 0;      // shared by the CTA
     static constexpr uint32_t kStagingPerWarp = 0;  // private to each epilogue warp
     template <class P>
-    static DH_DEVINL void init_smem(const P&, uint8_t*) {}
+    static DH_DEVINL void init_smem(const P&, uint8_t*, uint32_t /*tid*/, uint32_t /*count*/) {}
     // after the warp's last tile (e.g. drain asynchronous stores that read
     // shared memory before the CTA exits)
     static DH_DEVINL void finish(uint32_t /*lane*/) {}
@@ -137,7 +139,6 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
         tc::prefetch_tmap(&tmap_b);
     }
     if (warp == 1) tc::tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
-    Epi::init_smem(ep, extra_smem);
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -227,6 +228,11 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
     } else {
         // --------------------------------------------------------- epilogue
         const uint32_t ew = warp - 2;  // epilogue warp index
+        // the policy's per-CTA tables, filled by the epilogue warps alone
+        // (named barrier 1 counts exactly them; no wait precedes it, so every
+        // epilogue thread arrives) while the first tile's loads and MMAs run
+        Epi::init_smem(ep, extra_smem, threadIdx.x - 64u, Cfg::EPI_THREADS);
+        asm volatile("bar.sync 1, %0;" ::"r"(Cfg::EPI_THREADS) : "memory");
         const uint32_t group = ew / 8u;
         const uint32_t quad = warp & 3u;
         const uint32_t half = (ew >> 2) & 1u;

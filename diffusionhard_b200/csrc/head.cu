@@ -176,8 +176,8 @@ struct EpiHead : EpiBase {
         const int16_t* table;
         const uint8_t* stage;
     };
-    static DH_DEVINL void init_smem(const Params&, uint8_t* extra) {
-        load_gumbel_table(reinterpret_cast<int16_t*>(extra));
+    static DH_DEVINL void init_smem(const Params&, uint8_t* extra, uint32_t tid, uint32_t count) {
+        load_gumbel_table(reinterpret_cast<int16_t*>(extra), tid, count);
     }
     static DH_DEVINL bool tile_begin(const Params& p, TileState& st, const EpiCtx& ctx, uint32_t col_start) {
         const uint32_t row = ctx.row;
