@@ -119,7 +119,8 @@ template <uint32_t kHalf_>
 struct EpiQKVT : EpiBase {
     static constexpr uint32_t kHalf = kHalf_;
     static_assert(kHalf == 64 || kHalf == 128, "a tile half is one or two heads");
-    static constexpr uint32_t kStages = 3;
+    // four stages fit beside the staging buffers with 128 x 128 tiles
+    static constexpr uint32_t kStages = kHalf == 64 ? 4 : 3;
     static constexpr uint32_t kChunk = 64;
     // per warp: the 4 KB source of its q / k TMA stores, then its 128
     // columns' w_scale, bias and v_scale (512 B each); 1 KB multiples keep
@@ -368,8 +369,11 @@ using EpiResidualDeep = EpiResidualT<4, 96>;  // K = 3072: deeper TMA pipeline
 using EpiResidual256 = EpiResidualT<3, 128>;  // other N, multiples of 256
 // 128 x 64 tiles for a forward of few rows, where 128 x 192 tiles would
 // leave most SMs idle (1,024 rows: 32 tiles; 128 x 64: 96)
-using EpiResidualNarrow = EpiResidualT<3, 32, true, 1>;  // K = 768
-using EpiResidualNarrowDeep = EpiResidualT<4, 32>;       // K = 3072
+// The 128 x 64 tiles run where each CTA holds about one tile, so the first
+// tile's loads are all the pipeline sees: it keeps 6 (K = 768: the whole of
+// K) or 7 stages of 24 KB in flight.
+using EpiResidualNarrow = EpiResidualT<6, 32, true, 1>;  // K = 768
+using EpiResidualNarrowDeep = EpiResidualT<7, 32>;       // K = 3072
 
 DH_DEVINL float gelu_tanh(float x) {
     // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))   (nn.GELU(approx="tanh"))
@@ -527,6 +531,11 @@ struct EpiGelu : EpiBase {
     static DH_DEVINL void finish(uint32_t lane) {
         if (lane == 0) tc::tma_store_wait_all();
     }
+};
+
+// 128 x 128 MLP-up tiles (one per epilogue group and CTA): a fourth stage fits.
+struct EpiGeluNarrow : EpiGelu {
+    static constexpr uint32_t kStages = 4;
 };
 
 // Integer requantisation of the int32 accumulators, the RTL form of
@@ -789,7 +798,7 @@ extern "C" uint32_t dh_gemm_gelu(const int8_t* a, const float* a_scale, const in
     GemmShape shape{m, n, k, run_rows};
     const uint32_t tiles = ((m + 127) / 128) * (n / bn);
     const cudaError_t e = bn == 128
-        ? launch_gemm_i8<128, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream))
+        ? launch_gemm_i8<128, EpiGeluNarrow>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream))
         : launch_gemm_i8<256, EpiGelu>(ta, tb, shape, p, tiles, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return DH_ERR_CUDA;
     return DH_OK;
