@@ -36,6 +36,12 @@ struct EpiBase {
     static constexpr uint32_t kGroups = 1;
     static constexpr uint32_t kExtraSmem = 0;      // shared by the CTA
     static constexpr uint32_t kStagingPerWarp = 0;  // private to each epilogue warp
+    // Few-row mode: when a launch has at most 32 valid rows, its A rows are
+    // loaded into all four 32-row quarters of the tile, so every TMEM lane
+    // quadrant holds them; the four warps of a column half then split its
+    // columns four ways instead of one quadrant's warps doing all the work
+    // (needs (BN / 8) % kChunk == 0).
+    static constexpr bool kReplicateRows = false;
     template <class P>
     static DH_DEVINL void init_smem(const P&, uint8_t*, uint32_t /*tid*/, uint32_t /*count*/) {}
     // after the warp's last tile (e.g. drain asynchronous stores that read
@@ -104,7 +110,9 @@ struct GemmCfg {
 template <uint32_t BN, class Epi>
 __global__ void __launch_bounds__(GemmCfg<BN, Epi::kStages, Epi::kGroups>::THREADS, 1)
 gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                  const __grid_constant__ CUtensorMap tmap_b, GemmShape shape,
+                  const __grid_constant__ CUtensorMap tmap_b,
+                  const __grid_constant__ CUtensorMap tmap_a32,  // A, 32-row box (few-row mode)
+                  GemmShape shape,
                   const __grid_constant__ typename Epi::Params ep) {
     using Cfg = GemmCfg<BN, Epi::kStages, Epi::kGroups>;
     extern __shared__ uint8_t smem_raw[];
@@ -137,6 +145,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
         tc::fence_barrier_init();
         tc::prefetch_tmap(&tmap_a);
         tc::prefetch_tmap(&tmap_b);
+        if (Epi::kReplicateRows) tc::prefetch_tmap(&tmap_a32);
     }
     if (warp == 1) tc::tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
     tc::tc_fence_before();
@@ -150,6 +159,8 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const uint32_t n_tiles = (shape.N + BN - 1) / BN;
     const uint32_t k_blocks = (shape.K + Cfg::BK - 1) / Cfg::BK;
     const uint32_t total = m_tiles * n_tiles;
+    // few-row mode (one row tile): the 32-row A box lands in every quarter
+    const bool replicate = Epi::kReplicateRows && m_eff <= 32;
 
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
@@ -167,8 +178,16 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         break;
                     }
                     tc::mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
-                    tc::tma_load_2d(a_smem + stage * Cfg::A_BYTES, &tmap_a, &full_bar[stage],
-                                    static_cast<int32_t>(kb * Cfg::BK), static_cast<int32_t>(m0));
+                    if (replicate) {
+#pragma unroll
+                        for (uint32_t q = 0; q < 4; ++q)  // 4 KB quarters, 1 KB-aligned for the swizzle
+                            tc::tma_load_2d(a_smem + stage * Cfg::A_BYTES + q * (Cfg::A_BYTES / 4), &tmap_a32,
+                                            &full_bar[stage], static_cast<int32_t>(kb * Cfg::BK),
+                                            static_cast<int32_t>(m0));
+                    } else {
+                        tc::tma_load_2d(a_smem + stage * Cfg::A_BYTES, &tmap_a, &full_bar[stage],
+                                        static_cast<int32_t>(kb * Cfg::BK), static_cast<int32_t>(m0));
+                    }
                     tc::tma_load_2d(b_smem + stage * Cfg::B_BYTES, &tmap_b, &full_bar[stage],
                                     static_cast<int32_t>(kb * Cfg::BK), static_cast<int32_t>(n0));
                     issued_parity[stage] = phase;
@@ -236,10 +255,16 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const uint32_t group = ew / 8u;
         const uint32_t quad = warp & 3u;
         const uint32_t half = (ew >> 2) & 1u;
-        const uint32_t row_in_tile = quad * 32 + lane;
+        // few-row mode: every quadrant holds rows 0-31, and the quadrant's
+        // warps take a quarter of their half's columns each
+        const uint32_t quad_row = replicate ? 0u : quad * 32;
+        const uint32_t row_in_tile = quad_row + lane;
         constexpr uint32_t kHalf = BN / 2;
         constexpr uint32_t kChunk = Epi::kChunk;
         static_assert(kHalf % kChunk == 0, "chunk must divide the half tile");
+        static_assert(!Epi::kReplicateRows || (kHalf / 4) % kChunk == 0, "few-row mode: a chunk per quarter");
+        const uint32_t c_begin = replicate ? quad * (kHalf / 4) : 0u;
+        const uint32_t c_end = replicate ? c_begin + kHalf / 4 : kHalf;
         // tile k of this CTA is accumulated in TMEM buffer k % 2
         uint32_t acc = group, acc_phase = 0;
         for (uint32_t tile = blockIdx.x + group * gridDim.x; tile < total; tile += Cfg::GROUPS * gridDim.x) {
@@ -248,10 +273,10 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t row = m0 + row_in_tile;
             const bool row_ok = row < m_eff;
             const uint32_t next = tile + Cfg::GROUPS * gridDim.x;
-            const EpiCtx ctx{row, row_ok, m0 + quad * 32, m_eff, lane,
+            const EpiCtx ctx{row, row_ok, m0 + quad_row, m_eff, lane,
                              extra_smem + Epi::kExtraSmem + ew * Epi::kStagingPerWarp,
                              extra_smem, tile == blockIdx.x + group * gridDim.x, next < total,
-                             (next / n_tiles) * Cfg::BM + quad * 32, (next % n_tiles) * BN + half * kHalf,
+                             (next / n_tiles) * Cfg::BM + quad_row, (next % n_tiles) * BN + half * kHalf,
                              &pair_bars[group * 4 + quad]};
             typename Epi::TileState st;
             // tile_begin runs before the accumulator is ready: a policy may
@@ -261,7 +286,7 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
             if (!tc::mbar_wait(&accf_bar[acc], acc_phase, tc::kErrTimeoutAccFull)) break;
             tc::tc_fence_after();
 #pragma unroll 1
-            for (uint32_t c = 0; c < kHalf; c += kChunk) {
+            for (uint32_t c = c_begin; c < c_end; c += kChunk) {
                 const uint32_t col_in_tile = half * kHalf + c;
                 const uint32_t taddr =
                     tmem_base + ((quad * 32u) << 16) + acc * BN + col_in_tile;
@@ -297,7 +322,8 @@ gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
 template <uint32_t BN, class Epi>
 inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
                                   const GemmShape& shape, const typename Epi::Params& ep,
-                                  uint32_t tiles_hint, cudaStream_t stream) {
+                                  uint32_t tiles_hint, cudaStream_t stream,
+                                  const CUtensorMap* ta32 = nullptr) {
     using Cfg = GemmCfg<BN, Epi::kStages, Epi::kGroups>;
     auto kernel = gemm_i8_tc_kernel<BN, Epi>;
     static std::atomic<uint64_t> configured{0};
@@ -311,7 +337,8 @@ inline cudaError_t launch_gemm_i8(const CUtensorMap& ta, const CUtensorMap& tb,
             sms = v;
     }
     const uint32_t grid = tiles_hint == 0 ? 1u : (tiles_hint < static_cast<uint32_t>(sms) ? tiles_hint : sms);
-    kernel<<<grid, Cfg::THREADS, Cfg::template smem_bytes<Epi>(), stream>>>(ta, tb, shape, ep);
+    if (Epi::kReplicateRows && !ta32) return cudaErrorInvalidValue;
+    kernel<<<grid, Cfg::THREADS, Cfg::template smem_bytes<Epi>(), stream>>>(ta, tb, ta32 ? *ta32 : ta, shape, ep);
     return cudaGetLastError();
 }
 

@@ -167,6 +167,9 @@ struct EpiHead : EpiBase {
     // converted once per tile instead of once per logit
     static constexpr uint32_t kStagingPerWarp = 1536;
     static constexpr uint32_t kExtraSmem = 32 * 256 * 2;  // merged Gumbel table
+    // few rows (the revealed rows of one sequence): all four lane quadrants
+    // race a quarter of the columns each
+    static constexpr bool kReplicateRows = true;
     using Params = HeadParams;
     struct TileState {
         unsigned long long best;
@@ -373,12 +376,16 @@ uint32_t launch_head(const int8_t* hidden, uint64_t ld_hidden, const int8_t* wei
     uint32_t s = make_i8_operand_maps(&ta, &tb, hidden, ld_hidden, weights, ld_weights, rows,
                                       hp.vocab, hidden_size, 256);
     if (s != DH_OK) return s;
+    // the same rows with a 32-row box, for launches with at most 32 valid rows
+    CUtensorMap ta32;
+    if (!make_tmap_2d(&ta32, hidden, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, hidden_size, ld_hidden, 32, 128))
+        return DH_ERR_CUDA;
     const uint32_t zb = std::min<uint32_t>((rows + 255) / 256, 1024u);
     zero_u64_kernel<<<zb, 256, 0, st>>>(hp.packed, rows, rows_count);
     DH_LAUNCH_CHECK();
     GemmShape shape{rows, hp.vocab, hidden_size, rows_count};
     const uint32_t tiles = ((rows + 127) / 128) * ((hp.vocab + 255) / 256);
-    if (launch_gemm_i8<256, EpiHead>(ta, tb, shape, hp, tiles, st) != cudaSuccess) return DH_ERR_CUDA;
+    if (launch_gemm_i8<256, EpiHead>(ta, tb, shape, hp, tiles, st, &ta32) != cudaSuccess) return DH_ERR_CUDA;
     return DH_OK;
 }
 

@@ -86,8 +86,12 @@ def _head(torch, hq, hs, qm, mode, pos=None, key=None, ev=None, key_lo=0):
     return ids.cpu().numpy(), sc.cpu().numpy()
 
 
-@pytest.mark.parametrize("vocab,rows", [(1000, 300), (50258, 129)])
+@pytest.mark.parametrize("vocab,rows", [(1000, 300), (50258, 129), (50258, 16), (50258, 32), (1000, 1),
+                                       (1000, 33)])
 def test_head_bit_exact(cuda, vocab, rows):
+    """Up to 32 rows the head runs in its few-row mode (the rows loaded into
+    all four lane quadrants, the columns split four ways); 33 and more rows
+    take the one-row-per-thread path."""
     torch = cuda
     cfg = MDLMConfig(vocab_size=vocab, mask_token_id=vocab - 1, blocks=1)
     rng = np.random.default_rng(vocab)
@@ -112,6 +116,39 @@ def test_head_bit_exact(cuda, vocab, rows):
                                      row_key_hi=key, row_eval=ev, key_lo=7)
         assert np.array_equal(ids, oids), mode
         assert np.array_equal(sc, osc), mode
+    assert _device_error() == 0
+
+
+def test_head_few_rows_by_device_count(cuda):
+    """The few-row mode is chosen on the device: a launch over 300 host rows
+    whose device row count is 20 gives the oracle's ids for those 20 rows and
+    leaves the rest untouched."""
+    torch = cuda
+    vocab, rows, live = 50258, 300, 20
+    rng = np.random.default_rng(5)
+    w = np.clip(np.round(rng.normal(0, 40, (vocab, 768))), -127, 127).astype(np.int8)
+    ws = rng.uniform(0.5e-3, 2e-3, vocab).astype(np.float32)
+    bias = rng.normal(0, 0.02, vocab).astype(np.float32)
+    h = rng.integers(-127, 128, (rows, 768)).astype(np.int8)
+    a = rng.uniform(0.01, 0.05, rows).astype(np.float32)
+    pos, key, ev = (rng.integers(0, 1024, rows).astype(np.int32), rng.integers(0, 64, rows).astype(np.int32),
+                    rng.integers(0, 64, rows).astype(np.int32))
+    dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
+    hq, hs, wq, wsd, bd, pd, kd, ed = map(dev, (h, a, w, ws, bias, pos, key, ev))
+    count = torch.tensor([live], dtype=torch.int32, device="cuda")
+    packed = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    ids = torch.full((rows,), -5, dtype=torch.int32, device="cuda")
+    sc = torch.zeros(rows, dtype=torch.int32, device="cuda")
+    p = _lib.ptr
+    _lib.call("dh_head_argmax_i8", p(hq), 768, p(wq), 768, rows, p(count), 768, vocab, 0, vocab - 1, 1, p(hs),
+              p(wsd), p(bd), None, None, None, p(pd), p(kd), p(ed), 0, 7, 0, p(packed), p(ids), p(sc), None)
+    torch.cuda.synchronize()
+    oids, osc = pyoracle.head_i8(1, h[:live], w, vocab - 1, a_scale=a[:live], w_scale=ws, bias=bias,
+                                 row_position=pos[:live], row_key_hi=key[:live], row_eval=ev[:live], key_lo=7)
+    got = ids.cpu().numpy()
+    assert np.array_equal(got[:live], oids)
+    assert np.array_equal(sc.cpu().numpy()[:live], osc)
+    assert (got[live:] == -5).all()
     assert _device_error() == 0
 
 
