@@ -365,13 +365,15 @@ def test_prefix_cached_suffix_matches_oracle(cuda, small_model):
     assert _device_error() == 0
 
 
-def test_vocab_sharded_head_equals_unsharded(cuda):
+@pytest.mark.parametrize("rows", [257, 16])
+def test_vocab_sharded_head_equals_unsharded(cuda, rows):
     """Head rows split into 4 slices (global ids via vocab_offset); the MAX of
-    the packed words equals the unsharded head, ids and scores, both modes."""
+    the packed words equals the unsharded head, ids and scores, both modes
+    (16 rows: the few-row mode on every slice)."""
     torch = cuda
     from diffusionhard_b200.distributed import decode_packed, to_signed_, vocab_shards
 
-    V, rows, mask = 50258, 257, 50257
+    V, mask = 50258, 50257
     rng = np.random.default_rng(42)
     W = torch.from_numpy(np.clip(np.round(rng.normal(0, 40, (V, 768))), -127, 127).astype(np.int8)).cuda()
     ws = torch.from_numpy(rng.uniform(0.5e-3, 2e-3, V).astype(np.float32)).cuda()
